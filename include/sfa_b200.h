@@ -1,0 +1,171 @@
+/*
+ * sfa_b200.h — C ABI of the B200 (sm_100a) sparse flash attention library.
+ *
+ * The library computes block-sparse / top-k indexed attention forward and
+ * backward with the semantics of the reference op
+ * `SparseFlashAttentionTriton` (lilac-me/ops, SFA.py:69-306), generalised to
+ * grouped-query heads, separate k and v, block_size > 1, causal masking and
+ * varlen batches.  Every entry point:
+ *   - takes plain device pointers, element strides and sizes (no framework types);
+ *   - enqueues work on the given CUDA stream (a `cudaStream_t` passed as void*);
+ *   - allocates no memory (scratch comes from the caller's workspace);
+ *   - never synchronises the host with the device;
+ *   - returns SFA_OK (0) or a negative SFA_ERR_* code; sfa_last_error_string()
+ *     describes the last failure on the calling thread.
+ *
+ * Layouts.  Dense: q [B, Tq, Hq, Dqk], k [B, Tk, Hk, Dqk], v [B, Tk, Hk, Dv],
+ * block_indices [B, Tq, Hk, S] (int32), o/dout [B, Tq, Hq, Dv], lse [B, Tq, Hq].
+ * Varlen (cu_seqlens_q != NULL): the batch axis is dropped, rows of sequence i
+ * are [cu_seqlens_q[i], cu_seqlens_q[i+1]) for q/o/lse/indices and
+ * [cu_seqlens_k[i], cu_seqlens_k[i+1]) for k/v; block ids are relative to the
+ * sequence start.  Strides are in elements; the innermost dimension of every
+ * tensor is contiguous.  The reference's SBHD layout (SFA.py:87-90) is the
+ * dense layout with batch and token strides swapped.
+ *
+ * Index semantics.  A selected block id e is valid iff 0 <= e < ceil(kv_len /
+ * block_size); key e*block_size + j (j < block_size) is valid iff it is < kv_len
+ * and, when causal, <= t + kv_len - q_len.  Entries may sit in any slot; a
+ * duplicate entry counts once per slot.  lse is natural-log; a row with no valid
+ * key and no sink has o = 0 and lse = -inf.
+ */
+#ifndef SFA_B200_H
+#define SFA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SFA_ABI_VERSION 1
+
+enum {
+  SFA_OK = 0,
+  SFA_ERR_INVALID_ARGUMENT = -1,   /* bad shape, stride, alignment or null pointer */
+  SFA_ERR_UNSUPPORTED = -2,        /* shape outside every kernel family's limits */
+  SFA_ERR_WORKSPACE = -3,          /* workspace missing or smaller than required */
+  SFA_ERR_CUDA = -4,               /* a CUDA runtime/driver call failed */
+  SFA_ERR_DEVICE_TIMEOUT = -5      /* a kernel's bounded wait expired (see sfa_device_status) */
+};
+
+/* dK/dV algorithm (SfaParams.dkv_mode). */
+enum {
+  SFA_DKV_AUTO = 0,      /* pick from the launch table (measured throughput) */
+  SFA_DKV_INVERTED = 1,  /* block->query inverted index + key-centric pass; deterministic */
+  SFA_DKV_ATOMIC = 2     /* query-centric pass with fp32 atomics */
+};
+
+/* Kernel family (SfaParams.kernel); AUTO picks the tensor-core path when it
+ * supports the shape and the general CUDA-core path otherwise. */
+enum {
+  SFA_KERNEL_AUTO = 0,
+  SFA_KERNEL_TCGEN05 = 1,
+  SFA_KERNEL_GENERAL = 2
+};
+
+typedef struct SfaParams {
+  /* inputs (device pointers) */
+  const void* q;              /* bf16 */
+  const void* k;              /* bf16 */
+  const void* v;              /* bf16 */
+  const int32_t* block_indices;
+  const int32_t* cu_seqlens_q; /* [num_seqs + 1] or NULL for dense */
+  const int32_t* cu_seqlens_k; /* [num_seqs + 1] or NULL for dense */
+  const float* attn_sink;     /* [Hq] fp32 or NULL */
+  /* forward outputs / backward inputs */
+  void* o;                    /* bf16 */
+  float* lse;                 /* fp32, natural log */
+  /* backward */
+  const void* dout;           /* bf16 */
+  void* dq;                   /* bf16 */
+  void* dk;                   /* bf16 */
+  void* dv;                   /* bf16; may equal dk when k and v are one tensor (then dk := dk + dv) */
+  float* dsink;               /* [Hq] fp32 or NULL; overwritten */
+
+  /* element strides: batch (dense only), token, head */
+  int64_t q_sb, q_st, q_sh;
+  int64_t k_sb, k_st, k_sh;
+  int64_t v_sb, v_st, v_sh;
+  int64_t i_sb, i_st, i_sh;   /* block_indices; the S axis is contiguous */
+  int64_t o_sb, o_st, o_sh;
+  int64_t l_sb, l_st, l_sh;   /* lse */
+  int64_t do_sb, do_st, do_sh;
+  int64_t dq_sb, dq_st, dq_sh;
+  int64_t dk_sb, dk_st, dk_sh;
+  int64_t dv_sb, dv_st, dv_sh;
+
+  int32_t batch;      /* B (dense) or number of sequences (varlen) */
+  int32_t q_len;      /* Tq (dense) or max query length over sequences (varlen) */
+  int32_t kv_len;     /* Tk (dense) or max kv length over sequences (varlen) */
+  int32_t total_q;    /* varlen: cu_seqlens_q[batch]; dense: ignored */
+  int32_t total_kv;   /* varlen: cu_seqlens_k[batch]; dense: ignored */
+  int32_t h_q, h_kv;  /* h_q % h_kv == 0 */
+  int32_t d_qk, d_v;
+  int32_t block_size; /* keys per selected block (1 = token-level) */
+  int32_t topk;       /* S, slots per (query, kv head) */
+  float scale;        /* softmax scale applied to q.k */
+  int32_t causal;     /* 0 / 1 */
+  int32_t dkv_mode;   /* SFA_DKV_* */
+  int32_t kernel;     /* SFA_KERNEL_* */
+  int32_t reserved[3];
+} SfaParams;
+
+/* Library / ABI identification. */
+int sfa_abi_version(void);
+const char* sfa_build_info(void);
+
+/* Message for the last non-OK return on this thread. */
+const char* sfa_last_error_string(void);
+
+/* Which kernel family a call with these params would launch (SFA_KERNEL_*), or
+ * a negative error code if the shape is unsupported. */
+int sfa_select_kernel(const SfaParams* p, int is_backward);
+
+/* Workspace (device bytes) the forward / backward need for these params. */
+size_t sfa_fwd_workspace_bytes(const SfaParams* p);
+size_t sfa_bwd_workspace_bytes(const SfaParams* p);
+
+/* Forward: writes o and lse.  Replaces SparseFlashAttentionTriton.forward
+ * (SFA.py:75-164): the reference's `_attn_fwd` launch (SFA.py:122-159) and its
+ * per-launch workspaces (SFA.py:117-120), without the host sync of
+ * `_effective_topk` (SFA.py:62-66). */
+int sfa_fwd(const SfaParams* p, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward: writes dq, dk, dv and (if non-NULL) dsink.  Replaces
+ * SparseFlashAttentionTriton.backward (SFA.py:167-306): `_attn_bwd_dq_dsink`
+ * (SFA.py:199-251) and `_attn_bwd_dk_dv` (SFA.py:266-298). */
+int sfa_bwd(const SfaParams* p, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The backward's stages, for callers that schedule them separately.  Each takes
+ * the same workspace as sfa_bwd.
+ *  - preprocess: delta = rowsum(o * dout) in fp32 and dsink
+ *    (replaces `_get_delta_split`, SFA.py:590-610, and the dsink atomics,
+ *    SFA.py:964-970);
+ *  - dq: replaces `_attn_bwd_dq_dsink` / `_inner_dq` (SFA.py:613-716, 856-1002);
+ *  - dkdv: replaces `_attn_bwd_dk_dv` / `_inner_dkv` (SFA.py:719-853, 1005-1145);
+ *    with SFA_DKV_INVERTED it first builds the block->query index. */
+int sfa_bwd_preprocess(const SfaParams* p, void* workspace, size_t workspace_bytes, void* stream);
+int sfa_bwd_dq(const SfaParams* p, void* workspace, size_t workspace_bytes, void* stream);
+int sfa_bwd_dkdv(const SfaParams* p, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Inverted index alone (for tests): for every (sequence, kv head, block) the
+ * list of query rows that selected it, ascending by (query, slot).  Layout in
+ * the workspace is described by sfa_inverted_index_layout(). */
+int sfa_build_inverted_index(const SfaParams* p, void* workspace, size_t workspace_bytes, void* stream);
+/* Byte offsets inside the backward workspace of: block offsets (int32,
+ * [units * nblk + 1]) and query-row entries (int32, [pairs]); also reports
+ * nblk (blocks per unit) and units (= batch * h_kv). */
+int sfa_inverted_index_layout(const SfaParams* p, size_t* offsets_off, size_t* entries_off,
+                              int32_t* nblk, int32_t* units);
+
+/* Device status word written by kernels whose bounded waits expired.
+ * sfa_device_status copies it to *status (synchronising `stream`); sfa_reset_device_status
+ * clears it (stream-ordered). 0 = healthy. */
+int sfa_device_status(void* stream, int32_t* status);
+int sfa_reset_device_status(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SFA_B200_H */

@@ -1,0 +1,13 @@
+"""ops_b200 — B200-native (sm_100a) sparse flash attention.
+
+Public surface:
+  sparse_flash_attention(q, k, v, block_indices, ...) -> (o, lse)
+  SparseFlashAttention.apply(q, kv, attn_sink, topk_idxs, sm_scale) -> out   # reference signature
+The kernels live in libsfa_b200.so (C ABI: include/sfa_b200.h).
+"""
+from ._lib import SfaError, SfaParams, load as load_library
+from .sfa import SparseFlashAttention, reference_lse2, sparse_flash_attention
+from . import tiling
+
+__all__ = ["sparse_flash_attention", "SparseFlashAttention", "SfaError", "SfaParams", "load_library",
+           "reference_lse2", "tiling"]

@@ -1,0 +1,68 @@
+// sfa_internal.h — host-side declarations shared by the SFA translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/sfa_b200.h"
+
+namespace sfa {
+
+inline int num_rows_host(const SfaParams& p) {
+  return p.cu_seqlens_q == nullptr ? p.batch * p.q_len : p.total_q;
+}
+inline int64_t kv_rows_host(const SfaParams& p) {
+  return p.cu_seqlens_q == nullptr ? (int64_t)p.batch * p.kv_len : (int64_t)p.total_kv;
+}
+
+// Backward workspace carve-up (all regions 256-byte aligned).
+struct BwdLayout {
+  size_t delta;        // float [rows * h_q]
+  size_t dsink_part;   // float [pre_ctas * h_q]
+  size_t dk_acc;       // float [kv_rows * h_kv * d_qk]   (atomic dk/dv path)
+  size_t dv_acc;       // float [kv_rows * h_kv * d_v]    (atomic dk/dv path; unused when dv == dk)
+  size_t inv_offsets;  // int32 [units * nblk + 1]        (inverted path)
+  size_t inv_entries;  // int32 [pairs]                   (inverted path)
+  size_t inv_cursor;   // int32 [units * nblk]            (inverted path scratch)
+  size_t dq_acc;       // float [rows * h_q * d_qk]        (key-centric dq path)
+  size_t total;
+  int pre_ctas;
+  int nblk;
+  int units;
+  int64_t pairs;
+  bool atomic_dkv;
+  bool inverted_dkv;
+};
+
+constexpr int kPreRows = 16;  // query rows per preprocess CTA
+
+BwdLayout bwd_layout(const SfaParams& p, int kernel_family, int dkv_mode);
+
+// general (CUDA-core) family
+cudaError_t launch_fwd_general(const SfaParams& p, cudaStream_t st);
+cudaError_t launch_bwd_general(const SfaParams& p, const float* delta, float* dk_acc, float* dv_acc,
+                               cudaStream_t st);
+size_t fwd_general_smem(const SfaParams& p, int HG);
+size_t bwd_general_smem(const SfaParams& p, int HG);
+int general_head_group(const SfaParams& p);
+
+// backward preprocessing / epilogues
+cudaError_t launch_preprocess(const SfaParams& p, float* delta, float* dsink_part, int pre_ctas, cudaStream_t st);
+cudaError_t launch_convert_dkdv(const SfaParams& p, const float* dk_acc, const float* dv_acc, cudaStream_t st);
+
+// inverted block->query index
+cudaError_t launch_inverted_index(const SfaParams& p, const BwdLayout& L, char* ws, cudaStream_t st);
+
+// tensor-core (tcgen05) family
+bool tc_fwd_supported(const SfaParams& p, const char** why);
+bool tc_bwd_supported(const SfaParams& p, const char** why);
+cudaError_t launch_fwd_tc(const SfaParams& p, cudaStream_t st);
+cudaError_t launch_bwd_dq_tc(const SfaParams& p, const float* delta, cudaStream_t st);
+cudaError_t launch_bwd_dkdv_tc(const SfaParams& p, const BwdLayout& L, char* ws, const float* delta,
+                               cudaStream_t st);
+
+int device_sm_count();
+int device_cc();
+
+}  // namespace sfa

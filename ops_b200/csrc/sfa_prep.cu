@@ -1,0 +1,330 @@
+// sfa_prep.cu — backward preprocessing and bookkeeping kernels (CUDA cores,
+// HBM-bound):
+//   * delta = rowsum(o * dO) per (row, head) in fp32 plus per-CTA partial
+//     dsink sums, reduced in a fixed order (deterministic).  Replaces the
+//     reference's `_get_delta_split` (SFA.py:590-610), which both backward
+//     kernels recompute, and its dsink atomics (SFA.py:964-970).
+//   * fp32 dk/dv accumulators -> bf16 outputs (atomic dk/dv path).
+//   * the block->query inverted index used by the key-centric dk/dv pass:
+//     count -> exclusive scan -> fill, deterministic (no atomics on positions).
+#include "sfa_common.cuh"
+#include "sfa_internal.h"
+
+namespace sfa {
+
+// ---------------------------------------------------------------------------
+// delta + dsink partials
+// ---------------------------------------------------------------------------
+constexpr int kPreThreads = 256;
+
+__global__ void __launch_bounds__(kPreThreads)
+preprocess_kernel(SfaParams p, float* __restrict__ delta, float* __restrict__ dsink_part) {
+  extern __shared__ float sdelta[];  // [kPreRows][h_q]
+  const int rows = num_rows(p);
+  const int row0 = blockIdx.x * kPreRows;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = kPreThreads / 32;
+  const int Dv = p.d_v;
+  for (int pr = warp; pr < kPreRows * p.h_q; pr += nw) {
+    int rl = pr / p.h_q, h = pr - rl * p.h_q;
+    int row = row0 + rl;
+    float acc = 0.f;
+    if (row < rows) {
+      Row r = row_info(p, row);
+      const __nv_bfloat16* o = reinterpret_cast<const __nv_bfloat16*>(p.o) + r.b * p.o_sb + r.tq * p.o_st + (int64_t)h * p.o_sh;
+      const __nv_bfloat16* dO = reinterpret_cast<const __nv_bfloat16*>(p.dout) + r.b * p.do_sb + r.tq * p.do_st + (int64_t)h * p.do_sh;
+      if ((Dv & 1) == 0) {
+        const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(o);
+        const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(dO);
+        for (int d = lane; d < Dv / 2; d += 32) {
+          float2 a = __bfloat1622float2(o2[d]);
+          float2 b = __bfloat1622float2(d2[d]);
+          acc = fmaf(a.x, b.x, acc);
+          acc = fmaf(a.y, b.y, acc);
+        }
+      } else {
+        for (int d = lane; d < Dv; d += 32) acc = fmaf(bf2f(o[d]), bf2f(dO[d]), acc);
+      }
+#pragma unroll
+      for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+      if (lane == 0) delta[(int64_t)row * p.h_q + h] = acc;
+    }
+    if (lane == 0) sdelta[pr] = acc;
+  }
+  __syncthreads();
+  if (dsink_part == nullptr) return;
+  for (int h = threadIdx.x; h < p.h_q; h += kPreThreads) {
+    float sink2 = __ldg(p.attn_sink + h) * kLog2e;
+    float acc = 0.f;
+    for (int rl = 0; rl < kPreRows; ++rl) {
+      int row = row0 + rl;
+      if (row >= rows) break;
+      Row r = row_info(p, row);
+      float lse = p.lse[r.b * p.l_sb + r.tq * p.l_st + (int64_t)h * p.l_sh];
+      if (lse == -INFINITY) continue;
+      acc -= exp2f(sink2 - lse * kLog2e) * sdelta[rl * p.h_q + h];
+    }
+    dsink_part[(int64_t)blockIdx.x * p.h_q + h] = acc;
+  }
+}
+
+__global__ void dsink_reduce_kernel(const float* __restrict__ part, int nparts, int hq, float* __restrict__ dsink) {
+  // one warp per head, fixed-order pairwise tree over lanes: deterministic
+  int h = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  int lane = threadIdx.x & 31;
+  if (h >= hq) return;
+  float acc = 0.f;
+  for (int i = lane; i < nparts; i += 32) acc += part[(int64_t)i * hq + h];
+#pragma unroll
+  for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) dsink[h] = acc;
+}
+
+cudaError_t launch_preprocess(const SfaParams& p, float* delta, float* dsink_part, int pre_ctas, cudaStream_t st) {
+  if (pre_ctas == 0) {
+    if (p.dsink) return cudaMemsetAsync(p.dsink, 0, sizeof(float) * p.h_q, st);
+    return cudaSuccess;
+  }
+  size_t smem = sizeof(float) * kPreRows * p.h_q;
+  cudaError_t e = cudaFuncSetAttribute(preprocess_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  float* part = (p.dsink && p.attn_sink) ? dsink_part : nullptr;
+  preprocess_kernel<<<pre_ctas, kPreThreads, smem, st>>>(p, delta, part);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (p.dsink) {
+    if (!p.attn_sink) return cudaMemsetAsync(p.dsink, 0, sizeof(float) * p.h_q, st);
+    dsink_reduce_kernel<<<(p.h_q + 7) / 8, 256, 0, st>>>(part, pre_ctas, p.h_q, p.dsink);
+    e = cudaGetLastError();
+  }
+  return e;
+}
+
+// ---------------------------------------------------------------------------
+// fp32 accumulators -> bf16 dk / dv (or dk := dk + dv when they alias)
+// ---------------------------------------------------------------------------
+__global__ void convert_kernel(SfaParams p, const float* __restrict__ acc, int D, int64_t sb, int64_t st,
+                               int64_t sh, __nv_bfloat16* __restrict__ out, const float* __restrict__ acc2) {
+  int64_t n = (p.cu_seqlens_q == nullptr ? (int64_t)p.batch * p.kv_len : (int64_t)p.total_kv) * p.h_kv * D;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    int d = (int)(i % D);
+    int64_t rest = i / D;
+    int hk = (int)(rest % p.h_kv);
+    int64_t kr = rest / p.h_kv;
+    int64_t b = 0, t = kr;
+    if (p.cu_seqlens_q == nullptr) { b = kr / p.kv_len; t = kr - b * p.kv_len; }
+    float v = acc[i];
+    if (acc2) v += acc2[i];
+    out[b * sb + t * st + hk * sh + d] = f2bf(v);
+  }
+}
+
+cudaError_t launch_convert_dkdv(const SfaParams& p, const float* dk_acc, const float* dv_acc, cudaStream_t st) {
+  int sms = device_sm_count();
+  int grid = sms * 8;
+  bool shared_kv = (p.dk == p.dv);
+  convert_kernel<<<grid, 256, 0, st>>>(p, dk_acc, p.d_qk, p.dk_sb, p.dk_st, p.dk_sh,
+                                       reinterpret_cast<__nv_bfloat16*>(p.dk), shared_kv ? dv_acc : nullptr);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || shared_kv) return e;
+  convert_kernel<<<grid, 256, 0, st>>>(p, dv_acc, p.d_v, p.dv_sb, p.dv_st, p.dv_sh,
+                                       reinterpret_cast<__nv_bfloat16*>(p.dv), nullptr);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// inverted index: for unit u = (sequence, kv head) and block e, the query rows
+// that selected e.  Order inside a list: (sub-chunk of 32 rows, slot, lane) —
+// fixed, so the key-centric pass sums in a reproducible order.
+//
+// counts layout: [units][nblk][nsub] (flat exclusive scan gives positions)
+// ---------------------------------------------------------------------------
+constexpr int kInvWarps = 8;
+constexpr int kInvRowsPerWarp = 128;   // 4 batches of 32 rows
+constexpr int kInvRowsPerCta = kInvWarps * kInvRowsPerWarp;
+
+struct UnitRows {
+  int row0;   // first global row of the unit's sequence
+  int q_len;
+};
+
+__device__ __forceinline__ UnitRows unit_rows(const SfaParams& p, int seq) {
+  UnitRows u;
+  if (p.cu_seqlens_q == nullptr) {
+    u.row0 = seq * p.q_len;
+    u.q_len = p.q_len;
+  } else {
+    u.row0 = __ldg(p.cu_seqlens_q + seq);
+    u.q_len = __ldg(p.cu_seqlens_q + seq + 1) - u.row0;
+  }
+  return u;
+}
+
+template <bool kFill>
+__global__ void __launch_bounds__(kInvWarps * 32)
+inv_pass_kernel(SfaParams p, int nblk, int nsub, int32_t* __restrict__ counts, int32_t* __restrict__ entries) {
+  extern __shared__ int32_t scnt[];  // [kInvWarps][nblk]
+  const int seq = blockIdx.y / p.h_kv, hk = blockIdx.y - seq * p.h_kv;
+  const int unit = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const UnitRows ur = unit_rows(p, seq);
+  const int sub = blockIdx.x * kInvWarps + warp;  // sub-chunk of kInvRowsPerWarp rows
+  int32_t* cnt = scnt + warp * nblk;
+  int32_t* cbase = counts + (int64_t)unit * nblk * nsub + sub;  // stride nsub over blocks
+  for (int e = lane; e < nblk; e += 32) cnt[e] = kFill ? cbase[(int64_t)e * nsub] : 0;
+  __syncwarp();
+  const int t_begin = sub * kInvRowsPerWarp;
+  for (int tb = t_begin; tb < t_begin + kInvRowsPerWarp && tb < ur.q_len; tb += 32) {
+    int t = tb + lane;
+    bool live = t < ur.q_len;
+    Row r;
+    const int32_t* idx = nullptr;
+    if (live) {
+      r = row_info(p, ur.row0 + t);
+      idx = p.block_indices + r.b * p.i_sb + r.tq * p.i_st + (int64_t)hk * p.i_sh;
+    }
+    for (int s = 0; s < p.topk; ++s) {
+      int e = -1;
+      if (live) {
+        int ev = __ldg(idx + s);
+        if (block_valid_keys(ev, p.block_size, r.kv_len, r.pos, p.causal) > 0 && ev < nblk) e = ev;
+      }
+      unsigned grp = __match_any_sync(0xffffffffu, e);
+      int leader = __ffs(grp) - 1;
+      if (e >= 0) {
+        int rank = __popc(grp & ((1u << lane) - 1u));
+        int basepos = 0;
+        if (lane == leader) basepos = cnt[e];
+        basepos = __shfl_sync(grp, basepos, leader);
+        if (kFill) entries[basepos + rank] = ur.row0 + t;
+        if (lane == leader) cnt[e] = basepos + __popc(grp);
+      }
+      __syncwarp();
+    }
+  }
+  __syncwarp();
+  if (!kFill)
+    for (int e = lane; e < nblk; e += 32) cbase[(int64_t)e * nsub] = cnt[e];
+}
+
+// exclusive scan in three launches: tile sums, scan of tile sums, tile scans
+constexpr int kScanTile = 2048;
+constexpr int kScanThreads = 256;
+
+__global__ void scan_tile_sums(const int32_t* __restrict__ in, int64_t n, int32_t* __restrict__ sums) {
+  __shared__ int32_t red[kScanThreads / 32];
+  int64_t base = (int64_t)blockIdx.x * kScanTile;
+  int acc = 0;
+  for (int i = threadIdx.x; i < kScanTile; i += kScanThreads) {
+    int64_t j = base + i;
+    if (j < n) acc += in[j];
+  }
+  for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int s = 0;
+    for (int w = 0; w < kScanThreads / 32; ++w) s += red[w];
+    sums[blockIdx.x] = s;
+  }
+}
+
+__global__ void scan_sums_single(int32_t* __restrict__ sums, int nt, int32_t* __restrict__ total_out) {
+  // one CTA; sequential chunks per thread then a block scan of chunk totals
+  __shared__ int32_t part[1024];
+  int per = (nt + blockDim.x - 1) / blockDim.x;
+  int b = threadIdx.x * per, e = min(nt, b + per);
+  int s = 0;
+  for (int i = b; i < e; ++i) s += sums[i];
+  part[threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int i = 0; i < (int)blockDim.x; ++i) { int v = part[i]; part[i] = run; run += v; }
+    *total_out = run;
+  }
+  __syncthreads();
+  int run = part[threadIdx.x];
+  for (int i = b; i < e; ++i) { int v = sums[i]; sums[i] = run; run += v; }
+}
+
+__global__ void scan_tiles(int32_t* __restrict__ data, int64_t n, const int32_t* __restrict__ tile_off) {
+  __shared__ int32_t wsum[kScanThreads / 32];
+  int64_t base = (int64_t)blockIdx.x * kScanTile;
+  constexpr int per = kScanTile / kScanThreads;  // 8 consecutive items per thread
+  int local[per];
+  int s = 0;
+  for (int k = 0; k < per; ++k) {
+    int64_t j = base + threadIdx.x * per + k;
+    local[k] = j < n ? data[j] : 0;
+    s += local[k];
+  }
+  // warp inclusive scan of per-thread sums
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int incl = s;
+  for (int off = 1; off < 32; off <<= 1) {
+    int v = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += v;
+  }
+  if (lane == 31) wsum[w] = incl;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int i = 0; i < kScanThreads / 32; ++i) { int v = wsum[i]; wsum[i] = run; run += v; }
+  }
+  __syncthreads();
+  int run = tile_off[blockIdx.x] + wsum[w] + incl - s;
+  for (int k = 0; k < per; ++k) {
+    int64_t j = base + threadIdx.x * per + k;
+    if (j < n) data[j] = run;
+    run += local[k];
+  }
+}
+
+// offsets[u*nblk + e] = scanned[(u*nblk + e)*nsub]; offsets[units*nblk] = total
+__global__ void gather_offsets(const int32_t* __restrict__ scanned, int64_t nlists, int nsub,
+                               const int32_t* __restrict__ total, int32_t* __restrict__ offsets) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i <= nlists; i += (int64_t)gridDim.x * blockDim.x)
+    offsets[i] = i < nlists ? scanned[i * nsub] : *total;
+}
+
+cudaError_t launch_inverted_index(const SfaParams& p, const BwdLayout& L, char* ws, cudaStream_t st) {
+  const int nblk = L.nblk;
+  const int qmax = p.q_len;
+  const int nsub = (qmax + kInvRowsPerWarp - 1) / kInvRowsPerWarp;
+  const int ctas_x = (nsub + kInvWarps - 1) / kInvWarps;
+  const int nsub_pad = ctas_x * kInvWarps;
+  const int64_t ncount = (int64_t)L.units * nblk * nsub_pad;
+  int32_t* counts = reinterpret_cast<int32_t*>(ws + L.inv_cursor);
+  int32_t* entries = reinterpret_cast<int32_t*>(ws + L.inv_entries);
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.inv_offsets);
+  const int64_t ntiles = (ncount + kScanTile - 1) / kScanTile;
+  int32_t* tile_sums = counts + ncount;          // [ntiles]
+  int32_t* total = tile_sums + ntiles;           // [1]
+  size_t smem = sizeof(int32_t) * kInvWarps * nblk;
+  cudaError_t e;
+  e = cudaFuncSetAttribute(inv_pass_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(inv_pass_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(counts, 0, sizeof(int32_t) * ncount, st);
+  if (e != cudaSuccess) return e;
+  dim3 grid(ctas_x, L.units);
+  inv_pass_kernel<false><<<grid, kInvWarps * 32, smem, st>>>(p, nblk, nsub_pad, counts, entries);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  scan_tile_sums<<<(unsigned)ntiles, kScanThreads, 0, st>>>(counts, ncount, tile_sums);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  scan_sums_single<<<1, 1024, 0, st>>>(tile_sums, (int)ntiles, total);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  scan_tiles<<<(unsigned)ntiles, kScanThreads, 0, st>>>(counts, ncount, tile_sums);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  const int64_t nlists = (int64_t)L.units * nblk;
+  const int64_t gblocks = (nlists + 1 + 255) / 256;
+  gather_offsets<<<(unsigned)(gblocks < 4096 ? gblocks : 4096), 256, 0, st>>>(
+      counts, nlists, nsub_pad, total, offsets);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  inv_pass_kernel<true><<<grid, kInvWarps * 32, smem, st>>>(p, nblk, nsub_pad, counts, entries);
+  return cudaGetLastError();
+}
+
+}  // namespace sfa

@@ -1,0 +1,86 @@
+"""The C-ABI library: loads without a GPU, exports every declared symbol, and
+its parameter struct matches the header byte for byte (checked with gcc)."""
+import ctypes
+import os
+import re
+import subprocess
+import tempfile
+
+import pytest
+
+from ops_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "sfa_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\*?\s*(sfa_[a-z0-9_]+)\s*\(", src, re.M)))
+
+
+def test_library_loads_and_exports_all_declared_symbols():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 14
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in _lib.EXPORTS, f"{n} has no ctypes signature"
+    assert lib.sfa_abi_version() == 1
+    assert b"sm_100a" in lib.sfa_build_info()
+
+
+def test_struct_layout_matches_header():
+    fields = [f[0] for f in _lib.SfaParams._fields_]
+    prog = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void){",
+            'printf("%zu\\n", sizeof(SfaParams));']
+    for f in fields:
+        prog.append(f'printf("%zu\\n", offsetof(SfaParams, {f}));')
+    prog.append("return 0;}")
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        open(c, "w").write("\n".join(prog))
+        exe = os.path.join(d, "t")
+        subprocess.run(["gcc", c, "-o", exe], check=True)
+        out = [int(x) for x in subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()]
+    assert out[0] == ctypes.sizeof(_lib.SfaParams)
+    for f, off in zip(fields, out[1:]):
+        assert getattr(_lib.SfaParams, f).offset == off, f
+
+
+def _params(**kw):
+    P = _lib.SfaParams()
+    fake = 0x10000
+    for n in ("q", "k", "v", "block_indices", "o", "lse"):
+        setattr(P, n, fake)
+    P.batch, P.q_len, P.kv_len, P.h_q, P.h_kv, P.d_qk, P.d_v = 1, 64, 64, 16, 1, 64, 64
+    P.block_size, P.topk, P.scale, P.causal = 64, 1, 0.125, 1
+    for k, v in kw.items():
+        setattr(P, k, v)
+    return P
+
+
+@pytest.mark.parametrize("field,value,msg", [
+    ("h_kv", 3, "multiple"), ("topk", 0, "topk"), ("block_size", 0, "block_size"), ("q", None, "non-NULL"),
+    ("d_v", 0, "positive"), ("kernel", 7, "kernel"),
+])
+def test_argument_validation_without_gpu(field, value, msg):
+    lib = _lib.load()
+    P = _params(**{field: value})
+    rc = lib.sfa_select_kernel(ctypes.byref(P), 0)
+    assert rc == _lib.SFA_ERR_INVALID_ARGUMENT
+    assert msg in lib.sfa_last_error_string().decode()
+
+
+def test_backward_requires_gradient_buffers():
+    lib = _lib.load()
+    P = _params()
+    assert lib.sfa_select_kernel(ctypes.byref(P), 1) == _lib.SFA_ERR_INVALID_ARGUMENT
+    assert lib.sfa_bwd_workspace_bytes(ctypes.byref(P)) == 0
+
+
+def test_oversized_head_dims_are_unsupported_by_general_family():
+    lib = _lib.load()
+    P = _params(d_qk=8192, d_v=8192, kernel=_lib.SFA_KERNEL_GENERAL)
+    assert lib.sfa_select_kernel(ctypes.byref(P), 0) == _lib.SFA_ERR_UNSUPPORTED

@@ -1,0 +1,94 @@
+"""Host-side logic on the CPU: index generation for the benchmark configs,
+FLOP/pair accounting, the tiling layer, and input validation of the Python
+surface (which must refuse CPU tensors — there is no CPU implementation)."""
+import pytest
+import torch
+
+from oracle import sfa_oracle as O
+from ops_b200 import tiling, workloads as W
+
+
+def test_uniform_causal_indices_follow_the_config_rules():
+    cfg = W.scaled(W.CONFIGS["c2"], B=1, T=2048, Hk=2, S=16)
+    idx = W.make_indices(cfg)
+    T = cfg.T
+    cur = torch.arange(T) // cfg.bs
+    for h in range(cfg.Hk):
+        sel = idx[0, :, h]
+        assert (sel == cur[:, None]).any(1).all(), "current block always included"
+        valid = sel >= 0
+        assert ((sel <= cur[:, None]) | ~valid).all(), "causal range"
+        n_avail = torch.clamp(cur + 1, max=cfg.S)
+        assert torch.equal(valid.sum(1), n_avail), "-1 only when fewer blocks exist"
+        for t in (0, 100, 2047):
+            s = sel[t][sel[t] >= 0]
+            assert len(set(s.tolist())) == len(s), "without replacement"
+
+
+def test_recent_biased_indices():
+    cfg = W.scaled(W.CONFIGS["c3"], T=4096, Hk=1, S=32)
+    idx = W.make_indices(cfg)
+    cur = torch.arange(cfg.T) // cfg.bs
+    late = idx[0, 2048:, 0].long()
+    recent = (late > cur[2048:, None] - 8) & (late >= 0)
+    # with half the mass on 8 blocks, nearly all of them are picked
+    assert recent.sum(1).float().mean() > 7.5
+
+
+def test_token_level_indices():
+    cfg = W.scaled(W.CONFIGS["c4"], T=300, S=64)
+    idx = W.make_indices(cfg)
+    t = torch.arange(cfg.T)
+    sel = idx[0, :, 0]
+    assert ((sel <= t[:, None]) | (sel < 0)).all()
+    assert torch.equal((sel >= 0).sum(1), torch.clamp(t + 1, max=64))
+
+
+def test_decode_inputs():
+    cfg = W.scaled(W.CONFIGS["c5"], n_seqs=6, kv_min=100, kv_max=900, Hq=8, Hk=2, S=4)
+    d = W.make_decode(cfg)
+    assert d["q"].shape == (6, 8, 128) and d["cu_q"].tolist() == list(range(7))
+    nb = (d["kv_lens"] + 63) // 64
+    valid = d["idx"] >= 0
+    assert ((d["idx"] < nb[:, None, None]) | ~valid).all()
+    assert torch.equal(valid.sum(-1), torch.clamp(nb, max=4)[:, None].expand(-1, 2))
+
+
+@pytest.mark.parametrize("name", ["c1"])
+def test_pair_count_matches_oracle(name):
+    cfg = W.CONFIGS[name]
+    idx = W.make_indices(cfg)
+    a = W.count_pairs(idx, cfg.bs, cfg.T, cfg.T)
+    b = O.selected_pairs(idx, cfg.bs, cfg.T, cfg.T)
+    assert a == b
+    f = O.sfa_flops(a * cfg.Hq // cfg.Hk, cfg.Dqk, cfg.Dv)
+    assert 4.5e9 < f.total < 6e9   # about 5.4 GFLOP for config 1
+
+
+def test_reference_tiling_buckets():
+    assert tiling.resolve_tiling_config(128).BLOCK_N == 64
+    assert tiling.resolve_tiling_config(150).BLOCK_K_BWD == 40
+    assert tiling.resolve_tiling_config(2048).BLOCK_K_BWD == 64
+    with pytest.raises(ValueError):
+        tiling.resolve_tiling_config(0)
+    assert tiling.effective_topk(torch.tensor([[[1, 2, -1]], [[-1, -1, -1]]])) == 2
+    with pytest.raises(ValueError):
+        tiling.effective_topk(torch.empty(0))
+
+
+def test_python_surface_refuses_cpu_tensors():
+    import ops_b200
+    q = torch.randn(1, 4, 2, 8).bfloat16()
+    k = torch.randn(1, 4, 1, 8).bfloat16()
+    idx = torch.zeros(1, 4, 1, 1, dtype=torch.int32)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops_b200.sparse_flash_attention(q, k, k, idx, 4)
+
+
+def test_oracle_index_semantics():
+    # block 1 of size 4 for a query at position 5: keys 4,5 valid, 6,7 masked
+    keys, ok = O.key_table(torch.tensor([[1, -1, 9, 1]]), 4, torch.tensor([5]), 10, True)
+    assert keys[0, :4].tolist() == [4, 5, 0, 0] and ok[0, :4].tolist() == [True, True, False, False]
+    assert not ok[0, 4:8].any()              # -1
+    assert not ok[0, 8:12].any()             # block 9 is past kv_len 10 (blocks 0..2)
+    assert ok[0, 12:].tolist() == [True, True, False, False]   # duplicate counts again
