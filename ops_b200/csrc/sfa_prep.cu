@@ -124,7 +124,8 @@ cudaError_t launch_convert_dkdv(const SfaParams& p, const float* dk_acc, const f
   int grid = sms * 8;
   bool shared_kv = (p.dk == p.dv);
   convert_kernel<<<grid, 256, 0, st>>>(p, dk_acc, p.d_qk, p.dk_sb, p.dk_st, p.dk_sh,
-                                       reinterpret_cast<__nv_bfloat16*>(p.dk), shared_kv ? dv_acc : nullptr);
+                                       reinterpret_cast<__nv_bfloat16*>(p.dk),
+                                       (shared_kv && dv_acc != dk_acc) ? dv_acc : nullptr);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || shared_kv) return e;
   convert_kernel<<<grid, 256, 0, st>>>(p, dv_acc, p.d_v, p.dv_sb, p.dv_st, p.dv_sh,
@@ -141,7 +142,6 @@ cudaError_t launch_convert_dkdv(const SfaParams& p, const float* dk_acc, const f
 // ---------------------------------------------------------------------------
 constexpr int kInvWarps = 8;
 constexpr int kInvRowsPerWarp = 128;   // 4 batches of 32 rows
-constexpr int kInvRowsPerCta = kInvWarps * kInvRowsPerWarp;
 
 struct UnitRows {
   int row0;   // first global row of the unit's sequence
