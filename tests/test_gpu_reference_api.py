@@ -34,7 +34,8 @@ def test_reference_signature_against_golden(name):
     # against the reference's own outputs: within the reference's bf16 rounding
     assert max_abs_norm(out, d["out"]) < 2e-2 and rel_l2(out, d["out"]) < 1e-2
     assert rel_l2(dq, d["dq"]) < 1.5e-2 and rel_l2(dkv, d["dkv"]) < 1.5e-2
-    assert (dsink - d["dsink"]).abs().max() < 2e-2
+    # dsink sums -p_sink*delta over every row; delta comes from each side's own bf16 o
+    assert max_abs_norm(dsink, d["dsink"]) < 2e-2
     # against the oracle: the op's own tolerance
     o_ref, lse_ref = O.reference_compat_forward(d["q"], d["kv"], d["sink"], d["idx"], d["scale"])
     assert_close("o", out, o_ref)
