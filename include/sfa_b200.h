@@ -118,6 +118,10 @@ const char* sfa_build_info(void);
 /* Message for the last non-OK return on this thread. */
 const char* sfa_last_error_string(void);
 
+/* Number of kernels this library has enqueued since it was loaded (all
+ * threads); a caller brackets a region with two reads to count its launches. */
+unsigned long long sfa_kernel_launches(void);
+
 /* Which kernel family a call with these params would launch (SFA_KERNEL_*), or
  * a negative error code if the shape is unsupported. */
 int sfa_select_kernel(const SfaParams* p, int is_backward);

@@ -48,6 +48,7 @@ EXPORTS = {
     "sfa_abi_version": ([], _i32),
     "sfa_build_info": ([], ctypes.c_char_p),
     "sfa_last_error_string": ([], ctypes.c_char_p),
+    "sfa_kernel_launches": ([], ctypes.c_ulonglong),
     "sfa_select_kernel": ([ctypes.POINTER(SfaParams), _i32], _i32),
     "sfa_fwd_workspace_bytes": ([ctypes.POINTER(SfaParams)], ctypes.c_size_t),
     "sfa_bwd_workspace_bytes": ([ctypes.POINTER(SfaParams)], ctypes.c_size_t),

@@ -8,6 +8,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -71,6 +72,9 @@ int device_cc() {
   }
   return cache[dev];
 }
+
+static std::atomic<unsigned long long> g_launches{0};
+void note_launch(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -190,6 +194,8 @@ const char* sfa_build_info(void) {
 }
 
 const char* sfa_last_error_string(void) { return g_err.c_str(); }
+
+unsigned long long sfa_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int sfa_select_kernel(const SfaParams* p, int is_backward) {
   int rc = validate(p, is_backward != 0);

@@ -65,4 +65,7 @@ cudaError_t launch_bwd_dkdv_tc(const SfaParams& p, const BwdLayout& L, char* ws,
 int device_sm_count();
 int device_cc();
 
+// Count of kernels this library has enqueued (reported by sfa_kernel_launches).
+void note_launch(int n = 1);
+
 }  // namespace sfa

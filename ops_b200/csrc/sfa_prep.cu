@@ -90,11 +90,13 @@ cudaError_t launch_preprocess(const SfaParams& p, float* delta, float* dsink_par
   if (e != cudaSuccess) return e;
   float* part = (p.dsink && p.attn_sink) ? dsink_part : nullptr;
   preprocess_kernel<<<pre_ctas, kPreThreads, smem, st>>>(p, delta, part);
+  note_launch();
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (p.dsink) {
     if (!p.attn_sink) return cudaMemsetAsync(p.dsink, 0, sizeof(float) * p.h_q, st);
     dsink_reduce_kernel<<<(p.h_q + 7) / 8, 256, 0, st>>>(part, pre_ctas, p.h_q, p.dsink);
+    note_launch();
     e = cudaGetLastError();
   }
   return e;
@@ -126,10 +128,12 @@ cudaError_t launch_convert_dkdv(const SfaParams& p, const float* dk_acc, const f
   convert_kernel<<<grid, 256, 0, st>>>(p, dk_acc, p.d_qk, p.dk_sb, p.dk_st, p.dk_sh,
                                        reinterpret_cast<__nv_bfloat16*>(p.dk),
                                        (shared_kv && dv_acc != dk_acc) ? dv_acc : nullptr);
+  note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || shared_kv) return e;
   convert_kernel<<<grid, 256, 0, st>>>(p, dv_acc, p.d_v, p.dv_sb, p.dv_st, p.dv_sh,
                                        reinterpret_cast<__nv_bfloat16*>(p.dv), nullptr);
+  note_launch();
   return cudaGetLastError();
 }
 
@@ -311,19 +315,25 @@ cudaError_t launch_inverted_index(const SfaParams& p, const BwdLayout& L, char* 
   if (e != cudaSuccess) return e;
   dim3 grid(ctas_x, L.units);
   inv_pass_kernel<false><<<grid, kInvWarps * 32, smem, st>>>(p, nblk, nsub_pad, counts, entries);
+  note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   scan_tile_sums<<<(unsigned)ntiles, kScanThreads, 0, st>>>(counts, ncount, tile_sums);
+  note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   scan_sums_single<<<1, 1024, 0, st>>>(tile_sums, (int)ntiles, total);
+  note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   scan_tiles<<<(unsigned)ntiles, kScanThreads, 0, st>>>(counts, ncount, tile_sums);
+  note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   const int64_t nlists = (int64_t)L.units * nblk;
   const int64_t gblocks = (nlists + 1 + 255) / 256;
   gather_offsets<<<(unsigned)(gblocks < 4096 ? gblocks : 4096), 256, 0, st>>>(
       counts, nlists, nsub_pad, total, offsets);
+  note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   inv_pass_kernel<true><<<grid, kInvWarps * 32, smem, st>>>(p, nblk, nsub_pad, counts, entries);
+  note_launch();
   return cudaGetLastError();
 }
 
