@@ -129,7 +129,7 @@ static int select_family(const SfaParams& p, bool bwd, std::string* why) {
 
 static int resolve_dkv_mode(const SfaParams& p, int family) {
   if (family == SFA_KERNEL_GENERAL) return SFA_DKV_ATOMIC;
-  if (p.dkv_mode == SFA_DKV_ATOMIC) return SFA_DKV_ATOMIC;
+  if (p.dkv_mode == SFA_DKV_ATOMIC || !tc_dkdv_available()) return SFA_DKV_ATOMIC;
   return SFA_DKV_INVERTED;
 }
 
@@ -272,10 +272,10 @@ int sfa_bwd_dq(const SfaParams* p, void* workspace, size_t workspace_bytes, void
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const float* delta = reinterpret_cast<const float*>(ws + L.delta);
   cudaError_t e;
-  if (fam == SFA_KERNEL_TCGEN05 && mode == SFA_DKV_INVERTED) {
+  if (fam == SFA_KERNEL_TCGEN05) {
     e = launch_bwd_dq_tc(*p, delta, st);
   } else {
-    // the general / atomic kernel computes dq together with dk/dv
+    // the general kernel computes dq together with the dk/dv atomics
     float* dk_acc = reinterpret_cast<float*>(ws + L.dk_acc);
     float* dv_acc = reinterpret_cast<float*>(ws + L.dv_acc);
     const int64_t kvr = kv_rows_host(*p);
@@ -300,9 +300,21 @@ int sfa_bwd_dkdv(const SfaParams* p, void* workspace, size_t workspace_bytes, vo
     e = launch_inverted_index(*p, L, ws, st);
     if (e == cudaSuccess) e = launch_bwd_dkdv_tc(*p, L, ws, delta, st);
   } else {
-    // accumulators were filled by sfa_bwd_dq's fused pass
-    e = launch_convert_dkdv(*p, reinterpret_cast<const float*>(ws + L.dk_acc),
-                            reinterpret_cast<const float*>(ws + L.dv_acc), st);
+    float* dk_acc = reinterpret_cast<float*>(ws + L.dk_acc);
+    float* dv_acc = reinterpret_cast<float*>(ws + L.dv_acc);
+    e = cudaSuccess;
+    if (fam == SFA_KERNEL_TCGEN05) {
+      // dq came from the tensor-core kernel; the atomic pass adds dk/dv only
+      const int64_t kvr = kv_rows_host(*p);
+      e = cudaMemsetAsync(dk_acc, 0, sizeof(float) * kvr * p->h_kv * p->d_qk, st);
+      if (e == cudaSuccess && dv_acc != dk_acc)
+        e = cudaMemsetAsync(dv_acc, 0, sizeof(float) * kvr * p->h_kv * p->d_v, st);
+      SfaParams q = *p;
+      q.dq = nullptr;
+      if (e == cudaSuccess) e = launch_bwd_general(q, delta, dk_acc, dv_acc, st);
+    }
+    // else: the accumulators were filled by sfa_bwd_dq's fused pass
+    if (e == cudaSuccess) e = launch_convert_dkdv(*p, dk_acc, dv_acc, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "sfa_bwd_dkdv");
   return SFA_OK;

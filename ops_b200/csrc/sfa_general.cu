@@ -219,11 +219,13 @@ bwd_general_kernel(SfaParams p, int HG, const float* __restrict__ delta, float* 
       dss[i] = dsv;
     }
     __syncthreads();
-    for (int i = tid; i < nh * Dq; i += kGenThreads) {
-      int h = i / Dq, d = i - h * Dq;
-      float acc = dqs[i];
-      for (int kk = 0; kk < kKC; ++kk) acc = fmaf(dss[h * kKC + kk], ks[kk * Dq + d], acc);
-      dqs[i] = acc;
+    if (p.dq != nullptr) {
+      for (int i = tid; i < nh * Dq; i += kGenThreads) {
+        int h = i / Dq, d = i - h * Dq;
+        float acc = dqs[i];
+        for (int kk = 0; kk < kKC; ++kk) acc = fmaf(dss[h * kKC + kk], ks[kk * Dq + d], acc);
+        dqs[i] = acc;
+      }
     }
     for (int i = tid; i < kKC * Dq; i += kGenThreads) {
       int kk = i / Dq, d = i - kk * Dq, key = keyid[kk];
@@ -241,6 +243,7 @@ bwd_general_kernel(SfaParams p, int HG, const float* __restrict__ delta, float* 
     }
     __syncthreads();
   }
+  if (p.dq == nullptr) return;  // dq computed by another kernel; only the dk/dv atomics here
   __nv_bfloat16* dq = reinterpret_cast<__nv_bfloat16*>(p.dq) + r.b * p.dq_sb + r.tq * p.dq_st + (int64_t)h0 * p.dq_sh;
   for (int i = tid; i < nh * Dq; i += kGenThreads) dq[(i / Dq) * p.dq_sh + i % Dq] = f2bf(dqs[i] * p.scale);
 }

@@ -59,6 +59,7 @@ bool tc_fwd_supported(const SfaParams& p, const char** why);
 bool tc_bwd_supported(const SfaParams& p, const char** why);
 cudaError_t launch_fwd_tc(const SfaParams& p, cudaStream_t st);
 cudaError_t launch_bwd_dq_tc(const SfaParams& p, const float* delta, cudaStream_t st);
+bool tc_dkdv_available();
 cudaError_t launch_bwd_dkdv_tc(const SfaParams& p, const BwdLayout& L, char* ws, const float* delta,
                                cudaStream_t st);
 

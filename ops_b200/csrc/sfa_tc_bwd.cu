@@ -1,8 +1,441 @@
-// placeholder until the tcgen05 backward lands
+// sfa_tc_bwd.cu — tensor-core SFA backward for sm_100a.
+//
+// dQ pass (query-centric, swap-AB like the forward).  Work item = (query row,
+// kv head).  For every 128-key tile of the row's selected blocks:
+//     S^T  = K . Q^T        dP^T = V . dO^T          (M = 128 keys, N = 16 heads)
+//     dS^T = P^T o (dP^T - delta),  P^T = exp2(S^T*scale*log2e - lse2)
+//     dQ^T += K^T . dS^T                              (M = 128 dims, N = 16 heads)
+// lse comes from the forward, so no online softmax: every tile is independent
+// and dQ^T accumulates in TMEM across all tiles of the row.  The K tile is used
+// twice (K-major for S^T, MN-major for dQ^T) and held until the dQ MMA retires.
+// Replaces `_attn_bwd_dq_dsink` / `_inner_dq` (SFA.py:613-716, 856-1002).
+//
+// dK/dV pass (key-centric).  Work item = (sequence, kv head, 64-key block e),
+// taken from an atomic work counter; its query rows come from the inverted
+// block->query index.  Rows are processed 8 queries x 16 heads = 128 at a time:
+//     S  = Qb . K_e^T        dP = dOb . V_e^T         (M = 128 rows, N = 64 keys)
+//     P = exp2(S*scale*log2e - lse2),  dS = P o (dP - delta)
+//     dV^T += dOb^T . P      dK^T += Qb^T . dS        (M = 128 dims, N = 64 keys)
+// dK^T/dV^T stay in TMEM for the whole block; each key block is written once,
+// in a fixed order (no atomics): deterministic.  Replaces `_attn_bwd_dk_dv` /
+// `_inner_dkv` (SFA.py:719-853, 1005-1145) and its fp32 atomics (SFA.py:853).
 #include "sfa_common.cuh"
 #include "sfa_internal.h"
+#include "sfa_tc_common.cuh"
+#include "sfa_tc_host.h"
+
 namespace sfa {
-bool tc_bwd_supported(const SfaParams&, const char** why) { *why = "not built"; return false; }
-cudaError_t launch_bwd_dq_tc(const SfaParams&, const float*, cudaStream_t) { return cudaErrorNotSupported; }
-cudaError_t launch_bwd_dkdv_tc(const SfaParams&, const BwdLayout&, char*, const float*, cudaStream_t) { return cudaErrorNotSupported; }
+using namespace tc;
+
+namespace bwd {
+
+constexpr int kNH = 16;
+constexpr int kMaxTopk = 64;
+constexpr int kJD = 4;
+enum : int { kSentinel = 4 };
+
+// =========================================================================
+// dQ
+// =========================================================================
+namespace dq {
+
+constexpr int kThreads = 192;
+constexpr int kR = 4;            // S/dP TMEM slots and dS smem slots
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColSdP = 0;  // kR x (16 S + 16 dP)
+constexpr uint32_t kColDQ = 128; // 2 x 16
+
+struct JobDesc {
+  int row, hk, b, tq, kv0, kv_len, pos, nblk, flags;
+  int blocks[kMaxTopk];
+};
+
+template <int D>
+struct Smem {
+  static constexpr int kKS = 3, kVS = 2;
+  static constexpr int kStageBytes = 128 * D * 2;
+  static constexpr int kQBytes = kNH * D * 2;
+  alignas(1024) uint8_t kst[kKS][kStageBytes];
+  alignas(1024) uint8_t vst[kVS][kStageBytes];
+  alignas(1024) uint8_t q[2][kQBytes];
+  alignas(1024) uint8_t dO[2][kQBytes];
+  alignas(1024) uint8_t ds[kR][128 * kNH * 2];
+  JobDesc jd[kJD];
+  uint64_t k_full[kKS], k_empty[kKS], v_full[kVS], v_empty[kVS];
+  uint64_t qdo_full[2], qdo_empty[2];
+  uint64_t sdp_full[kR], sdp_empty[kR], ds_full[kR], ds_empty[kR];
+  uint64_t dq_full[2], dq_empty[2];
+  uint64_t jd_full[kJD], jd_empty[kJD];
+  uint32_t tmem_base;
+};
+
+struct Args {
+  SfaParams p;
+  const float* delta;
+  int nitems, nrows, oob_row;
+  int32_t* status;
+};
+
+__device__ __forceinline__ bool wt(uint64_t* bar, uint32_t parity, int32_t* status, int site) {
+  if (mbar_wait(bar, parity)) return true;
+  record_status(status, (2 << 16) | site);
+  return false;
 }
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUtensorMap tmq,
+                     const __grid_constant__ CUtensorMap tmdo, const __grid_constant__ CUtensorMap tmk,
+                     const __grid_constant__ CUtensorMap tmv) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem<D>& sm = *reinterpret_cast<Smem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int KS = Smem<D>::kKS, VS = Smem<D>::kVS;
+  const SfaParams& p = args.p;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.h_q / p.h_kv;
+  int32_t* st = args.status;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < KS; ++i) { mbar_init(&sm.k_full[i], 1); mbar_init(&sm.k_empty[i], 1); }
+    for (int i = 0; i < VS; ++i) { mbar_init(&sm.v_full[i], 1); mbar_init(&sm.v_empty[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.qdo_full[i], 1);
+      mbar_init(&sm.qdo_empty[i], 1);
+      mbar_init(&sm.dq_full[i], 1);
+      mbar_init(&sm.dq_empty[i], 128);
+    }
+    for (int i = 0; i < kR; ++i) {
+      mbar_init(&sm.sdp_full[i], 1);
+      mbar_init(&sm.sdp_empty[i], 128);
+      mbar_init(&sm.ds_full[i], 128);
+      mbar_init(&sm.ds_empty[i], 1);
+    }
+    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 1 + 128); }
+    fence_barrier_init();
+  }
+  for (int i = threadIdx.x; i < 2 * Smem<D>::kQBytes / 16; i += kThreads) {
+    reinterpret_cast<uint4*>(&sm.q[0][0])[i] = make_uint4(0, 0, 0, 0);
+    reinterpret_cast<uint4*>(&sm.dO[0][0])[i] = make_uint4(0, 0, 0, 0);
+  }
+  fence_proxy_async_smem();
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmq);
+    prefetch_tmap(&tmdo);
+    prefetch_tmap(&tmk);
+    prefetch_tmap(&tmv);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ============================================================ producer
+    int job = 0, g = 0;
+    bool ok = true;
+    const uint32_t chunk_bytes = 128u * D * 2u;
+    auto load_tile = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* full, const JobDesc& d, int c) {
+      mbar_arrive_expect_tx(full, chunk_bytes);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int bi = 2 * c + half;
+        const int row = bi < d.nblk ? d.kv0 + d.blocks[bi] * 64 : args.oob_row;
+#pragma unroll
+        for (int cd = 0; cd < D / 64; ++cd)
+          tma_load_4d(dst + cd * 128 * 128 + half * 64 * 128, map, full, cd * 64, d.hk, row, d.b);
+      }
+    };
+    for (int item = blockIdx.x; item < args.nitems && ok; item += gridDim.x, ++job) {
+      const int hk = item / args.nrows, row = item - hk * args.nrows;
+      const Row r = row_info(p, row);
+      const int32_t* idx = p.block_indices + r.b * p.i_sb + r.tq * p.i_st + (int64_t)hk * p.i_sh;
+      const int js = job % kJD;
+      if (lane == 0) ok = wt(&sm.jd_empty[js], ((job / kJD) & 1) ^ 1, st, 1);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+      JobDesc& d = sm.jd[js];
+      int n = 0;
+      for (int s0 = 0; s0 < p.topk; s0 += 32) {
+        const int s = s0 + lane;
+        int e = -1;
+        bool valid = false;
+        if (s < p.topk) {
+          e = __ldg(idx + s);
+          valid = block_valid_keys(e, 64, r.kv_len, r.pos, p.causal) > 0;
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, valid);
+        if (valid) d.blocks[n + __popc(m & ((1u << lane) - 1u))] = e;
+        n += __popc(m);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        d.row = row;
+        d.hk = hk;
+        d.b = r.b;
+        d.tq = (int)r.tq;
+        d.kv0 = (int)r.kv0;
+        d.kv_len = r.kv_len;
+        d.pos = r.pos;
+        d.nblk = n;
+        d.flags = 0;
+        mbar_arrive(&sm.jd_full[js]);
+        const int ib = job & 1;
+        ok = wt(&sm.qdo_empty[ib], ((job >> 1) & 1) ^ 1, st, 2);
+        if (ok) {
+          mbar_arrive_expect_tx(&sm.qdo_full[ib], (uint32_t)(2 * G * D * 2));
+#pragma unroll
+          for (int cd = 0; cd < D / 64; ++cd) {
+            tma_load_4d(&sm.q[ib][cd * kNH * 128], &tmq, &sm.qdo_full[ib], cd * 64, hk * G, (int)r.tq, r.b);
+            tma_load_4d(&sm.dO[ib][cd * kNH * 128], &tmdo, &sm.qdo_full[ib], cd * 64, hk * G, (int)r.tq, r.b);
+          }
+        }
+        for (int c = 0; c < (n + 1) / 2 && ok; ++c, ++g) {
+          const int ks = g % KS, vs = g % VS;
+          if (!(ok = wt(&sm.k_empty[ks], ((g / KS) & 1) ^ 1, st, 3))) break;
+          load_tile(&tmk, sm.kst[ks], &sm.k_full[ks], d, c);
+          if (!(ok = wt(&sm.v_empty[vs], ((g / VS) & 1) ^ 1, st, 4))) break;
+          load_tile(&tmv, sm.vst[vs], &sm.v_full[vs], d, c);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      g = __shfl_sync(0xffffffffu, g, 0);
+    }
+    if (lane == 0 && ok) {
+      const int js = job % kJD;
+      if (wt(&sm.jd_empty[js], ((job / kJD) & 1) ^ 1, st, 5)) {
+        sm.jd[js].flags = kSentinel;
+        mbar_arrive(&sm.jd_full[js]);
+      }
+    }
+  } else if (warp == 1) {
+    // ============================================================ MMA issuer
+    if (lane == 0) {
+      const uint32_t id_sdp = idesc_bf16(128, kNH, false, false);
+      const uint32_t id_dq = idesc_bf16(128, kNH, true, true);
+      const uint32_t lbo_k = D == 128 ? 128u * 128u : 0u;
+      struct Pending { int g, ks, slot, ib, js; bool first, last; };
+      Pending pend{};
+      bool has_pend = false, ok = true;
+      int job = 0, g = 0;
+      auto issue_dq = [&](const Pending& pd) -> bool {
+        if (!wt(&sm.ds_full[pd.slot], (pd.g / kR) & 1, st, 10)) return false;
+        if (pd.first && !wt(&sm.dq_empty[pd.ib], (((pd.js >> 1)) & 1) ^ 1, st, 11)) return false;
+        tc_fence_after();
+        const uint32_t kb = smem_u32(&sm.kst[pd.ks][0]);
+        const uint32_t db = smem_u32(&sm.ds[pd.slot][0]);
+        const uint32_t dcol = tmem + kColDQ + pd.ib * kNH;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t a = smem_desc(kb + kk * 2048, lbo_k, 1024, kSw128);
+          const uint64_t b = smem_desc(db + kk * 16 * (kNH * 2), 0, 256, kSw32);
+          mma_bf16_ss(dcol, a, b, id_dq, (pd.first && kk == 0) ? 0u : 1u);
+        }
+        mma_commit(&sm.k_empty[pd.ks]);
+        mma_commit(&sm.ds_empty[pd.slot]);
+        if (pd.last) {
+          mma_commit(&sm.dq_full[pd.ib]);
+          mbar_arrive(&sm.jd_empty[pd.js % kJD]);
+        }
+        return true;
+      };
+      while (ok) {
+        const int js = job % kJD;
+        if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 12))) break;
+        const JobDesc& d = sm.jd[js];
+        if (d.flags & kSentinel) break;
+        const int ib = job & 1;
+        if (!(ok = wt(&sm.qdo_full[ib], (job >> 1) & 1, st, 13))) break;
+        const int nch = (d.nblk + 1) / 2;
+        if (nch == 0) {
+          if (has_pend) { if (!(ok = issue_dq(pend))) break; has_pend = false; }
+          if (!(ok = wt(&sm.dq_empty[ib], ((job >> 1) & 1) ^ 1, st, 14))) break;
+          mma_commit(&sm.qdo_empty[ib]);
+          mma_commit(&sm.dq_full[ib]);
+          mbar_arrive(&sm.jd_empty[js]);
+          ++job;
+          continue;
+        }
+        const uint32_t qb = smem_u32(&sm.q[ib][0]);
+        const uint32_t ob = smem_u32(&sm.dO[ib][0]);
+        for (int c = 0; c < nch && ok; ++c, ++g) {
+          const int slot = g % kR, ks = g % KS, vs = g % VS;
+          if (!(ok = wt(&sm.sdp_empty[slot], ((g / kR) & 1) ^ 1, st, 15))) break;
+          if (!(ok = wt(&sm.k_full[ks], (g / KS) & 1, st, 16))) break;
+          if (!(ok = wt(&sm.v_full[vs], (g / VS) & 1, st, 17))) break;
+          tc_fence_after();
+          const uint32_t kb = smem_u32(&sm.kst[ks][0]);
+          const uint32_t vb = smem_u32(&sm.vst[vs][0]);
+          const uint32_t scol = tmem + kColSdP + slot * 32;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t ko = (k >> 2) * (128 * 128) + (k & 3) * 32;
+            const uint32_t qo = (k >> 2) * (kNH * 128) + (k & 3) * 32;
+            mma_bf16_ss(scol, smem_desc(kb + ko, 16, 1024, kSw128), smem_desc(qb + qo, 16, 1024, kSw128), id_sdp,
+                        k != 0);
+          }
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t vo = (k >> 2) * (128 * 128) + (k & 3) * 32;
+            const uint32_t oo = (k >> 2) * (kNH * 128) + (k & 3) * 32;
+            mma_bf16_ss(scol + 16, smem_desc(vb + vo, 16, 1024, kSw128), smem_desc(ob + oo, 16, 1024, kSw128),
+                        id_sdp, k != 0);
+          }
+          mma_commit(&sm.v_empty[vs]);
+          mma_commit(&sm.sdp_full[slot]);
+          if (c == nch - 1) mma_commit(&sm.qdo_empty[ib]);
+          if (has_pend && !(ok = issue_dq(pend))) break;
+          pend = Pending{g, ks, slot, ib, job, c == 0, c == nch - 1};
+          has_pend = true;
+        }
+        ++job;
+      }
+      if (ok && has_pend) issue_dq(pend);
+    }
+  } else {
+    // ============================================================ dS / epilogue
+    const int wq = warp & 3;
+    const int lrow = wq * 32 + lane;
+    const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
+    const float c2 = p.scale * kLog2e;
+    int job = 0, g = 0;
+    bool ok = true;
+    while (ok) {
+      const int js = job % kJD;
+      if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 20))) break;
+      const JobDesc& d = sm.jd[js];
+      if (d.flags & kSentinel) break;
+      const int ib = job & 1;
+      float lse2[16], dl[16];
+      const int64_t rowoff = (int64_t)d.row * p.h_q + d.hk * G;
+      const float* lsep = p.lse + d.b * p.l_sb + (int64_t)d.tq * p.l_st + (int64_t)(d.hk * G) * p.l_sh;
+#pragma unroll
+      for (int h = 0; h < 16; ++h) {
+        lse2[h] = h < G ? lsep[h * p.l_sh] * kLog2e : -INFINITY;
+        dl[h] = h < G ? args.delta[rowoff + h] : 0.f;
+      }
+      const int nch = (d.nblk + 1) / 2;
+      for (int c = 0; c < nch && ok; ++c, ++g) {
+        const int slot = g % kR;
+        if (!(ok = wt(&sm.sdp_full[slot], (g / kR) & 1, st, 21))) break;
+        tc_fence_after();
+        float s[16], dp[16];
+        tmem_ld16(tl + kColSdP + slot * 32, s);
+        tmem_ld16(tl + kColSdP + slot * 32 + 16, dp);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&sm.sdp_empty[slot]);
+        const int bi = 2 * c + (lrow >> 6);
+        bool valid = bi < d.nblk;
+        if (valid) {
+          const int key = d.blocks[bi] * 64 + (lrow & 63);
+          valid = key < d.kv_len && (!p.causal || key <= d.pos);
+        }
+        float ds[16];
+#pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          const float pr = (valid && lse2[h] != -INFINITY) ? exp2f(s[h] * c2 - lse2[h]) : 0.f;
+          ds[h] = pr * (dp[h] - dl[h]);
+        }
+        if (!(ok = wt(&sm.ds_empty[slot], ((g / kR) & 1) ^ 1, st, 22))) break;
+        const uint32_t off = smem_u32(&sm.ds[slot][0]) + lrow * 32;
+        const uint32_t sw = ((lrow >> 2) & 1) << 4;
+        st_shared_v4(off + sw, pack_bf16x2(ds[0], ds[1]), pack_bf16x2(ds[2], ds[3]), pack_bf16x2(ds[4], ds[5]),
+                     pack_bf16x2(ds[6], ds[7]));
+        st_shared_v4(off + (16 - sw), pack_bf16x2(ds[8], ds[9]), pack_bf16x2(ds[10], ds[11]),
+                     pack_bf16x2(ds[12], ds[13]), pack_bf16x2(ds[14], ds[15]));
+        fence_proxy_async_smem();
+        mbar_arrive(&sm.ds_full[slot]);
+      }
+      if (!ok) break;
+      // epilogue: dq = scale * dQ^T (thread = dim)
+      if (!(ok = wt(&sm.dq_full[ib], (job >> 1) & 1, st, 23))) break;
+      tc_fence_after();
+      float acc[16];
+      if (nch > 0) {
+        tmem_ld16(tl + kColDQ + ib * kNH, acc);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int h = 0; h < 16; ++h) acc[h] = 0.f;
+      }
+      tc_fence_before();
+      mbar_arrive(&sm.dq_empty[ib]);
+      if (lrow < D) {
+        __nv_bfloat16* dqp = reinterpret_cast<__nv_bfloat16*>(p.dq) + d.b * p.dq_sb + (int64_t)d.tq * p.dq_st +
+                             (int64_t)(d.hk * G) * p.dq_sh + lrow;
+#pragma unroll
+        for (int h = 0; h < 16; ++h)
+          if (h < G) dqp[h * p.dq_sh] = f2bf(acc[h] * p.scale);
+      }
+      mbar_arrive(&sm.jd_empty[js]);
+      ++job;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+template <int D>
+cudaError_t launch(const SfaParams& p, const float* delta, cudaStream_t stream) {
+  CUtensorMap tq, tdo, tk, tv;
+  const int G = p.h_q / p.h_kv;
+  const bool vl = p.cu_seqlens_q != nullptr;
+  const int64_t qrows = vl ? p.total_q : p.q_len, krows = vl ? p.total_kv : p.kv_len;
+  const int64_t nb = vl ? 1 : p.batch;
+  cudaError_t e = make_tmap_bf16_4d(&tq, p.q, {(uint64_t)D, (uint64_t)p.h_q, (uint64_t)qrows, (uint64_t)nb},
+                                    {p.q_sh, p.q_st, p.q_sb}, {64u, (uint32_t)G, 1u, 1u});
+  if (e == cudaSuccess)
+    e = make_tmap_bf16_4d(&tdo, p.dout, {(uint64_t)D, (uint64_t)p.h_q, (uint64_t)qrows, (uint64_t)nb},
+                          {p.do_sh, p.do_st, p.do_sb}, {64u, (uint32_t)G, 1u, 1u});
+  if (e == cudaSuccess)
+    e = make_tmap_bf16_4d(&tk, p.k, {(uint64_t)D, (uint64_t)p.h_kv, (uint64_t)krows, (uint64_t)nb},
+                          {p.k_sh, p.k_st, p.k_sb}, {64u, 1u, 64u, 1u});
+  if (e == cudaSuccess)
+    e = make_tmap_bf16_4d(&tv, p.v, {(uint64_t)D, (uint64_t)p.h_kv, (uint64_t)krows, (uint64_t)nb},
+                          {p.v_sh, p.v_st, p.v_sb}, {64u, 1u, 64u, 1u});
+  if (e != cudaSuccess) return e;
+  Args a;
+  a.p = p;
+  a.delta = delta;
+  a.nrows = num_rows_host(p);
+  a.nitems = a.nrows * p.h_kv;
+  a.oob_row = (int)krows;
+  a.status = device_status_ptr();
+  if (a.nitems == 0) return cudaSuccess;
+  static_assert(sizeof(Smem<D>) + 1024 <= 227 * 1024, "shared memory budget");
+  const size_t smem = sizeof(Smem<D>) + 1024;
+  e = cudaFuncSetAttribute(sfa_bwd_dq_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int grid = a.nitems < device_sm_count() ? a.nitems : device_sm_count();
+  sfa_bwd_dq_tc_kernel<D><<<grid, kThreads, smem, stream>>>(a, tq, tdo, tk, tv);
+  note_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace dq
+}  // namespace bwd
+
+bool tc_bwd_supported(const SfaParams& p, const char** why) {
+  if (!tc_fwd_supported(p, why)) return false;
+  if (!tma_compatible(p.dout, p.do_sb, p.do_st, p.do_sh)) { *why = "dout needs 16-byte alignment"; return false; }
+  return true;
+}
+
+bool tc_dkdv_available() { return false; }
+
+cudaError_t launch_bwd_dq_tc(const SfaParams& p, const float* delta, cudaStream_t st) {
+  return p.d_qk == 128 ? bwd::dq::launch<128>(p, delta, st) : bwd::dq::launch<64>(p, delta, st);
+}
+
+cudaError_t launch_bwd_dkdv_tc(const SfaParams&, const BwdLayout&, char*, const float*, cudaStream_t) {
+  return cudaErrorNotSupported;
+}
+
+}  // namespace sfa

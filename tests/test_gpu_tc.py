@@ -22,11 +22,11 @@ def _case(cfg, seed, sink=True):
     W.scaled(W.CONFIGS["c2"], B=1, T=4096, Hq=16, Hk=1, S=16),
     W.scaled(W.CONFIGS["c3"], T=2048, Hq=32, Hk=2, S=32),
 ], ids=["c1", "c2s", "c2s_long", "c3s_two_segments"])
-def test_tc_forward(cfg):
+def test_tc_forward_backward(cfg):
     d, s = _case(cfg, 5)
-    got = run_op(d["q"], d["k"], d["v"], d["idx"], cfg.bs, cfg.scale, s, True, None, kernel="tcgen05")
-    ref = run_oracle(d["q"], d["k"], d["v"], d["idx"], cfg.bs, cfg.scale, s, True)
-    check_all(got, ref, grads=False)
+    got = run_op(d["q"], d["k"], d["v"], d["idx"], cfg.bs, cfg.scale, s, True, d["do"], kernel="tcgen05")
+    ref = run_oracle(d["q"], d["k"], d["v"], d["idx"], cfg.bs, cfg.scale, s, True, d["do"], o_for_bwd=got["o"])
+    check_all(got, ref)
 
 
 def test_tc_forward_decode_varlen():
@@ -53,9 +53,10 @@ def test_tc_forward_edge_indices(G, causal):
     idx[:, 70, :, 2] = idx[:, 70, :, 1]
     idx[:, 90, :, :] = 1
     sink = torch.randn(G * Hk, generator=g)
-    got = run_op(q, k, v, idx, bs, None, sink, causal, None, kernel="tcgen05")
-    ref = run_oracle(q, k, v, idx, bs, None, sink, causal)
-    check_all(got, ref, grads=False)
+    do = torch.randn(B, T, G * Hk, D, generator=g).bfloat16()
+    got = run_op(q, k, v, idx, bs, None, sink, causal, do, kernel="tcgen05")
+    ref = run_oracle(q, k, v, idx, bs, None, sink, causal, do, o_for_bwd=got["o"])
+    check_all(got, ref)
 
 
 def test_tc_matches_general_family():
