@@ -171,11 +171,8 @@ BwdLayout bwd_layout(const SfaParams& p, int family, int dkv_mode) {
     int64_t ntiles = (ncount + 2047) / 2048;
     L.inv_cursor = off;
     off = align256(off + sizeof(int32_t) * (ncount + ntiles + 1));
-    if (family == SFA_KERNEL_TCGEN05 && p.dk == p.dv) {
-      // shared k/v: dk and dv are summed in fp32 before rounding
-      L.dk_acc = off;
-      off = align256(off + sizeof(float) * kvr * p.h_kv * p.d_qk);
-    }
+    L.sched = off;
+    off = align256(off + sizeof(int32_t));
   }
   L.total = off;
   return L;

@@ -25,7 +25,7 @@ struct BwdLayout {
   size_t inv_offsets;  // int32 [units * nblk + 1]        (inverted path)
   size_t inv_entries;  // int32 [pairs]                   (inverted path)
   size_t inv_cursor;   // int32 [units * nblk]            (inverted path scratch)
-  size_t dq_acc;       // float [rows * h_q * d_qk]        (key-centric dq path)
+  size_t sched;        // int32 work counter               (inverted path)
   size_t total;
   int pre_ctas;
   int nblk;

@@ -420,6 +420,427 @@ cudaError_t launch(const SfaParams& p, const float* delta, cudaStream_t stream) 
 }
 
 }  // namespace dq
+
+// =========================================================================
+// dK / dV (key-centric over the inverted index)
+// =========================================================================
+namespace dkdv {
+
+constexpr int kThreads = 192;
+constexpr int kQB = 8;              // queries per batch (x 16 heads = 128 MMA rows)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColSdP = 0;     // 2 slots x (64 S + 64 dP)
+constexpr uint32_t kColAcc = 256;   // 2 buffers x (64 dV^T + 64 dK^T)
+
+struct JobDesc {
+  int e, b, hk, kv0, kv_len, n, list0, flags;
+};
+
+template <int D>
+struct Smem {
+  static constexpr int kBatchBytes = 128 * D * 2;   // 128 rows x D bf16
+  static constexpr int kKVBytes = 64 * D * 2;       // 64 keys x D bf16
+  alignas(1024) uint8_t qb[2][kBatchBytes];
+  alignas(1024) uint8_t dob[2][kBatchBytes];
+  alignas(1024) uint8_t ke[kKVBytes];
+  alignas(1024) uint8_t ve[kKVBytes];
+  alignas(1024) uint8_t pbuf[128 * 64 * 2];
+  alignas(1024) uint8_t dsbuf[128 * 64 * 2];
+  JobDesc jd[kJD];
+  uint64_t b_full[2], b_empty[2], kv_full, kv_empty;
+  uint64_t sdp_full[2], sdp_empty[2], pds_full, pds_empty;
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t jd_full[kJD], jd_empty[kJD];
+  uint32_t tmem_base;
+};
+
+struct Args {
+  SfaParams p;
+  const float* delta;
+  const int32_t* offsets;   // [units * nblk + 1]
+  const int32_t* entries;   // query rows
+  int* sched;               // work counter (zeroed by the host)
+  int units, nblk, nitems;
+  int32_t* status;
+};
+
+__device__ __forceinline__ bool wt(uint64_t* bar, uint32_t parity, int32_t* status, int site) {
+  if (mbar_wait(bar, parity)) return true;
+  record_status(status, (3 << 16) | site);
+  return false;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUtensorMap tmq,
+                       const __grid_constant__ CUtensorMap tmdo, const __grid_constant__ CUtensorMap tmk,
+                       const __grid_constant__ CUtensorMap tmv) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem<D>& sm = *reinterpret_cast<Smem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const SfaParams& p = args.p;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.h_q / p.h_kv;
+  int32_t* st = args.status;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.b_full[i], 1);
+      mbar_init(&sm.b_empty[i], 1);
+      mbar_init(&sm.sdp_full[i], 1);
+      mbar_init(&sm.sdp_empty[i], 128);
+      mbar_init(&sm.acc_full[i], 1);
+      mbar_init(&sm.acc_empty[i], 128);
+    }
+    mbar_init(&sm.kv_full, 1);
+    mbar_init(&sm.kv_empty, 1);
+    mbar_init(&sm.pds_full, 128);
+    mbar_init(&sm.pds_empty, 1);
+    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 1 + 128); }
+    fence_barrier_init();
+  }
+  // padded head rows (G..15 of every query) stay zero
+  for (int i = threadIdx.x; i < 2 * Smem<D>::kBatchBytes / 16; i += kThreads) {
+    reinterpret_cast<uint4*>(&sm.qb[0][0])[i] = make_uint4(0, 0, 0, 0);
+    reinterpret_cast<uint4*>(&sm.dob[0][0])[i] = make_uint4(0, 0, 0, 0);
+  }
+  fence_proxy_async_smem();
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmq);
+    prefetch_tmap(&tmdo);
+    prefetch_tmap(&tmk);
+    prefetch_tmap(&tmv);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ============================================================ producer
+    int job = 0, gb = 0;
+    bool ok = true;
+    while (ok) {
+      int item = 0;
+      if (lane == 0) item = atomicAdd(args.sched, 1);
+      item = __shfl_sync(0xffffffffu, item, 0);
+      if (item >= args.nitems) break;
+      const int e = item / args.units, u = item - e * args.units;
+      const int seq = u / p.h_kv, hk = u - seq * p.h_kv;
+      int kv0 = 0, kv_len = p.kv_len, b = seq;
+      if (p.cu_seqlens_q != nullptr) {
+        kv0 = __ldg(p.cu_seqlens_k + seq);
+        kv_len = __ldg(p.cu_seqlens_k + seq + 1) - kv0;
+        b = 0;
+      }
+      if (e * 64 >= kv_len) continue;   // past this sequence's last block
+      const int list0 = __ldg(args.offsets + (int64_t)u * args.nblk + e);
+      const int n = __ldg(args.offsets + (int64_t)u * args.nblk + e + 1) - list0;
+      const int js = job % kJD;
+      if (lane == 0) {
+        ok = wt(&sm.jd_empty[js], ((job / kJD) & 1) ^ 1, st, 1);
+        if (ok) {
+          JobDesc& d = sm.jd[js];
+          d.e = e;
+          d.b = b;
+          d.hk = hk;
+          d.kv0 = kv0;
+          d.kv_len = kv_len;
+          d.n = n;
+          d.list0 = list0;
+          d.flags = 0;
+          mbar_arrive(&sm.jd_full[js]);
+          ok = wt(&sm.kv_empty, (job & 1) ^ 1, st, 2);
+        }
+        if (ok) {
+          mbar_arrive_expect_tx(&sm.kv_full, 2u * 64u * D * 2u);
+#pragma unroll
+          for (int cd = 0; cd < D / 64; ++cd) {
+            tma_load_4d(&sm.ke[cd * 64 * 128], &tmk, &sm.kv_full, cd * 64, hk, kv0 + e * 64, b);
+            tma_load_4d(&sm.ve[cd * 64 * 128], &tmv, &sm.kv_full, cd * 64, hk, kv0 + e * 64, b);
+          }
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      const int nb = (n + kQB - 1) / kQB;
+      for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
+        const int m = min(kQB, n - jb * kQB);
+        // lanes 0..m-1 look up their query row
+        int tq = 0, bb = 0;
+        if (lane < m) {
+          const int row = __ldg(args.entries + list0 + jb * kQB + lane);
+          const Row r = row_info(p, row);
+          tq = (int)r.tq;
+          bb = r.b;
+        }
+        const int s = gb & 1;
+        if (lane == 0) {
+          ok = wt(&sm.b_empty[s], ((gb >> 1) & 1) ^ 1, st, 3);
+          if (ok) mbar_arrive_expect_tx(&sm.b_full[s], (uint32_t)(2 * m * G * D * 2));
+        }
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        for (int j = 0; j < m; ++j) {
+          const int tqj = __shfl_sync(0xffffffffu, tq, j);
+          const int bj = __shfl_sync(0xffffffffu, bb, j);
+          if (lane == 0 && ok) {
+#pragma unroll
+            for (int cd = 0; cd < D / 64; ++cd) {
+              tma_load_4d(&sm.qb[s][cd * 128 * 128 + j * 16 * 128], &tmq, &sm.b_full[s], cd * 64, hk * G, tqj, bj);
+              tma_load_4d(&sm.dob[s][cd * 128 * 128 + j * 16 * 128], &tmdo, &sm.b_full[s], cd * 64, hk * G, tqj,
+                          bj);
+            }
+          }
+        }
+      }
+      ++job;
+    }
+    if (lane == 0 && ok) {
+      const int js = job % kJD;
+      if (wt(&sm.jd_empty[js], ((job / kJD) & 1) ^ 1, st, 4)) {
+        sm.jd[js].flags = kSentinel;
+        mbar_arrive(&sm.jd_full[js]);
+      }
+    }
+  } else if (warp == 1) {
+    // ============================================================ MMA issuer
+    if (lane == 0) {
+      const uint32_t id_sdp = idesc_bf16(128, 64, false, false);
+      const uint32_t id_acc = idesc_bf16(128, 64, true, true);
+      const uint32_t lbo_rows = D == 128 ? 128u * 128u : 0u;   // 64-dim slabs of the 128-row buffers
+      struct Pending { int gb, s, ab, job; bool first, last; };
+      Pending pend{};
+      bool has_pend = false, ok = true;
+      int job = 0, gb = 0;
+      auto issue_acc = [&](const Pending& pd) -> bool {
+        if (!wt(&sm.pds_full, pd.gb & 1, st, 10)) return false;
+        if (pd.first && !wt(&sm.acc_empty[pd.ab], ((pd.job >> 1) & 1) ^ 1, st, 11)) return false;
+        tc_fence_after();
+        const uint32_t ob = smem_u32(&sm.dob[pd.s][0]);
+        const uint32_t qb = smem_u32(&sm.qb[pd.s][0]);
+        const uint32_t pb = smem_u32(&sm.pbuf[0]);
+        const uint32_t db = smem_u32(&sm.dsbuf[0]);
+        const uint32_t acc = tmem + kColAcc + pd.ab * 128;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t accum = (pd.first && kk == 0) ? 0u : 1u;
+          mma_bf16_ss(acc, smem_desc(ob + kk * 2048, lbo_rows, 1024, kSw128), smem_desc(pb + kk * 2048, 0, 1024, kSw128),
+                      id_acc, accum);
+          mma_bf16_ss(acc + 64, smem_desc(qb + kk * 2048, lbo_rows, 1024, kSw128),
+                      smem_desc(db + kk * 2048, 0, 1024, kSw128), id_acc, accum);
+        }
+        mma_commit(&sm.b_empty[pd.s]);
+        mma_commit(&sm.pds_empty);
+        if (pd.last) {
+          mma_commit(&sm.acc_full[pd.ab]);
+          mbar_arrive(&sm.jd_empty[pd.job % kJD]);
+        }
+        return true;
+      };
+      while (ok) {
+        const int js = job % kJD;
+        if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 12))) break;
+        const JobDesc& d = sm.jd[js];
+        if (d.flags & kSentinel) break;
+        const int ab = job & 1;
+        if (!(ok = wt(&sm.kv_full, job & 1, st, 13))) break;
+        const int nb = (d.n + kQB - 1) / kQB;
+        if (nb == 0) {
+          if (has_pend) { if (!(ok = issue_acc(pend))) break; has_pend = false; }
+          if (!(ok = wt(&sm.acc_empty[ab], ((job >> 1) & 1) ^ 1, st, 14))) break;
+          mma_commit(&sm.kv_empty);
+          mma_commit(&sm.acc_full[ab]);
+          mbar_arrive(&sm.jd_empty[js]);
+          ++job;
+          continue;
+        }
+        const uint32_t kb = smem_u32(&sm.ke[0]);
+        const uint32_t vb = smem_u32(&sm.ve[0]);
+        for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
+          const int s = gb & 1;
+          if (!(ok = wt(&sm.sdp_empty[s], ((gb >> 1) & 1) ^ 1, st, 15))) break;
+          if (!(ok = wt(&sm.b_full[s], (gb >> 1) & 1, st, 16))) break;
+          tc_fence_after();
+          const uint32_t qb = smem_u32(&sm.qb[s][0]);
+          const uint32_t ob = smem_u32(&sm.dob[s][0]);
+          const uint32_t scol = tmem + kColSdP + s * 128;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t ro = (k >> 2) * (128 * 128) + (k & 3) * 32;
+            const uint32_t ko = (k >> 2) * (64 * 128) + (k & 3) * 32;
+            mma_bf16_ss(scol, smem_desc(qb + ro, 16, 1024, kSw128), smem_desc(kb + ko, 16, 1024, kSw128), id_sdp,
+                        k != 0);
+            mma_bf16_ss(scol + 64, smem_desc(ob + ro, 16, 1024, kSw128), smem_desc(vb + ko, 16, 1024, kSw128),
+                        id_sdp, k != 0);
+          }
+          mma_commit(&sm.sdp_full[s]);
+          if (jb == nb - 1) mma_commit(&sm.kv_empty);
+          if (has_pend && !(ok = issue_acc(pend))) break;
+          pend = Pending{gb, s, ab, job, jb == 0, jb == nb - 1};
+          has_pend = true;
+        }
+        ++job;
+      }
+      if (ok && has_pend) issue_acc(pend);
+    }
+  } else {
+    // ============================================================ P/dS and epilogue
+    const int wq = warp & 3;
+    const int lrow = wq * 32 + lane;        // TMEM lane: (query j, head h) row, or dim in the epilogue
+    const int jq = lrow >> 4, h = lrow & 15;
+    const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
+    const float c2 = p.scale * kLog2e;
+    const bool shared_kv = p.dk == p.dv;
+    int job = 0, gb = 0;
+    bool ok = true;
+    while (ok) {
+      const int js = job % kJD;
+      if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 20))) break;
+      const JobDesc& d = sm.jd[js];
+      if (d.flags & kSentinel) break;
+      const int ab = job & 1;
+      const int nb = (d.n + kQB - 1) / kQB;
+      for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
+        const int s = gb & 1;
+        const int m = min(kQB, d.n - jb * kQB);
+        bool rvalid = jq < m && h < G;
+        float lse2 = -INFINITY, dl = 0.f;
+        int pos = 0;
+        if (rvalid) {
+          const int row = __ldg(args.entries + d.list0 + jb * kQB + jq);
+          const Row r = row_info(p, row);
+          lse2 = p.lse[r.b * p.l_sb + r.tq * p.l_st + (int64_t)(d.hk * G + h) * p.l_sh] * kLog2e;
+          dl = args.delta[(int64_t)row * p.h_q + d.hk * G + h];
+          pos = r.pos;
+          rvalid = lse2 != -INFINITY;
+        }
+        if (!(ok = wt(&sm.sdp_full[s], (gb >> 1) & 1, st, 21))) break;
+        tc_fence_after();
+        uint32_t pk[32], dk[32];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float sv[16], dp[16];
+          tmem_ld16(tl + kColSdP + s * 128 + q4 * 16, sv);
+          tmem_ld16(tl + kColSdP + s * 128 + 64 + q4 * 16, dp);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const int key0 = d.e * 64 + q4 * 16 + i;
+            const bool v0 = rvalid && key0 < d.kv_len && (!p.causal || key0 <= pos);
+            const bool v1 = rvalid && key0 + 1 < d.kv_len && (!p.causal || key0 + 1 <= pos);
+            const float p0 = v0 ? exp2f(sv[i] * c2 - lse2) : 0.f;
+            const float p1 = v1 ? exp2f(sv[i + 1] * c2 - lse2) : 0.f;
+            pk[q4 * 8 + i / 2] = pack_bf16x2(p0, p1);
+            dk[q4 * 8 + i / 2] = pack_bf16x2(p0 * (dp[i] - dl), p1 * (dp[i + 1] - dl));
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&sm.sdp_empty[s]);
+        if (!(ok = wt(&sm.pds_empty, (gb & 1) ^ 1, st, 22))) break;
+        // row lrow: 64 keys = 8 chunks of 16 bytes, 128B swizzle (chunk ^= row & 7)
+        const uint32_t prow = smem_u32(&sm.pbuf[0]) + lrow * 128;
+        const uint32_t drow = smem_u32(&sm.dsbuf[0]) + lrow * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t off = (uint32_t)((c ^ (lrow & 7)) * 16);
+          st_shared_v4(prow + off, pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
+          st_shared_v4(drow + off, dk[c * 4], dk[c * 4 + 1], dk[c * 4 + 2], dk[c * 4 + 3]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&sm.pds_full);
+      }
+      if (!ok) break;
+      // epilogue: thread = dim; 64 keys of dV^T and dK^T
+      if (!(ok = wt(&sm.acc_full[ab], (job >> 1) & 1, st, 23))) break;
+      tc_fence_after();
+      const bool has = nb > 0;
+      __nv_bfloat16* dkp = reinterpret_cast<__nv_bfloat16*>(p.dk) + d.b * p.dk_sb + (int64_t)d.hk * p.dk_sh + lrow;
+      __nv_bfloat16* dvp = reinterpret_cast<__nv_bfloat16*>(p.dv) + d.b * p.dv_sb + (int64_t)d.hk * p.dv_sh + lrow;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float vv[16], kv[16];
+        if (has) {
+          tmem_ld16(tl + kColAcc + ab * 128 + q4 * 16, vv);
+          tmem_ld16(tl + kColAcc + ab * 128 + 64 + q4 * 16, kv);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) { vv[i] = 0.f; kv[i] = 0.f; }
+        }
+        if (lrow < D) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int key = d.e * 64 + q4 * 16 + i;
+            if (key < d.kv_len) {
+              const int64_t t = (int64_t)d.kv0 + key;
+              if (shared_kv) {
+                dkp[t * p.dk_st] = f2bf(kv[i] * p.scale + vv[i]);
+              } else {
+                dkp[t * p.dk_st] = f2bf(kv[i] * p.scale);
+                dvp[t * p.dv_st] = f2bf(vv[i]);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sm.acc_empty[ab]);
+      mbar_arrive(&sm.jd_empty[js]);
+      ++job;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+template <int D>
+cudaError_t launch(const SfaParams& p, const BwdLayout& L, char* ws, const float* delta, cudaStream_t stream) {
+  CUtensorMap tq, tdo, tk, tv;
+  const int G = p.h_q / p.h_kv;
+  const bool vl = p.cu_seqlens_q != nullptr;
+  const int64_t qrows = vl ? p.total_q : p.q_len, krows = vl ? p.total_kv : p.kv_len;
+  const int64_t nb = vl ? 1 : p.batch;
+  cudaError_t e = make_tmap_bf16_4d(&tq, p.q, {(uint64_t)D, (uint64_t)p.h_q, (uint64_t)qrows, (uint64_t)nb},
+                                    {p.q_sh, p.q_st, p.q_sb}, {64u, (uint32_t)G, 1u, 1u});
+  if (e == cudaSuccess)
+    e = make_tmap_bf16_4d(&tdo, p.dout, {(uint64_t)D, (uint64_t)p.h_q, (uint64_t)qrows, (uint64_t)nb},
+                          {p.do_sh, p.do_st, p.do_sb}, {64u, (uint32_t)G, 1u, 1u});
+  if (e == cudaSuccess)
+    e = make_tmap_bf16_4d(&tk, p.k, {(uint64_t)D, (uint64_t)p.h_kv, (uint64_t)krows, (uint64_t)nb},
+                          {p.k_sh, p.k_st, p.k_sb}, {64u, 1u, 64u, 1u});
+  if (e == cudaSuccess)
+    e = make_tmap_bf16_4d(&tv, p.v, {(uint64_t)D, (uint64_t)p.h_kv, (uint64_t)krows, (uint64_t)nb},
+                          {p.v_sh, p.v_st, p.v_sb}, {64u, 1u, 64u, 1u});
+  if (e != cudaSuccess) return e;
+  Args a;
+  a.p = p;
+  a.delta = delta;
+  a.offsets = reinterpret_cast<const int32_t*>(ws + L.inv_offsets);
+  a.entries = reinterpret_cast<const int32_t*>(ws + L.inv_entries);
+  a.sched = reinterpret_cast<int*>(ws + L.sched);
+  a.units = L.units;
+  a.nblk = L.nblk;
+  a.nitems = L.units * L.nblk;
+  a.status = device_status_ptr();
+  if (a.nitems == 0) return cudaSuccess;
+  e = cudaMemsetAsync(a.sched, 0, sizeof(int), stream);
+  if (e != cudaSuccess) return e;
+  static_assert(sizeof(Smem<D>) + 1024 <= 227 * 1024, "shared memory budget");
+  const size_t smem = sizeof(Smem<D>) + 1024;
+  e = cudaFuncSetAttribute(sfa_bwd_dkdv_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int grid = a.nitems < device_sm_count() ? a.nitems : device_sm_count();
+  sfa_bwd_dkdv_tc_kernel<D><<<grid, kThreads, smem, stream>>>(a, tq, tdo, tk, tv);
+  note_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace dkdv
 }  // namespace bwd
 
 bool tc_bwd_supported(const SfaParams& p, const char** why) {
@@ -428,14 +849,15 @@ bool tc_bwd_supported(const SfaParams& p, const char** why) {
   return true;
 }
 
-bool tc_dkdv_available() { return false; }
+bool tc_dkdv_available() { return true; }
 
 cudaError_t launch_bwd_dq_tc(const SfaParams& p, const float* delta, cudaStream_t st) {
   return p.d_qk == 128 ? bwd::dq::launch<128>(p, delta, st) : bwd::dq::launch<64>(p, delta, st);
 }
 
-cudaError_t launch_bwd_dkdv_tc(const SfaParams&, const BwdLayout&, char*, const float*, cudaStream_t) {
-  return cudaErrorNotSupported;
+cudaError_t launch_bwd_dkdv_tc(const SfaParams& p, const BwdLayout& L, char* ws, const float* delta,
+                               cudaStream_t st) {
+  return p.d_qk == 128 ? bwd::dkdv::launch<128>(p, L, ws, delta, st) : bwd::dkdv::launch<64>(p, L, ws, delta, st);
 }
 
 }  // namespace sfa
