@@ -2,10 +2,14 @@
 the same seeded inputs and compare with the tolerances the op promises.
 
 Tolerances (bf16 outputs against the fp32 oracle): o, dq, dk, dv max-abs 2e-2
-and rel-L2 5e-3; lse max-abs 1e-3.  Max-abs is taken on values normalised by
-max(1, |oracle|): a bf16 result carries a rounding error of up to 2^-9 of its
-own magnitude, which exceeds 2e-2 for gradient entries above 10 (dk/dv sum
-over every query that selected a key)."""
+and rel-L2 5e-3; lse max-abs 1e-3.  Max-abs is taken on errors normalised by
+max(1, RMS of the oracle's row): a dk/dv row sums the contributions of every
+query that selected the key, and the bf16 rounding of the MMA operands P and
+dS (the reference rounds them the same way, SFA.py:700, 807-808) leaves an
+error proportional to that row's magnitude — up to 2^-9 of it — on every
+element of the row, including elements whose own value is small.  Measured on
+the CPU: bf16 P alone gives 1.6e-2 element-normalised max-abs on a T=4096
+dv.  For o and dq rows (RMS below 1) the bound is the plain absolute 2e-2."""
 import math
 
 import torch
@@ -24,7 +28,10 @@ def rel_l2(a, b):
 
 def max_abs_norm(a, b):
     a, b = a.double(), b.double()
-    return float(((a - b).abs() / b.abs().clamp_min(1.0)).max()) if a.numel() else 0.0
+    if not a.numel():
+        return 0.0
+    scale = b.pow(2).mean(-1, keepdim=True).sqrt().clamp_min(1.0) if b.dim() else b.abs().clamp_min(1.0)
+    return float(((a - b).abs() / scale).max())
 
 
 def assert_close(name, got, ref, maxabs=TOL_MAXABS, rl2=TOL_REL_L2):
