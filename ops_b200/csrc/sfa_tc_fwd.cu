@@ -6,20 +6,30 @@
 //     S^T[keys, heads]  = K_sel[keys, D] . Q^T[D, heads]        (M = 128 keys, N = 16)
 //     O^T[D, heads]    += V_sel^T[D, keys] . P^T[keys, heads]   (M = 128 dims, N = 16)
 // with both accumulators in TMEM.  A segment of up to 1024 selected keys is
-// scored completely before its softmax (so the max/sum need one cross-thread
-// reduction per segment instead of per tile); segments of one row are merged in
-// registers with the usual log-sum-exp rescale.
+// scored completely before its softmax, so the max and the sum need one
+// cross-thread reduction per segment; segments of one row merge in registers
+// with the usual log-sum-exp rescale.
 //
-// Warp roles (192 threads, one persistent CTA per SM):
-//   warp 0      TMA producer: compacts the row's valid block ids, loads Q and
-//               gathers 64-key K/V blocks (one 4-D box per block and 64-dim
-//               slab, 128B swizzle) into a ring of 128-key stages;
-//   warp 1      MMA issuer (one thread): S^T for job j, then PV for job j-1;
-//   warps 2-5   softmax (thread = key lane of a 128-key tile) and epilogue
-//               (thread = dim lane of O^T): writes o (bf16) and lse (fp32).
-// Hand-offs: mbarriers (TMA complete_tx, tcgen05.commit, thread arrivals).
-// Every wait is bounded (~2 s); on expiry the kernel records a status word
-// and returns.
+// Cost model (measured on B200): an M=128, K=16 tcgen05 MMA with N = 16 takes
+// 45 cycles — its A operand (4 KB) is read from shared memory — so with G = 16
+// the forward is bounded by shared-memory bandwidth (TMA writes of the gathered
+// K/V plus MMA operand reads), not by the tensor pipe.  The kernel is organised
+// to keep that port busy: K and V stream through separate rings fed by separate
+// producer warps, and the softmax runs on two warpgroups with S held in
+// registers (one TMEM read per score).
+//
+// Warp roles (352 threads, one persistent CTA per SM):
+//   warp 0      K producer: compacts the row's valid block ids into a job
+//               descriptor, loads Q, gathers 64-key K blocks (4-D TMA box per
+//               block and 64-dim slab, 128B swizzle) into 128-key stages;
+//   warp 10     V producer: the same gathers for V, one job behind;
+//   warp 1      MMA issuer (one thread): S^T for job j+1, then PV for job j;
+//   warps 2-9   two softmax warpgroups (thread = key lane of a 128-key tile,
+//               warpgroup w takes tiles 4w..4w+3) and the epilogue
+//               (thread = dim lane of O^T, warpgroup w takes heads 8w..8w+7):
+//               writes o (bf16) and lse (fp32, natural log).
+// Every wait is bounded (~2 s); on expiry the kernel records a status word and
+// returns.
 //
 // Replaces `_attn_fwd` / `_inner_fwd` (SFA.py:309-587): same math, no
 // per-program global-memory workspaces, one gather per selected block per
@@ -34,8 +44,9 @@ using namespace tc;
 
 namespace fwd {
 
-constexpr int kThreads = 192;
-constexpr int kSegBlocks = 16;      // 64-key blocks per segment (1024 keys)
+constexpr int kThreads = 352;
+constexpr int kSoftmaxThreads = 256;
+constexpr int kSegBlocks = 16;      // 64-key blocks per segment (1024 keys, 8 tiles)
 constexpr int kJD = 4;              // job descriptor ring depth
 constexpr int kNH = 16;             // MMA N: query heads padded to 16
 constexpr int kMaxTopk = 64;
@@ -52,23 +63,25 @@ struct JobDesc {
 
 template <int D>
 struct Smem {
-  static constexpr int kStages = D == 128 ? 4 : 8;
-  static constexpr int kStageBytes = 128 * D * 2;   // 128 keys x D bf16
+  static constexpr int kKS = D == 128 ? 3 : 6;      // K ring stages (128 keys each)
+  static constexpr int kVS = D == 128 ? 2 : 4;      // V ring stages
+  static constexpr int kStageBytes = 128 * D * 2;
   static constexpr int kQBytes = kNH * D * 2;
   static constexpr int kPBytes = kSegBlocks * 64 * kNH * 2;
-  alignas(1024) uint8_t stage[kStages][kStageBytes];
+  alignas(1024) uint8_t kst[kKS][kStageBytes];
+  alignas(1024) uint8_t vst[kVS][kStageBytes];
   alignas(1024) uint8_t q[2][kQBytes];
-  alignas(1024) uint8_t p[2][kPBytes];
+  alignas(1024) uint8_t p[kPBytes];
   JobDesc jd[kJD];
-  float red[4][16];
-  float ml[2][2][16];
+  alignas(16) float red[8][16];
+  alignas(16) float redl[8][16];
+  alignas(16) float ml[2][2][16];
   int plist[kMaxTopk];
-  uint64_t stage_full[kStages], stage_empty[kStages];
+  uint64_t k_full[kKS], k_empty[kKS], v_full[kVS], v_empty[kVS];
   uint64_t q_full[2], q_empty[2];
-  uint64_t s_full[2], s_empty[2], p_full[2], p_empty[2], o_full[2], o_empty[2];
+  uint64_t s_full[2], s_empty[2], p_full, p_empty, o_full[2], o_empty[2];
   uint64_t jd_full[kJD], jd_empty[kJD];
   uint32_t tmem_base;
-  int abort_flag;
 };
 
 struct Args {
@@ -79,41 +92,62 @@ struct Args {
   int32_t* status;
 };
 
-template <int D>
-__device__ __forceinline__ bool wait_or_abort(Smem<D>& sm, uint64_t* bar, uint32_t parity, int32_t* status,
-                                              int site) {
+__device__ __forceinline__ bool wt(uint64_t* bar, uint32_t parity, int32_t* status, int site) {
   if (mbar_wait(bar, parity)) return true;
   record_status(status, (1 << 16) | site);
-  atomicExch(&sm.abort_flag, 1);
   return false;
 }
 
-// Reduce 16 per-thread values over the 128 threads of warps 2-5; result for
-// head h is written to out[h] (shared) and returned in v.
-template <bool kMax, int D>
-__device__ __forceinline__ void wg_reduce16(Smem<D>& sm, float (&v)[16], float* out, int wq, int lane, int tid) {
+// Sum (kMax = false) or max of v[h] over the 32 lanes of a warp, 16 heads at
+// once with 16 shuffles: halve the head set at each butterfly step.  The result
+// for head (lane >> 1) & 15 is returned (lanes 2h and 2h+1 hold head h).
+template <bool kMax>
+__device__ __forceinline__ float warp_reduce16(const float (&v)[16], int lane) {
+  auto op = [](float a, float b) { return kMax ? fmaxf(a, b) : a + b; };
+  float a[8], b[4], c[2];
+  const bool h4 = lane & 16, h3 = lane & 8, h2 = lane & 4, h1 = lane & 2;
 #pragma unroll
-  for (int h = 0; h < 16; ++h) {
-    float x = v[h];
+  for (int i = 0; i < 8; ++i) {
+    const float send = h4 ? v[i] : v[i + 8], keep = h4 ? v[i + 8] : v[i];
+    a[i] = op(keep, __shfl_xor_sync(0xffffffffu, send, 16));
+  }
 #pragma unroll
-    for (int off = 16; off; off >>= 1) {
-      float y = __shfl_xor_sync(0xffffffffu, x, off);
-      x = kMax ? fmaxf(x, y) : x + y;
+  for (int i = 0; i < 4; ++i) {
+    const float send = h3 ? a[i] : a[i + 4], keep = h3 ? a[i + 4] : a[i];
+    b[i] = op(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = h2 ? b[i] : b[i + 2], keep = h2 ? b[i + 2] : b[i];
+    c[i] = op(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+  }
+  float d = op(h1 ? c[1] : c[0], __shfl_xor_sync(0xffffffffu, h1 ? c[0] : c[1], 2));
+  return op(d, __shfl_xor_sync(0xffffffffu, d, 1));
+}
+
+// Reduce over the 256 softmax threads; every thread gets all 16 results.
+template <bool kMax>
+__device__ __forceinline__ void block_reduce16(float (&v)[16], float (*buf)[16], int w8, int lane) {
+  const float r = warp_reduce16<kMax>(v, lane);
+  if ((lane & 1) == 0) buf[w8][(lane >> 1) & 15] = r;
+  named_barrier(1, kSoftmaxThreads);
+#pragma unroll
+  for (int h4 = 0; h4 < 4; ++h4) {
+    float4 acc = reinterpret_cast<const float4*>(buf[0])[h4];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) {
+      const float4 x = reinterpret_cast<const float4*>(buf[w])[h4];
+      if (kMax) {
+        acc.x = fmaxf(acc.x, x.x); acc.y = fmaxf(acc.y, x.y); acc.z = fmaxf(acc.z, x.z); acc.w = fmaxf(acc.w, x.w);
+      } else {
+        acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+      }
     }
-    v[h] = x;
+    v[4 * h4 + 0] = acc.x;
+    v[4 * h4 + 1] = acc.y;
+    v[4 * h4 + 2] = acc.z;
+    v[4 * h4 + 3] = acc.w;
   }
-  if (lane == 0) {
-#pragma unroll
-    for (int h = 0; h < 16; ++h) sm.red[wq][h] = v[h];
-  }
-  named_barrier(1, 128);
-  if (tid < 16) {
-    float a = sm.red[0][tid], b = sm.red[1][tid], c = sm.red[2][tid], d = sm.red[3][tid];
-    out[tid] = kMax ? fmaxf(fmaxf(a, b), fmaxf(c, d)) : (a + b) + (c + d);
-  }
-  named_barrier(1, 128);
-#pragma unroll
-  for (int h = 0; h < 16; ++h) v[h] = out[h];
 }
 
 template <int D>
@@ -122,26 +156,29 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
                   const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv) {
   extern __shared__ uint8_t smem_raw[];
   Smem<D>& sm = *reinterpret_cast<Smem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int S = Smem<D>::kStages;
+  constexpr int KS = Smem<D>::kKS, VS = Smem<D>::kVS;
   const SfaParams& p = args.p;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.h_q / p.h_kv;
+  int32_t* st = args.status;
+  const uint32_t chunk_bytes = 128u * D * 2u;
 
   // ---------------------------------------------------------------- setup
   if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) { mbar_init(&sm.stage_full[i], 1); mbar_init(&sm.stage_empty[i], 1); }
+    for (int i = 0; i < KS; ++i) { mbar_init(&sm.k_full[i], 1); mbar_init(&sm.k_empty[i], 1); }
+    for (int i = 0; i < VS; ++i) { mbar_init(&sm.v_full[i], 1); mbar_init(&sm.v_empty[i], 1); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.q_full[i], 1);
       mbar_init(&sm.q_empty[i], 1);
       mbar_init(&sm.s_full[i], 1);
-      mbar_init(&sm.s_empty[i], 128);
-      mbar_init(&sm.p_full[i], 128);
-      mbar_init(&sm.p_empty[i], 1);
+      mbar_init(&sm.s_empty[i], kSoftmaxThreads);
       mbar_init(&sm.o_full[i], 1);
-      mbar_init(&sm.o_empty[i], 128);
+      mbar_init(&sm.o_empty[i], kSoftmaxThreads);
     }
-    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 1 + 128); }
-    sm.abort_flag = 0;
+    mbar_init(&sm.p_full, kSoftmaxThreads);
+    mbar_init(&sm.p_empty, 1);
+    // consumers of a job descriptor: MMA thread, V producer, softmax threads
+    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 2 + kSoftmaxThreads); }
     fence_barrier_init();
   }
   // padded query rows (G..15) stay zero for the whole kernel
@@ -162,26 +199,21 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
+  auto load_tile = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* full, const JobDesc& d, int c) {
+    mbar_arrive_expect_tx(full, chunk_bytes);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int bi = 2 * c + half;
+      const int row = bi < d.nblk ? d.kv0 + d.blocks[bi] * 64 : args.oob_row;
+#pragma unroll
+      for (int cd = 0; cd < D / 64; ++cd)
+        tma_load_4d(dst + cd * 128 * 128 + half * 64 * 128, map, full, cd * 64, d.hk, row, d.b);
+    }
+  };
+
   if (warp == 0) {
-    // ============================================================ producer
+    // ============================================================ K producer
     int job = 0, item_i = 0, use = 0;
-    const uint32_t chunk_bytes = 128u * D * 2u;
-    auto load_chunk = [&](const CUtensorMap* map, const JobDesc& d, int c) -> bool {
-      const int s = use % S;
-      if (!wait_or_abort(sm, &sm.stage_empty[s], ((use / S) & 1) ^ 1, args.status, 1)) return false;
-      mbar_arrive_expect_tx(&sm.stage_full[s], chunk_bytes);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int bi = 2 * c + half;
-        const int row = bi < d.nblk ? d.kv0 + d.blocks[bi] * 64 : args.oob_row;
-#pragma unroll
-        for (int cd = 0; cd < D / 64; ++cd)
-          tma_load_4d(&sm.stage[s][cd * 128 * 128 + half * 64 * 128], map, &sm.stage_full[s], cd * 64, d.hk, row,
-                      d.b);
-      }
-      ++use;
-      return true;
-    };
     bool ok = true;
     for (int item = blockIdx.x; item < args.nitems && ok; item += gridDim.x, ++item_i) {
       const int hk = item / args.nrows, row = item - hk * args.nrows;
@@ -204,7 +236,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       const int nseg = n == 0 ? 1 : (n + kSegBlocks - 1) / kSegBlocks;
       if (lane == 0) {
         const int qs = item_i & 1;
-        ok = wait_or_abort(sm, &sm.q_empty[qs], ((item_i >> 1) & 1) ^ 1, args.status, 2);
+        ok = wt(&sm.q_empty[qs], ((item_i >> 1) & 1) ^ 1, st, 2);
         if (ok) {
           mbar_arrive_expect_tx(&sm.q_full[qs], (uint32_t)(G * D * 2));
 #pragma unroll
@@ -213,8 +245,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
         }
         for (int seg = 0; seg < nseg && ok; ++seg, ++job) {
           const int js = job % kJD;
-          ok = wait_or_abort(sm, &sm.jd_empty[js], ((job / kJD) & 1) ^ 1, args.status, 3);
-          if (!ok) break;
+          if (!(ok = wt(&sm.jd_empty[js], ((job / kJD) & 1) ^ 1, st, 3))) break;
           JobDesc& d = sm.jd[js];
           const int nb = n == 0 ? 0 : min(kSegBlocks, n - seg * kSegBlocks);
           d.row = row;
@@ -228,10 +259,10 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
           d.flags = (seg == 0 ? kFirst : 0) | (seg == nseg - 1 ? kLast : 0);
           for (int i = 0; i < nb; ++i) d.blocks[i] = sm.plist[seg * kSegBlocks + i];
           mbar_arrive(&sm.jd_full[js]);
-          for (int c = 0; c < (nb + 1) / 2 && ok; ++c) ok = load_chunk(&tmk, d, c);
-          if (job > 0 && ok) {
-            const JobDesc& pd = sm.jd[(job - 1) % kJD];
-            for (int c = 0; c < (pd.nblk + 1) / 2 && ok; ++c) ok = load_chunk(&tmv, pd, c);
+          for (int c = 0; c < (nb + 1) / 2 && ok; ++c, ++use) {
+            const int s = use % KS;
+            if (!(ok = wt(&sm.k_empty[s], ((use / KS) & 1) ^ 1, st, 1))) break;
+            load_tile(&tmk, sm.kst[s], &sm.k_full[s], d, c);
           }
         }
       }
@@ -240,13 +271,28 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
     }
     if (lane == 0 && ok) {
       const int js = job % kJD;
-      if (wait_or_abort(sm, &sm.jd_empty[js], ((job / kJD) & 1) ^ 1, args.status, 4)) {
+      if (wt(&sm.jd_empty[js], ((job / kJD) & 1) ^ 1, st, 4)) {
         sm.jd[js].flags = kSentinel;
         mbar_arrive(&sm.jd_full[js]);
-        if (job > 0) {
-          const JobDesc& pd = sm.jd[(job - 1) % kJD];
-          for (int c = 0; c < (pd.nblk + 1) / 2 && ok; ++c) ok = load_chunk(&tmv, pd, c);
+      }
+    }
+  } else if (warp == 10) {
+    // ============================================================ V producer
+    if (lane == 0) {
+      int job = 0, use = 0;
+      bool ok = true;
+      while (ok) {
+        const int js = job % kJD;
+        if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 5))) break;
+        const JobDesc& d = sm.jd[js];
+        if (d.flags & kSentinel) break;
+        for (int c = 0; c < (d.nblk + 1) / 2 && ok; ++c, ++use) {
+          const int s = use % VS;
+          if (!(ok = wt(&sm.v_empty[s], ((use / VS) & 1) ^ 1, st, 6))) break;
+          load_tile(&tmv, sm.vst[s], &sm.v_full[s], d, c);
         }
+        mbar_arrive(&sm.jd_empty[js]);
+        ++job;
       }
     }
   } else if (warp == 1) {
@@ -257,54 +303,53 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       // A = V tile as MN-major: 64-dim slabs LBO apart (D = 64 repeats the slab;
       // rows 64-127 of O^T are then ignored), 8-key groups 1024 B apart.
       const uint32_t lbo_v = D == 128 ? 128u * 128u : 0u;
-      int job = 0, item_i = 0, use = 0;
+      int job = 0, item_i = 0, kuse = 0, vuse = 0;
       bool ok = true;
       auto pv = [&](int jj) -> bool {
         const JobDesc& d = sm.jd[jj % kJD];
         const int sb = jj & 1;
-        if (!wait_or_abort(sm, &sm.p_full[sb], (jj >> 1) & 1, args.status, 10)) return false;
-        if (!wait_or_abort(sm, &sm.o_empty[sb], ((jj >> 1) & 1) ^ 1, args.status, 11)) return false;
+        if (!wt(&sm.p_full, jj & 1, st, 10)) return false;
+        if (!wt(&sm.o_empty[sb], ((jj >> 1) & 1) ^ 1, st, 11)) return false;
         tc_fence_after();
         const uint32_t dcol = tmem + kColO + sb * kNH;
-        const uint32_t pbase = smem_u32(&sm.p[sb][0]);
+        const uint32_t pbase = smem_u32(&sm.p[0]);
         const int nch = (d.nblk + 1) / 2;
-        for (int c = 0; c < nch; ++c) {
-          const int s = use % S;
-          if (!wait_or_abort(sm, &sm.stage_full[s], (use / S) & 1, args.status, 12)) return false;
+        for (int c = 0; c < nch; ++c, ++vuse) {
+          const int s = vuse % VS;
+          if (!wt(&sm.v_full[s], (vuse / VS) & 1, st, 12)) return false;
           tc_fence_after();
-          const uint32_t vbase = smem_u32(&sm.stage[s][0]);
+          const uint32_t vbase = smem_u32(&sm.vst[s][0]);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint64_t a = smem_desc(vbase + kk * 2048, lbo_v, 1024, kSw128);
             const uint64_t b = smem_desc(pbase + (c * 128 + kk * 16) * (kNH * 2), 0, 256, kSw32);
             mma_bf16_ss(dcol, a, b, id_o, (c | kk) != 0);
           }
-          mma_commit(&sm.stage_empty[s]);
-          ++use;
+          mma_commit(&sm.v_empty[s]);
         }
-        mma_commit(&sm.p_empty[sb]);
+        mma_commit(&sm.p_empty);
         mma_commit(&sm.o_full[sb]);
         mbar_arrive(&sm.jd_empty[jj % kJD]);
         return true;
       };
       while (ok) {
         const int js = job % kJD;
-        if (!(ok = wait_or_abort(sm, &sm.jd_full[js], (job / kJD) & 1, args.status, 13))) break;
+        if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 13))) break;
         const JobDesc& d = sm.jd[js];
         if (d.flags & kSentinel) break;
         const int qs = item_i & 1;
         if (d.flags & kFirst)
-          if (!(ok = wait_or_abort(sm, &sm.q_full[qs], (item_i >> 1) & 1, args.status, 14))) break;
+          if (!(ok = wt(&sm.q_full[qs], (item_i >> 1) & 1, st, 14))) break;
         const int sb = job & 1;
-        if (!(ok = wait_or_abort(sm, &sm.s_empty[sb], ((job >> 1) & 1) ^ 1, args.status, 15))) break;
+        if (!(ok = wt(&sm.s_empty[sb], ((job >> 1) & 1) ^ 1, st, 15))) break;
         tc_fence_after();
         const uint32_t qbase = smem_u32(&sm.q[qs][0]);
         const int nch = (d.nblk + 1) / 2;
-        for (int c = 0; c < nch && ok; ++c) {
-          const int s = use % S;
-          if (!(ok = wait_or_abort(sm, &sm.stage_full[s], (use / S) & 1, args.status, 16))) break;
+        for (int c = 0; c < nch && ok; ++c, ++kuse) {
+          const int s = kuse % KS;
+          if (!(ok = wt(&sm.k_full[s], (kuse / KS) & 1, st, 16))) break;
           tc_fence_after();
-          const uint32_t kbase = smem_u32(&sm.stage[s][0]);
+          const uint32_t kbase = smem_u32(&sm.kst[s][0]);
           const uint32_t dcol = tmem + kColS + sb * 128 + c * kNH;
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
@@ -312,8 +357,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
             const uint64_t b = smem_desc(qbase + (k >> 2) * (kNH * 128) + (k & 3) * 32, 16, 1024, kSw128);
             mma_bf16_ss(dcol, a, b, id_s, k != 0);
           }
-          mma_commit(&sm.stage_empty[s]);
-          ++use;
+          mma_commit(&sm.k_empty[s]);
         }
         if (!ok) break;
         mma_commit(&sm.s_full[sb]);
@@ -328,72 +372,90 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
     }
   } else {
     // ============================================================ softmax / epilogue
+    const int w8 = warp - 2;             // 0..7
+    const int wg = w8 >> 2;              // warpgroup 0 / 1
     const int wq = warp & 3;             // TMEM lane quadrant of this warp
-    const int tid = threadIdx.x - 64;    // 0..127
+    const int tid = threadIdx.x - 64;    // 0..255
     const int lrow = wq * 32 + lane;     // TMEM lane: key (softmax) or dim (epilogue)
     const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
     const float c2 = p.scale * kLog2e;
-    float acc[16], mrun[16], lrun[16];
+    float acc[8], mrun[8], lrun[8];      // epilogue state for heads 8*wg .. 8*wg+7
 #pragma unroll
-    for (int h = 0; h < 16; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
+    for (int h = 0; h < 8; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
     bool ok = true;
-    auto key_valid = [&](const JobDesc& d, int c) -> bool {
-      const int bi = 2 * c + (lrow >> 6);
-      if (bi >= d.nblk) return false;
-      const int key = d.blocks[bi] * 64 + (lrow & 63);
-      return key < d.kv_len && (!p.causal || key <= d.pos);
-    };
     auto softmax = [&](int j) -> bool {
       const JobDesc& d = sm.jd[j % kJD];
       const int sb = j & 1;
-      if (!wait_or_abort(sm, &sm.s_full[sb], (j >> 1) & 1, args.status, 20)) return false;
+      if (!wt(&sm.s_full[sb], (j >> 1) & 1, st, 20)) return false;
       tc_fence_after();
       const int nch = (d.nblk + 1) / 2;
       const uint32_t ts = tl + kColS + sb * 128;
+      float s[4][16];
+      bool valid[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = wg * 4 + i;
+        if (c < nch) tmem_ld16(ts + c * kNH, s[i]);
+      }
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&sm.s_empty[sb]);
       float m[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) m[h] = -INFINITY;
-      for (int c = 0; c < nch; ++c) {
-        float s[16];
-        tmem_ld16(ts + c * kNH, s);
-        tmem_ld_wait();
-        if (key_valid(d, c)) {
 #pragma unroll
-          for (int h = 0; h < 16; ++h) m[h] = fmaxf(m[h], s[h] * c2);
+      for (int i = 0; i < 4; ++i) {
+        const int c = wg * 4 + i;
+        const int bi = 2 * c + (lrow >> 6);
+        bool v = c < nch && bi < d.nblk;
+        if (v) {
+          const int key = d.blocks[bi] * 64 + (lrow & 63);
+          v = key < d.kv_len && (!p.causal || key <= d.pos);
+        }
+        valid[i] = v;
+        if (v) {
+#pragma unroll
+          for (int h = 0; h < 16; ++h) {
+            s[i][h] *= c2;
+            m[h] = fmaxf(m[h], s[i][h]);
+          }
         }
       }
-      wg_reduce16<true>(sm, m, sm.ml[sb][0], wq, lane, tid);
-      if (!wait_or_abort(sm, &sm.p_empty[sb], ((j >> 1) & 1) ^ 1, args.status, 21)) return false;
+      block_reduce16<true>(m, sm.red, w8, lane);
       float l[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) l[h] = 0.f;
-      const uint32_t pbase = smem_u32(&sm.p[sb][0]);
-      for (int c = 0; c < nch; ++c) {
-        float s[16];
-        tmem_ld16(ts + c * kNH, s);
-        tmem_ld_wait();
-        const bool v = key_valid(d, c);
-        float pr[16];
+      if (!wt(&sm.p_empty, (j & 1) ^ 1, st, 21)) return false;
+      const uint32_t pbase = smem_u32(&sm.p[0]);
 #pragma unroll
-        for (int h = 0; h < 16; ++h) {
-          pr[h] = v ? exp2f(s[h] * c2 - m[h]) : 0.f;
-          l[h] += pr[h];
+      for (int i = 0; i < 4; ++i) {
+        const int c = wg * 4 + i;
+        if (c < nch) {
+          float pr[16];
+#pragma unroll
+          for (int h = 0; h < 16; ++h) {
+            pr[h] = valid[i] ? exp2f(s[i][h] - m[h]) : 0.f;
+            l[h] += pr[h];
+          }
+          // row = key within the segment; 32-byte rows, 32B swizzle (16-byte
+          // halves swap when bit 2 of the row is set)
+          const int rowk = c * 128 + lrow;
+          const uint32_t off = pbase + rowk * 32;
+          const uint32_t sw = ((rowk >> 2) & 1) << 4;
+          st_shared_v4(off + sw, pack_bf16x2(pr[0], pr[1]), pack_bf16x2(pr[2], pr[3]), pack_bf16x2(pr[4], pr[5]),
+                       pack_bf16x2(pr[6], pr[7]));
+          st_shared_v4(off + (16 - sw), pack_bf16x2(pr[8], pr[9]), pack_bf16x2(pr[10], pr[11]),
+                       pack_bf16x2(pr[12], pr[13]), pack_bf16x2(pr[14], pr[15]));
         }
-        // row = key within the segment; 32-byte rows, 32B swizzle (16-byte halves
-        // swap when bit 2 of the row is set)
-        const int rowk = c * 128 + lrow;
-        const uint32_t off = pbase + rowk * 32;
-        const uint32_t sw = ((rowk >> 2) & 1) << 4;
-        st_shared_v4(off + sw, pack_bf16x2(pr[0], pr[1]), pack_bf16x2(pr[2], pr[3]), pack_bf16x2(pr[4], pr[5]),
-                     pack_bf16x2(pr[6], pr[7]));
-        st_shared_v4(off + (16 - sw), pack_bf16x2(pr[8], pr[9]), pack_bf16x2(pr[10], pr[11]),
-                     pack_bf16x2(pr[12], pr[13]), pack_bf16x2(pr[14], pr[15]));
       }
-      tc_fence_before();
-      mbar_arrive(&sm.s_empty[sb]);
       fence_proxy_async_smem();
-      mbar_arrive(&sm.p_full[sb]);
-      wg_reduce16<false>(sm, l, sm.ml[sb][1], wq, lane, tid);
+      mbar_arrive(&sm.p_full);
+      block_reduce16<false>(l, sm.redl, w8, lane);
+      if (tid < 16) {
+#pragma unroll
+        for (int h = 0; h < 16; ++h)
+          if (h == tid) { sm.ml[sb][0][h] = m[h]; sm.ml[sb][1][h] = l[h]; }
+      }
       return true;
     };
     auto epilogue = [&](int jj) -> bool {
@@ -401,20 +463,22 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       const int sb = jj & 1;
       if (d.flags & kFirst) {
 #pragma unroll
-        for (int h = 0; h < 16; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
+        for (int h = 0; h < 8; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
       }
-      if (!wait_or_abort(sm, &sm.o_full[sb], (jj >> 1) & 1, args.status, 22)) return false;
+      if (!wt(&sm.o_full[sb], (jj >> 1) & 1, st, 22)) return false;
       tc_fence_after();
       if (d.nblk > 0) {
         float o[16];
-        tmem_ld16(tl + kColO + sb * kNH, o);
+        tmem_ld16(tl + kColO + sb * kNH, o);   // all 16 heads; this warpgroup keeps 8
         tmem_ld_wait();
 #pragma unroll
-        for (int h = 0; h < 16; ++h) {
-          const float ms = sm.ml[sb][0][h], ls = sm.ml[sb][1][h];
+        for (int h = 0; h < 8; ++h) {
+          const int hh = wg * 8 + h;
+          const float ov = wg ? o[8 + h] : o[h];
+          const float ms = sm.ml[sb][0][hh], ls = sm.ml[sb][1][hh];
           const float M = fmaxf(mrun[h], ms);
           const float a = exp2f(mrun[h] - M), bb = exp2f(ms - M);
-          acc[h] = acc[h] * a + o[h] * bb;
+          acc[h] = acc[h] * a + ov * bb;
           lrun[h] = lrun[h] * a + ls * bb;
           mrun[h] = M;
         }
@@ -426,9 +490,10 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
                            (int64_t)(d.hk * G) * p.o_sh;
         float* lse = p.lse + d.b * p.l_sb + (int64_t)d.tq * p.l_st + (int64_t)(d.hk * G) * p.l_sh;
 #pragma unroll
-        for (int h = 0; h < 16; ++h) {
-          if (h < G) {
-            const float s2 = p.attn_sink ? __ldg(p.attn_sink + d.hk * G + h) * kLog2e : -INFINITY;
+        for (int h = 0; h < 8; ++h) {
+          const int hh = wg * 8 + h;
+          if (hh < G) {
+            const float s2 = p.attn_sink ? __ldg(p.attn_sink + d.hk * G + hh) * kLog2e : -INFINITY;
             const float M = fmaxf(mrun[h], s2);
             float outv = 0.f, lv = -INFINITY;
             if (M != -INFINITY) {
@@ -436,8 +501,8 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
               outv = acc[h] * exp2f(mrun[h] - M) / lt;
               lv = (M + log2f(lt)) * kLn2;
             }
-            if (lrow < D) o[h * p.o_sh + lrow] = f2bf(outv);
-            if (lrow == h) lse[h * p.l_sh] = lv;
+            if (lrow < D) o[hh * p.o_sh + lrow] = f2bf(outv);
+            if (lrow == h) lse[hh * p.l_sh] = lv;
           }
         }
       }
@@ -447,7 +512,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
     int job = 0;
     while (ok) {
       const int js = job % kJD;
-      if (!(ok = wait_or_abort(sm, &sm.jd_full[js], (job / kJD) & 1, args.status, 23))) break;
+      if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 23))) break;
       if (sm.jd[js].flags & kSentinel) break;
       if (!(ok = softmax(job))) break;
       if (job > 0 && !(ok = epilogue(job - 1))) break;
