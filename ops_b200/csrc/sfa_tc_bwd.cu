@@ -48,6 +48,8 @@ constexpr uint32_t kColDQ = 128; // 2 x 16
 struct JobDesc {
   int row, hk, b, tq, kv0, kv_len, pos, nblk, flags;
   int blocks[kMaxTopk];
+  float lse2[kNH];   // lse * log2(e) of the row's heads (-inf past G)
+  float dl[kNH];     // delta of the row's heads
 };
 
 template <int D>
@@ -170,6 +172,15 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
         const unsigned m = __ballot_sync(0xffffffffu, valid);
         if (valid) d.blocks[n + __popc(m & ((1u << lane) - 1u))] = e;
         n += __popc(m);
+      }
+      if (lane < kNH) {
+        float l2 = -INFINITY, dlv = 0.f;
+        if (lane < G) {
+          l2 = p.lse[r.b * p.l_sb + r.tq * p.l_st + (int64_t)(hk * G + lane) * p.l_sh] * kLog2e;
+          dlv = args.delta[(int64_t)row * p.h_q + hk * G + lane];
+        }
+        d.lse2[lane] = l2;
+        d.dl[lane] = dlv;
       }
       __syncwarp();
       if (lane == 0) {
@@ -310,12 +321,12 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
       if (d.flags & kSentinel) break;
       const int ib = job & 1;
       float lse2[16], dl[16];
-      const int64_t rowoff = (int64_t)d.row * p.h_q + d.hk * G;
-      const float* lsep = p.lse + d.b * p.l_sb + (int64_t)d.tq * p.l_st + (int64_t)(d.hk * G) * p.l_sh;
 #pragma unroll
-      for (int h = 0; h < 16; ++h) {
-        lse2[h] = h < G ? lsep[h * p.l_sh] * kLog2e : -INFINITY;
-        dl[h] = h < G ? args.delta[rowoff + h] : 0.f;
+      for (int h4 = 0; h4 < 4; ++h4) {
+        const float4 a = reinterpret_cast<const float4*>(d.lse2)[h4];
+        const float4 b = reinterpret_cast<const float4*>(d.dl)[h4];
+        lse2[4 * h4] = a.x; lse2[4 * h4 + 1] = a.y; lse2[4 * h4 + 2] = a.z; lse2[4 * h4 + 3] = a.w;
+        dl[4 * h4] = b.x; dl[4 * h4 + 1] = b.y; dl[4 * h4 + 2] = b.z; dl[4 * h4 + 3] = b.w;
       }
       const int nch = (d.nblk + 1) / 2;
       for (int c = 0; c < nch && ok; ++c, ++g) {
@@ -436,6 +447,13 @@ struct JobDesc {
   int e, b, hk, kv0, kv_len, n, list0, flags;
 };
 
+// Per-batch metadata written by the producer next to the batch's Q/dO tiles.
+struct BatchMeta {
+  int pos[kQB];
+  float lse2[kQB][kNH];   // -inf marks an absent (query, head) row
+  float dl[kQB][kNH];
+};
+
 template <int D>
 struct Smem {
   static constexpr int kBatchBytes = 128 * D * 2;   // 128 rows x D bf16
@@ -447,6 +465,7 @@ struct Smem {
   alignas(1024) uint8_t pbuf[128 * 64 * 2];
   alignas(1024) uint8_t dsbuf[128 * 64 * 2];
   JobDesc jd[kJD];
+  alignas(16) BatchMeta meta[2];
   uint64_t b_full[2], b_empty[2], kv_full, kv_empty;
   uint64_t sdp_full[2], sdp_empty[2], pds_full, pds_empty;
   uint64_t acc_full[2], acc_empty[2];
@@ -569,19 +588,37 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
         const int m = min(kQB, n - jb * kQB);
         // lanes 0..m-1 look up their query row
-        int tq = 0, bb = 0;
+        int tq = 0, bb = 0, rowid = 0, pos = 0;
         if (lane < m) {
-          const int row = __ldg(args.entries + list0 + jb * kQB + lane);
-          const Row r = row_info(p, row);
+          rowid = __ldg(args.entries + list0 + jb * kQB + lane);
+          const Row r = row_info(p, rowid);
           tq = (int)r.tq;
           bb = r.b;
+          pos = r.pos;
         }
         const int s = gb & 1;
-        if (lane == 0) {
-          ok = wt(&sm.b_empty[s], ((gb >> 1) & 1) ^ 1, st, 3);
-          if (ok) mbar_arrive_expect_tx(&sm.b_full[s], (uint32_t)(2 * m * G * D * 2));
-        }
+        if (lane == 0) ok = wt(&sm.b_empty[s], ((gb >> 1) & 1) ^ 1, st, 3);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+        // metadata of the batch's 8 x 16 (query, head) rows
+        BatchMeta& mt = sm.meta[s];
+        if (lane < kQB) mt.pos[lane] = pos;
+#pragma unroll
+        for (int it = 0; it < kQB * kNH / 32; ++it) {
+          const int i = it * 32 + lane, j = i >> 4, h = i & 15;
+          const int rj = __shfl_sync(0xffffffffu, rowid, j);
+          const int tj = __shfl_sync(0xffffffffu, tq, j);
+          const int bj = __shfl_sync(0xffffffffu, bb, j);
+          float l2 = -INFINITY, dlv = 0.f;
+          if (j < m && h < G) {
+            l2 = p.lse[bj * p.l_sb + (int64_t)tj * p.l_st + (int64_t)(hk * G + h) * p.l_sh] * kLog2e;
+            dlv = args.delta[(int64_t)rj * p.h_q + hk * G + h];
+          }
+          mt.lse2[j][h] = l2;
+          mt.dl[j][h] = dlv;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(&sm.b_full[s], (uint32_t)(2 * m * G * D * 2));
         for (int j = 0; j < m; ++j) {
           const int tqj = __shfl_sync(0xffffffffu, tq, j);
           const int bj = __shfl_sync(0xffffffffu, bb, j);
@@ -704,20 +741,17 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       const int nb = (d.n + kQB - 1) / kQB;
       for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
         const int s = gb & 1;
-        const int m = min(kQB, d.n - jb * kQB);
-        bool rvalid = jq < m && h < G;
-        float lse2 = -INFINITY, dl = 0.f;
-        int pos = 0;
-        if (rvalid) {
-          const int row = __ldg(args.entries + d.list0 + jb * kQB + jq);
-          const Row r = row_info(p, row);
-          lse2 = p.lse[r.b * p.l_sb + r.tq * p.l_st + (int64_t)(d.hk * G + h) * p.l_sh] * kLog2e;
-          dl = args.delta[(int64_t)row * p.h_q + d.hk * G + h];
-          pos = r.pos;
-          rvalid = lse2 != -INFINITY;
-        }
         if (!(ok = wt(&sm.sdp_full[s], (gb >> 1) & 1, st, 21))) break;
         tc_fence_after();
+        // the producer published the batch metadata with its arrive on b_full; that
+        // phase is complete (the MMA consumed the batch) and cannot advance again
+        // before this batch's P/dS are written, so this wait returns at once and
+        // orders the metadata reads after the producer's writes
+        if (!(ok = wt(&sm.b_full[s], (gb >> 1) & 1, st, 24))) break;
+        const float lse2 = sm.meta[s].lse2[jq][h];
+        const float dl = sm.meta[s].dl[jq][h];
+        const int pos = sm.meta[s].pos[jq];
+        const bool rvalid = lse2 != -INFINITY;
         uint32_t pk[32], dk[32];
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
