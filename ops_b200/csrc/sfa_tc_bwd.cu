@@ -48,9 +48,10 @@ constexpr uint32_t kColDQ = 128; // 2 x 16
 struct JobDesc {
   int row, hk, b, tq, kv0, kv_len, pos, nblk, flags;
   int blocks[kMaxTopk];
-  float lse2[kNH];   // lse * log2(e) of the row's heads (-inf past G)
-  float dl[kNH];     // delta of the row's heads
+  alignas(16) float lse2[kNH];   // lse * log2(e) of the row's heads (-inf past G); read as float4
+  alignas(16) float dl[kNH];     // delta of the row's heads
 };
+static_assert(offsetof(JobDesc, lse2) % 16 == 0 && offsetof(JobDesc, dl) % 16 == 0, "float4 reads");
 
 template <int D>
 struct Smem {
