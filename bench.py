@@ -177,6 +177,25 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+def reduce_over_ranks(step_ms, e2e_ms, flops, device):
+    """Whole-job figures: the slowest rank's step times and the work of all
+    ranks (each rank processes its own batch; nothing else is exchanged)."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return float(step_ms), float(e2e_ms), float(flops)
+    t = torch.tensor([step_ms, e2e_ms], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    f = torch.tensor([flops], dtype=torch.float64, device=device)
+    dist.all_reduce(f, op=dist.ReduceOp.SUM)
+    return float(t[0]), float(t[1]), float(f[0])
+
+
+def rank_seed(rank: int) -> int:
+    """Each rank draws its own batch of the configuration."""
+    return 1000 + rank
+
+
 def config_dict(cfg, n):
     return {"workload": f"{cfg.name}: block-sparse GQA attention fwd+bwd, B={cfg.B}/rank, T={cfg.T}, "
                         f"Hq={cfg.Hq}, Hk={cfg.Hk}, Dqk={cfg.Dqk}, Dv={cfg.Dv}, block_size={cfg.bs}, "
@@ -208,7 +227,7 @@ def run_ours(args, cfg):
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     lib = _lib.load()
 
-    d = W.make_inputs(cfg, dev, seed=1000 + rank)
+    d = W.make_inputs(cfg, dev, seed=rank_seed(rank))
     q, k, v, idx, do = d["q"], d["k"], d["v"], d["idx"], d["do"]
     G = cfg.Hq // cfg.Hk
     pairs = W.count_pairs(idx, cfg.bs, cfg.T, cfg.T) * G
@@ -309,16 +328,7 @@ def run_ours(args, cfg):
     sampler.stop()
     clocks = sampler.summary(t_wall0, t_wall1)
 
-    # max over ranks; total work over ranks
-    t = torch.tensor([step_ms, e_ms, fl.total], dtype=torch.float64, device=dev)
-    if world > 1:
-        tmax = t.clone()
-        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-        tsum = t.clone()
-        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
-        step_ms_max, e_ms_max, flops_all = float(tmax[0]), float(tmax[1]), float(tsum[2])
-    else:
-        step_ms_max, e_ms_max, flops_all = step_ms, e_ms, fl.total
+    step_ms_max, e_ms_max, flops_all = reduce_over_ranks(step_ms, e_ms, fl.total, dev)
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
