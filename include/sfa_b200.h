@@ -149,6 +149,17 @@ int sfa_bwd(const SfaParams* p, void* workspace, size_t workspace_bytes, void* s
  *  - dq: replaces `_attn_bwd_dq_dsink` / `_inner_dq` (SFA.py:613-716, 856-1002);
  *  - dkdv: replaces `_attn_bwd_dk_dv` / `_inner_dkv` (SFA.py:719-853, 1005-1145);
  *    with SFA_DKV_INVERTED it first builds the block->query index. */
+/* Backward for callers that cannot allocate device memory (no counterpart in the
+ * reference).  Same results as sfa_bwd, but the scratch comes from a 32 MiB
+ * static device array inside the library instead of a caller workspace; every
+ * GPU that loads the library reserves that array until the process exits.
+ * Problems whose sfa_bwd_workspace_bytes() exceeds 32 MiB are refused with
+ * SFA_ERR_WORKSPACE before anything is launched.  The first call on a device
+ * looks up the array's device address; make it before any stream capture.
+ * Calls share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller. */
+int sfa_bwd_noalloc(const SfaParams* p, void* stream);
+
 int sfa_bwd_preprocess(const SfaParams* p, void* workspace, size_t workspace_bytes, void* stream);
 int sfa_bwd_dq(const SfaParams* p, void* workspace, size_t workspace_bytes, void* stream);
 int sfa_bwd_dkdv(const SfaParams* p, void* workspace, size_t workspace_bytes, void* stream);

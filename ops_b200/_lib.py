@@ -54,6 +54,7 @@ EXPORTS = {
     "sfa_bwd_workspace_bytes": ([ctypes.POINTER(SfaParams)], ctypes.c_size_t),
     "sfa_fwd": ([ctypes.POINTER(SfaParams), _c_void_p, ctypes.c_size_t, _c_void_p], _i32),
     "sfa_bwd": ([ctypes.POINTER(SfaParams), _c_void_p, ctypes.c_size_t, _c_void_p], _i32),
+    "sfa_bwd_noalloc": ([ctypes.POINTER(SfaParams), _c_void_p], _i32),
     "sfa_bwd_preprocess": ([ctypes.POINTER(SfaParams), _c_void_p, ctypes.c_size_t, _c_void_p], _i32),
     "sfa_bwd_dq": ([ctypes.POINTER(SfaParams), _c_void_p, ctypes.c_size_t, _c_void_p], _i32),
     "sfa_bwd_dkdv": ([ctypes.POINTER(SfaParams), _c_void_p, ctypes.c_size_t, _c_void_p], _i32),

@@ -24,6 +24,8 @@ static int fail(int code, const std::string& msg) {
   return code;
 }
 
+int report_error(int code, const std::string& msg) { return fail(code, msg); }
+
 static int cuda_fail(cudaError_t e, const char* where) {
   return fail(SFA_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
 }

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <string>
+
 #include "../../include/sfa_b200.h"
 
 namespace sfa {
@@ -68,5 +70,8 @@ int device_cc();
 
 // Count of kernels this library has enqueued (reported by sfa_kernel_launches).
 void note_launch(int n = 1);
+
+// Record `msg` for sfa_last_error_string() and return `code`.
+int report_error(int code, const std::string& msg);
 
 }  // namespace sfa
