@@ -438,8 +438,9 @@ cudaError_t launch(const SfaParams& p, const float* delta, cudaStream_t stream) 
 // =========================================================================
 namespace dkdv {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 224;       // warp 0 metadata, 1 MMA, 2-5 P/dS + epilogue, 6 TMA
 constexpr int kQB = 8;              // queries per batch (x 16 heads = 128 MMA rows)
+constexpr int kMeta = 6;            // batch metadata ring depth
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColSdP = 0;     // 2 slots x (64 S + 64 dP)
 constexpr uint32_t kColAcc = 256;   // 2 buffers x (64 dV^T + 64 dK^T)
@@ -448,9 +449,12 @@ struct JobDesc {
   int e, b, hk, kv0, kv_len, n, list0, flags;
 };
 
-// Per-batch metadata written by the producer next to the batch's Q/dO tiles.
+// Per-batch metadata of the (query, head) rows of one batch, written by the
+// metadata warp ahead of the loads: TMA coordinates of each query, its causal
+// position, and lse/delta of each (query, head).
 struct BatchMeta {
-  int pos[kQB];
+  int tq[kQB], b[kQB], pos[kQB];
+  int m;                  // queries in the batch
   float lse2[kQB][kNH];   // -inf marks an absent (query, head) row
   float dl[kQB][kNH];
 };
@@ -466,8 +470,9 @@ struct Smem {
   alignas(1024) uint8_t pbuf[128 * 64 * 2];
   alignas(1024) uint8_t dsbuf[128 * 64 * 2];
   JobDesc jd[kJD];
-  alignas(16) BatchMeta meta[2];
+  alignas(16) BatchMeta meta[kMeta];
   uint64_t b_full[2], b_empty[2], kv_full, kv_empty;
+  uint64_t meta_full[kMeta], meta_empty[kMeta];
   uint64_t sdp_full[2], sdp_empty[2], pds_full, pds_empty;
   uint64_t acc_full[2], acc_empty[2];
   uint64_t jd_full[kJD], jd_empty[kJD];
@@ -511,11 +516,16 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       mbar_init(&sm.acc_full[i], 1);
       mbar_init(&sm.acc_empty[i], 128);
     }
+    for (int i = 0; i < kMeta; ++i) {
+      mbar_init(&sm.meta_full[i], 1);
+      mbar_init(&sm.meta_empty[i], 1 + 128);   // TMA thread + P/dS threads
+    }
     mbar_init(&sm.kv_full, 1);
     mbar_init(&sm.kv_empty, 1);
     mbar_init(&sm.pds_full, 128);
     mbar_init(&sm.pds_empty, 1);
-    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 1 + 128); }
+    // consumers of a job descriptor: MMA thread, TMA thread, P/dS threads
+    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 2 + 128); }
     fence_barrier_init();
   }
   // padded head rows (G..15 of every query) stay zero
@@ -528,7 +538,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
     tmem_alloc(&sm.tmem_base, kTmemCols);
     tmem_relinquish();
   }
-  if (warp == 0 && lane == 0) {
+  if (warp == 6 && lane == 0) {
     prefetch_tmap(&tmq);
     prefetch_tmap(&tmdo);
     prefetch_tmap(&tmk);
@@ -540,7 +550,10 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
   const uint32_t tmem = sm.tmem_base;
 
   if (warp == 0) {
-    // ============================================================ producer
+    // ============================================================ scheduler + metadata
+    // Items run unit-major (all blocks of one (sequence, kv head) before the
+    // next), so the CTAs working at one time share that unit's Q/dO in L2; the
+    // lowest blocks, which have the longest query lists, start first.
     int job = 0, gb = 0;
     bool ok = true;
     while (ok) {
@@ -548,7 +561,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       if (lane == 0) item = atomicAdd(args.sched, 1);
       item = __shfl_sync(0xffffffffu, item, 0);
       if (item >= args.nitems) break;
-      const int e = item / args.units, u = item - e * args.units;
+      const int u = item / args.nblk, e = item - u * args.nblk;
       const int seq = u / p.h_kv, hk = u - seq * p.h_kv;
       int kv0 = 0, kv_len = p.kv_len, b = seq;
       if (p.cu_seqlens_q != nullptr) {
@@ -573,22 +586,16 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
           d.list0 = list0;
           d.flags = 0;
           mbar_arrive(&sm.jd_full[js]);
-          ok = wt(&sm.kv_empty, (job & 1) ^ 1, st, 2);
-        }
-        if (ok) {
-          mbar_arrive_expect_tx(&sm.kv_full, 2u * 64u * D * 2u);
-#pragma unroll
-          for (int cd = 0; cd < D / 64; ++cd) {
-            tma_load_4d(&sm.ke[cd * 64 * 128], &tmk, &sm.kv_full, cd * 64, hk, kv0 + e * 64, b);
-            tma_load_4d(&sm.ve[cd * 64 * 128], &tmv, &sm.kv_full, cd * 64, hk, kv0 + e * 64, b);
-          }
         }
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       const int nb = (n + kQB - 1) / kQB;
       for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
+        const int slot = gb % kMeta;
+        if (lane == 0) ok = wt(&sm.meta_empty[slot], ((gb / kMeta) & 1) ^ 1, st, 2);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
         const int m = min(kQB, n - jb * kQB);
-        // lanes 0..m-1 look up their query row
         int tq = 0, bb = 0, rowid = 0, pos = 0;
         if (lane < m) {
           rowid = __ldg(args.entries + list0 + jb * kQB + lane);
@@ -597,13 +604,13 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
           bb = r.b;
           pos = r.pos;
         }
-        const int s = gb & 1;
-        if (lane == 0) ok = wt(&sm.b_empty[s], ((gb >> 1) & 1) ^ 1, st, 3);
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (!ok) break;
-        // metadata of the batch's 8 x 16 (query, head) rows
-        BatchMeta& mt = sm.meta[s];
-        if (lane < kQB) mt.pos[lane] = pos;
+        BatchMeta& mt = sm.meta[slot];
+        if (lane < kQB) {
+          mt.tq[lane] = tq;
+          mt.b[lane] = bb;
+          mt.pos[lane] = pos;
+        }
+        if (lane == 0) mt.m = m;
 #pragma unroll
         for (int it = 0; it < kQB * kNH / 32; ++it) {
           const int i = it * 32 + lane, j = i >> 4, h = i & 15;
@@ -619,19 +626,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
           mt.dl[j][h] = dlv;
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive_expect_tx(&sm.b_full[s], (uint32_t)(2 * m * G * D * 2));
-        for (int j = 0; j < m; ++j) {
-          const int tqj = __shfl_sync(0xffffffffu, tq, j);
-          const int bj = __shfl_sync(0xffffffffu, bb, j);
-          if (lane == 0 && ok) {
-#pragma unroll
-            for (int cd = 0; cd < D / 64; ++cd) {
-              tma_load_4d(&sm.qb[s][cd * 128 * 128 + j * 16 * 128], &tmq, &sm.b_full[s], cd * 64, hk * G, tqj, bj);
-              tma_load_4d(&sm.dob[s][cd * 128 * 128 + j * 16 * 128], &tmdo, &sm.b_full[s], cd * 64, hk * G, tqj,
-                          bj);
-            }
-          }
-        }
+        if (lane == 0) mbar_arrive(&sm.meta_full[slot]);
       }
       ++job;
     }
@@ -640,6 +635,46 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       if (wt(&sm.jd_empty[js], ((job / kJD) & 1) ^ 1, st, 4)) {
         sm.jd[js].flags = kSentinel;
         mbar_arrive(&sm.jd_full[js]);
+      }
+    }
+  } else if (warp == 6) {
+    // ============================================================ TMA loads
+    if (lane == 0) {
+      int job = 0, gb = 0;
+      bool ok = true;
+      while (ok) {
+        const int js = job % kJD;
+        if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 5))) break;
+        const JobDesc& d = sm.jd[js];
+        if (d.flags & kSentinel) break;
+        if (!(ok = wt(&sm.kv_empty, (job & 1) ^ 1, st, 6))) break;
+        mbar_arrive_expect_tx(&sm.kv_full, 2u * 64u * D * 2u);
+#pragma unroll
+        for (int cd = 0; cd < D / 64; ++cd) {
+          tma_load_4d(&sm.ke[cd * 64 * 128], &tmk, &sm.kv_full, cd * 64, d.hk, d.kv0 + d.e * 64, d.b);
+          tma_load_4d(&sm.ve[cd * 64 * 128], &tmv, &sm.kv_full, cd * 64, d.hk, d.kv0 + d.e * 64, d.b);
+        }
+        const int nb = (d.n + kQB - 1) / kQB;
+        for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
+          const int slot = gb % kMeta, s = gb & 1;
+          if (!(ok = wt(&sm.meta_full[slot], (gb / kMeta) & 1, st, 7))) break;
+          if (!(ok = wt(&sm.b_empty[s], ((gb >> 1) & 1) ^ 1, st, 3))) break;
+          const BatchMeta& mt = sm.meta[slot];
+          const int m = mt.m;
+          mbar_arrive_expect_tx(&sm.b_full[s], (uint32_t)(2 * m * G * D * 2));
+          for (int j = 0; j < m; ++j) {
+            const int tq = mt.tq[j], bb = mt.b[j];
+#pragma unroll
+            for (int cd = 0; cd < D / 64; ++cd) {
+              tma_load_4d(&sm.qb[s][cd * 128 * 128 + j * 16 * 128], &tmq, &sm.b_full[s], cd * 64, d.hk * G, tq, bb);
+              tma_load_4d(&sm.dob[s][cd * 128 * 128 + j * 16 * 128], &tmdo, &sm.b_full[s], cd * 64, d.hk * G, tq,
+                          bb);
+            }
+          }
+          mbar_arrive(&sm.meta_empty[slot]);
+        }
+        mbar_arrive(&sm.jd_empty[js]);
+        ++job;
       }
     }
   } else if (warp == 1) {
@@ -724,7 +759,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       if (ok && has_pend) issue_acc(pend);
     }
   } else {
-    // ============================================================ P/dS and epilogue
+    // ============================================================ P/dS and epilogue (warps 2-5)
     const int wq = warp & 3;
     const int lrow = wq * 32 + lane;        // TMEM lane: (query j, head h) row, or dim in the epilogue
     const int jq = lrow >> 4, h = lrow & 15;
@@ -741,34 +776,35 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       const int ab = job & 1;
       const int nb = (d.n + kQB - 1) / kQB;
       for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
-        const int s = gb & 1;
+        const int s = gb & 1, slot = gb % kMeta;
+        if (!(ok = wt(&sm.meta_full[slot], (gb / kMeta) & 1, st, 24))) break;
+        const BatchMeta& mt = sm.meta[slot];
+        const float lse2 = mt.lse2[jq][h];
+        const float dl = mt.dl[jq][h];
+        const int pos = mt.pos[jq];
+        const bool rvalid = lse2 != -INFINITY;
+        mbar_arrive(&sm.meta_empty[slot]);
         if (!(ok = wt(&sm.sdp_full[s], (gb >> 1) & 1, st, 21))) break;
         tc_fence_after();
-        // the producer published the batch metadata with its arrive on b_full; that
-        // phase is complete (the MMA consumed the batch) and cannot advance again
-        // before this batch's P/dS are written, so this wait returns at once and
-        // orders the metadata reads after the producer's writes
-        if (!(ok = wt(&sm.b_full[s], (gb >> 1) & 1, st, 24))) break;
-        const float lse2 = sm.meta[s].lse2[jq][h];
-        const float dl = sm.meta[s].dl[jq][h];
-        const int pos = sm.meta[s].pos[jq];
-        const bool rvalid = lse2 != -INFINITY;
         uint32_t pk[32], dk[32];
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          float sv[16], dp[16];
-          tmem_ld16(tl + kColSdP + s * 128 + q4 * 16, sv);
-          tmem_ld16(tl + kColSdP + s * 128 + 64 + q4 * 16, dp);
+        for (int half = 0; half < 2; ++half) {
+          float sv[32], dp[32];
+          const uint32_t col = tl + kColSdP + s * 128 + half * 32;
+          tmem_ld16(col, *reinterpret_cast<float(*)[16]>(&sv[0]));
+          tmem_ld16(col + 16, *reinterpret_cast<float(*)[16]>(&sv[16]));
+          tmem_ld16(col + 64, *reinterpret_cast<float(*)[16]>(&dp[0]));
+          tmem_ld16(col + 80, *reinterpret_cast<float(*)[16]>(&dp[16]));
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 16; i += 2) {
-            const int key0 = d.e * 64 + q4 * 16 + i;
+          for (int i = 0; i < 32; i += 2) {
+            const int key0 = d.e * 64 + half * 32 + i;
             const bool v0 = rvalid && key0 < d.kv_len && (!p.causal || key0 <= pos);
             const bool v1 = rvalid && key0 + 1 < d.kv_len && (!p.causal || key0 + 1 <= pos);
             const float p0 = v0 ? exp2f(sv[i] * c2 - lse2) : 0.f;
             const float p1 = v1 ? exp2f(sv[i + 1] * c2 - lse2) : 0.f;
-            pk[q4 * 8 + i / 2] = pack_bf16x2(p0, p1);
-            dk[q4 * 8 + i / 2] = pack_bf16x2(p0 * (dp[i] - dl), p1 * (dp[i + 1] - dl));
+            pk[half * 16 + i / 2] = pack_bf16x2(p0, p1);
+            dk[half * 16 + i / 2] = pack_bf16x2(p0 * (dp[i] - dl), p1 * (dp[i + 1] - dl));
           }
         }
         tc_fence_before();
