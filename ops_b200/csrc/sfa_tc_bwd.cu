@@ -237,15 +237,14 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
         if (!wt(&sm.ds_full[pd.slot], (pd.g / kR) & 1, st, 10)) return false;
         if (pd.first && !wt(&sm.dq_empty[pd.ib], (((pd.js >> 1)) & 1) ^ 1, st, 11)) return false;
         tc_fence_after();
-        const uint32_t kb = smem_u32(&sm.kst[pd.ks][0]);
-        const uint32_t db = smem_u32(&sm.ds[pd.slot][0]);
+        const uint64_t a0 = smem_desc(smem_u32(&sm.kst[pd.ks][0]), lbo_k, 1024, kSw128);
+        const uint64_t b0 = smem_desc(smem_u32(&sm.ds[pd.slot][0]), 0, 256, kSw32);
         const uint32_t dcol = tmem + kColDQ + pd.ib * kNH;
+        // descriptors advance by adding the byte offset / 16 to the start-address field
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t a = smem_desc(kb + kk * 2048, lbo_k, 1024, kSw128);
-          const uint64_t b = smem_desc(db + kk * 16 * (kNH * 2), 0, 256, kSw32);
-          mma_bf16_ss(dcol, a, b, id_dq, (pd.first && kk == 0) ? 0u : 1u);
-        }
+        for (int kk = 0; kk < 8; ++kk)
+          mma_bf16_ss(dcol, a0 + (uint64_t)(kk * 2048 >> 4), b0 + (uint64_t)(kk * 16 * (kNH * 2) >> 4), id_dq,
+                      (pd.first && kk == 0) ? 0u : 1u);
         mma_commit(&sm.k_empty[pd.ks]);
         mma_commit(&sm.ds_empty[pd.slot]);
         if (pd.last) {
@@ -271,30 +270,28 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
           ++job;
           continue;
         }
-        const uint32_t qb = smem_u32(&sm.q[ib][0]);
-        const uint32_t ob = smem_u32(&sm.dO[ib][0]);
+        const uint64_t qdesc = smem_desc(smem_u32(&sm.q[ib][0]), 16, 1024, kSw128);
+        const uint64_t odesc = smem_desc(smem_u32(&sm.dO[ib][0]), 16, 1024, kSw128);
         for (int c = 0; c < nch && ok; ++c, ++g) {
           const int slot = g % kR, ks = g % KS, vs = g % VS;
           if (!(ok = wt(&sm.sdp_empty[slot], ((g / kR) & 1) ^ 1, st, 15))) break;
           if (!(ok = wt(&sm.k_full[ks], (g / KS) & 1, st, 16))) break;
           if (!(ok = wt(&sm.v_full[vs], (g / VS) & 1, st, 17))) break;
           tc_fence_after();
-          const uint32_t kb = smem_u32(&sm.kst[ks][0]);
-          const uint32_t vb = smem_u32(&sm.vst[vs][0]);
+          const uint64_t kdesc = smem_desc(smem_u32(&sm.kst[ks][0]), 16, 1024, kSw128);
+          const uint64_t vdesc = smem_desc(smem_u32(&sm.vst[vs][0]), 16, 1024, kSw128);
           const uint32_t scol = tmem + kColSdP + slot * 32;
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
-            const uint32_t ko = (k >> 2) * (128 * 128) + (k & 3) * 32;
-            const uint32_t qo = (k >> 2) * (kNH * 128) + (k & 3) * 32;
-            mma_bf16_ss(scol, smem_desc(kb + ko, 16, 1024, kSw128), smem_desc(qb + qo, 16, 1024, kSw128), id_sdp,
-                        k != 0);
+            const uint64_t ko = (uint64_t)(((k >> 2) * (128 * 128) + (k & 3) * 32) >> 4);
+            const uint64_t qo = (uint64_t)(((k >> 2) * (kNH * 128) + (k & 3) * 32) >> 4);
+            mma_bf16_ss(scol, kdesc + ko, qdesc + qo, id_sdp, k != 0);
           }
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
-            const uint32_t vo = (k >> 2) * (128 * 128) + (k & 3) * 32;
-            const uint32_t oo = (k >> 2) * (kNH * 128) + (k & 3) * 32;
-            mma_bf16_ss(scol + 16, smem_desc(vb + vo, 16, 1024, kSw128), smem_desc(ob + oo, 16, 1024, kSw128),
-                        id_sdp, k != 0);
+            const uint64_t vo = (uint64_t)(((k >> 2) * (128 * 128) + (k & 3) * 32) >> 4);
+            const uint64_t oo = (uint64_t)(((k >> 2) * (kNH * 128) + (k & 3) * 32) >> 4);
+            mma_bf16_ss(scol + 16, vdesc + vo, odesc + oo, id_sdp, k != 0);
           }
           mma_commit(&sm.v_empty[vs]);
           mma_commit(&sm.sdp_full[slot]);
@@ -691,18 +688,17 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         if (!wt(&sm.pds_full, pd.gb & 1, st, 10)) return false;
         if (pd.first && !wt(&sm.acc_empty[pd.ab], ((pd.job >> 1) & 1) ^ 1, st, 11)) return false;
         tc_fence_after();
-        const uint32_t ob = smem_u32(&sm.dob[pd.s][0]);
-        const uint32_t qb = smem_u32(&sm.qb[pd.s][0]);
-        const uint32_t pb = smem_u32(&sm.pbuf[0]);
-        const uint32_t db = smem_u32(&sm.dsbuf[0]);
+        const uint64_t od = smem_desc(smem_u32(&sm.dob[pd.s][0]), lbo_rows, 1024, kSw128);
+        const uint64_t qd = smem_desc(smem_u32(&sm.qb[pd.s][0]), lbo_rows, 1024, kSw128);
+        const uint64_t pdsc = smem_desc(smem_u32(&sm.pbuf[0]), 0, 1024, kSw128);
+        const uint64_t dd = smem_desc(smem_u32(&sm.dsbuf[0]), 0, 1024, kSw128);
         const uint32_t acc = tmem + kColAcc + pd.ab * 128;
+        // 16 rows per K-step: +2048 bytes = +128 in the start-address field
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t accum = (pd.first && kk == 0) ? 0u : 1u;
-          mma_bf16_ss(acc, smem_desc(ob + kk * 2048, lbo_rows, 1024, kSw128), smem_desc(pb + kk * 2048, 0, 1024, kSw128),
-                      id_acc, accum);
-          mma_bf16_ss(acc + 64, smem_desc(qb + kk * 2048, lbo_rows, 1024, kSw128),
-                      smem_desc(db + kk * 2048, 0, 1024, kSw128), id_acc, accum);
+          mma_bf16_ss(acc, od + (uint64_t)(kk * 128), pdsc + (uint64_t)(kk * 128), id_acc, accum);
+          mma_bf16_ss(acc + 64, qd + (uint64_t)(kk * 128), dd + (uint64_t)(kk * 128), id_acc, accum);
         }
         mma_commit(&sm.b_empty[pd.s]);
         mma_commit(&sm.pds_empty);
@@ -729,24 +725,22 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
           ++job;
           continue;
         }
-        const uint32_t kb = smem_u32(&sm.ke[0]);
-        const uint32_t vb = smem_u32(&sm.ve[0]);
+        const uint64_t kd = smem_desc(smem_u32(&sm.ke[0]), 16, 1024, kSw128);
+        const uint64_t vd = smem_desc(smem_u32(&sm.ve[0]), 16, 1024, kSw128);
         for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
           const int s = gb & 1;
           if (!(ok = wt(&sm.sdp_empty[s], ((gb >> 1) & 1) ^ 1, st, 15))) break;
           if (!(ok = wt(&sm.b_full[s], (gb >> 1) & 1, st, 16))) break;
           tc_fence_after();
-          const uint32_t qb = smem_u32(&sm.qb[s][0]);
-          const uint32_t ob = smem_u32(&sm.dob[s][0]);
+          const uint64_t qd = smem_desc(smem_u32(&sm.qb[s][0]), 16, 1024, kSw128);
+          const uint64_t od = smem_desc(smem_u32(&sm.dob[s][0]), 16, 1024, kSw128);
           const uint32_t scol = tmem + kColSdP + s * 128;
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
-            const uint32_t ro = (k >> 2) * (128 * 128) + (k & 3) * 32;
-            const uint32_t ko = (k >> 2) * (64 * 128) + (k & 3) * 32;
-            mma_bf16_ss(scol, smem_desc(qb + ro, 16, 1024, kSw128), smem_desc(kb + ko, 16, 1024, kSw128), id_sdp,
-                        k != 0);
-            mma_bf16_ss(scol + 64, smem_desc(ob + ro, 16, 1024, kSw128), smem_desc(vb + ko, 16, 1024, kSw128),
-                        id_sdp, k != 0);
+            const uint64_t ro = (uint64_t)(((k >> 2) * (128 * 128) + (k & 3) * 32) >> 4);
+            const uint64_t ko = (uint64_t)(((k >> 2) * (64 * 128) + (k & 3) * 32) >> 4);
+            mma_bf16_ss(scol, qd + ro, kd + ko, id_sdp, k != 0);
+            mma_bf16_ss(scol + 64, od + ro, vd + ko, id_sdp, k != 0);
           }
           mma_commit(&sm.sdp_full[s]);
           if (jb == nb - 1) mma_commit(&sm.kv_empty);

@@ -73,8 +73,8 @@ struct Smem {
   alignas(1024) uint8_t q[2][kQBytes];
   alignas(1024) uint8_t p[kPBytes];
   JobDesc jd[kJD];
-  alignas(16) float red[8][16];
-  alignas(16) float redl[8][16];
+  alignas(16) float red[9][16];
+  alignas(16) float redl[9][16];
   alignas(16) float ml[2][2][16];
   int plist[kMaxTopk];
   uint64_t k_full[kKS], k_empty[kKS], v_full[kVS], v_empty[kVS];
@@ -126,27 +126,26 @@ __device__ __forceinline__ float warp_reduce16(const float (&v)[16], int lane) {
 }
 
 // Reduce over the 256 softmax threads; every thread gets all 16 results.
+// buf holds the 8 warps' partials in rows 0..7 and the final values in row 8.
 template <bool kMax>
-__device__ __forceinline__ void block_reduce16(float (&v)[16], float (*buf)[16], int w8, int lane) {
+__device__ __forceinline__ void block_reduce16(float (&v)[16], float (*buf)[16], int w8, int lane, int tid) {
   const float r = warp_reduce16<kMax>(v, lane);
   if ((lane & 1) == 0) buf[w8][(lane >> 1) & 15] = r;
   named_barrier(1, kSoftmaxThreads);
+  if (tid < 16) {
+    float a = buf[0][tid];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) a = kMax ? fmaxf(a, buf[w][tid]) : a + buf[w][tid];
+    buf[8][tid] = a;
+  }
+  named_barrier(1, kSoftmaxThreads);
 #pragma unroll
   for (int h4 = 0; h4 < 4; ++h4) {
-    float4 acc = reinterpret_cast<const float4*>(buf[0])[h4];
-#pragma unroll
-    for (int w = 1; w < 8; ++w) {
-      const float4 x = reinterpret_cast<const float4*>(buf[w])[h4];
-      if (kMax) {
-        acc.x = fmaxf(acc.x, x.x); acc.y = fmaxf(acc.y, x.y); acc.z = fmaxf(acc.z, x.z); acc.w = fmaxf(acc.w, x.w);
-      } else {
-        acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
-      }
-    }
-    v[4 * h4 + 0] = acc.x;
-    v[4 * h4 + 1] = acc.y;
-    v[4 * h4 + 2] = acc.z;
-    v[4 * h4 + 3] = acc.w;
+    const float4 x = reinterpret_cast<const float4*>(buf[8])[h4];
+    v[4 * h4 + 0] = x.x;
+    v[4 * h4 + 1] = x.y;
+    v[4 * h4 + 2] = x.z;
+    v[4 * h4 + 3] = x.w;
   }
 }
 
@@ -215,19 +214,28 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
     // ============================================================ K producer
     int job = 0, item_i = 0, use = 0;
     bool ok = true;
+    // the index slots of the next item are loaded one item ahead (lane s holds
+    // slots s and s + 32), so their latency overlaps this item's loads
+    auto fetch = [&](int item, int& e0, int& e1, Row& r) {
+      const int hk = item / args.nrows, row = item - hk * args.nrows;
+      r = row_info(p, row);
+      const int32_t* idx = p.block_indices + r.b * p.i_sb + r.tq * p.i_st + (int64_t)hk * p.i_sh;
+      e0 = lane < p.topk ? __ldg(idx + lane) : -1;
+      e1 = lane + 32 < p.topk ? __ldg(idx + lane + 32) : -1;
+    };
+    int nx0 = -1, nx1 = -1;
+    Row nr{};
+    if (blockIdx.x < args.nitems) fetch(blockIdx.x, nx0, nx1, nr);
     for (int item = blockIdx.x; item < args.nitems && ok; item += gridDim.x, ++item_i) {
       const int hk = item / args.nrows, row = item - hk * args.nrows;
-      const Row r = row_info(p, row);
-      const int32_t* idx = p.block_indices + r.b * p.i_sb + r.tq * p.i_st + (int64_t)hk * p.i_sh;
+      const Row r = nr;
+      const int cur0 = nx0, cur1 = nx1;
+      if (item + (int)gridDim.x < args.nitems) fetch(item + gridDim.x, nx0, nx1, nr);
       int n = 0;
-      for (int s0 = 0; s0 < p.topk; s0 += 32) {
-        const int s = s0 + lane;
-        int e = -1;
-        bool valid = false;
-        if (s < p.topk) {
-          e = __ldg(idx + s);
-          valid = block_valid_keys(e, 64, r.kv_len, r.pos, p.causal) > 0;
-        }
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int e = half ? cur1 : cur0;
+        const bool valid = block_valid_keys(e, 64, r.kv_len, r.pos, p.causal) > 0;
         const unsigned m = __ballot_sync(0xffffffffu, valid);
         if (valid) sm.plist[n + __popc(m & ((1u << lane) - 1u))] = e;
         n += __popc(m);
@@ -312,19 +320,19 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
         if (!wt(&sm.o_empty[sb], ((jj >> 1) & 1) ^ 1, st, 11)) return false;
         tc_fence_after();
         const uint32_t dcol = tmem + kColO + sb * kNH;
-        const uint32_t pbase = smem_u32(&sm.p[0]);
+        const uint64_t pdesc = smem_desc(smem_u32(&sm.p[0]), 0, 256, kSw32);
         const int nch = (d.nblk + 1) / 2;
         for (int c = 0; c < nch; ++c, ++vuse) {
           const int s = vuse % VS;
           if (!wt(&sm.v_full[s], (vuse / VS) & 1, st, 12)) return false;
           tc_fence_after();
-          const uint32_t vbase = smem_u32(&sm.vst[s][0]);
+          // descriptors advance by adding the byte offset / 16 to the start-address field
+          const uint64_t a0 = smem_desc(smem_u32(&sm.vst[s][0]), lbo_v, 1024, kSw128);
+          const uint64_t b0 = pdesc + (uint64_t)(c * 128 * (kNH * 2) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t a = smem_desc(vbase + kk * 2048, lbo_v, 1024, kSw128);
-            const uint64_t b = smem_desc(pbase + (c * 128 + kk * 16) * (kNH * 2), 0, 256, kSw32);
-            mma_bf16_ss(dcol, a, b, id_o, (c | kk) != 0);
-          }
+          for (int kk = 0; kk < 8; ++kk)
+            mma_bf16_ss(dcol, a0 + (uint64_t)(kk * 2048 >> 4), b0 + (uint64_t)(kk * 16 * (kNH * 2) >> 4), id_o,
+                        (c | kk) != 0);
           mma_commit(&sm.v_empty[s]);
         }
         mma_commit(&sm.p_empty);
@@ -343,20 +351,18 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
         const int sb = job & 1;
         if (!(ok = wt(&sm.s_empty[sb], ((job >> 1) & 1) ^ 1, st, 15))) break;
         tc_fence_after();
-        const uint32_t qbase = smem_u32(&sm.q[qs][0]);
+        const uint64_t qdesc = smem_desc(smem_u32(&sm.q[qs][0]), 16, 1024, kSw128);
         const int nch = (d.nblk + 1) / 2;
         for (int c = 0; c < nch && ok; ++c, ++kuse) {
           const int s = kuse % KS;
           if (!(ok = wt(&sm.k_full[s], (kuse / KS) & 1, st, 16))) break;
           tc_fence_after();
-          const uint32_t kbase = smem_u32(&sm.kst[s][0]);
+          const uint64_t kdesc = smem_desc(smem_u32(&sm.kst[s][0]), 16, 1024, kSw128);
           const uint32_t dcol = tmem + kColS + sb * 128 + c * kNH;
 #pragma unroll
-          for (int k = 0; k < D / 16; ++k) {
-            const uint64_t a = smem_desc(kbase + (k >> 2) * (128 * 128) + (k & 3) * 32, 16, 1024, kSw128);
-            const uint64_t b = smem_desc(qbase + (k >> 2) * (kNH * 128) + (k & 3) * 32, 16, 1024, kSw128);
-            mma_bf16_ss(dcol, a, b, id_s, k != 0);
-          }
+          for (int k = 0; k < D / 16; ++k)
+            mma_bf16_ss(dcol, kdesc + (uint64_t)(((k >> 2) * (128 * 128) + (k & 3) * 32) >> 4),
+                        qdesc + (uint64_t)(((k >> 2) * (kNH * 128) + (k & 3) * 32) >> 4), id_s, k != 0);
           mma_commit(&sm.k_empty[s]);
         }
         if (!ok) break;
@@ -421,7 +427,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
           }
         }
       }
-      block_reduce16<true>(m, sm.red, w8, lane);
+      block_reduce16<true>(m, sm.red, w8, lane, tid);
       float l[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) l[h] = 0.f;
@@ -450,7 +456,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       }
       fence_proxy_async_smem();
       mbar_arrive(&sm.p_full);
-      block_reduce16<false>(l, sm.redl, w8, lane);
+      block_reduce16<false>(l, sm.redl, w8, lane, tid);
       if (tid < 16) {
 #pragma unroll
         for (int h = 0; h < 16; ++h)
