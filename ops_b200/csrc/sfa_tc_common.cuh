@@ -58,6 +58,21 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps (instead of spinning and
+// taking issue slots from the warps sharing its SM sub-partition) until the
+// phase completes or about `hint_ns` elapse.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity; gives up after ~2 s (returns false).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
@@ -65,8 +80,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
     if (global_timer_ns() - t0 > kWaitLimitNs) return false;
   }
 }
