@@ -346,7 +346,7 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
         float ds[16];
 #pragma unroll
         for (int h = 0; h < 16; ++h) {
-          const float pr = (valid && lse2[h] != -INFINITY) ? exp2f(s[h] * c2 - lse2[h]) : 0.f;
+          const float pr = (valid && lse2[h] != -INFINITY) ? ex2(s[h] * c2 - lse2[h]) : 0.f;
           ds[h] = pr * (dp[h] - dl[h]);
         }
         if (!(ok = wt(&sm.ds_empty[slot], ((g / kR) & 1) ^ 1, st, 22))) break;
@@ -435,7 +435,8 @@ cudaError_t launch(const SfaParams& p, const float* delta, cudaStream_t stream) 
 // =========================================================================
 namespace dkdv {
 
-constexpr int kThreads = 224;       // warp 0 metadata, 1 MMA, 2-5 P/dS + epilogue, 6 TMA
+constexpr int kThreads = 352;       // warp 0 metadata, 1 MMA, 2-9 P/dS + epilogue, 10 TMA
+constexpr int kWG = 256;            // P/dS threads: 2 warpgroups, each takes 32 of the 64 keys
 constexpr int kQB = 8;              // queries per batch (x 16 heads = 128 MMA rows)
 constexpr int kMeta = 6;            // batch metadata ring depth
 constexpr uint32_t kTmemCols = 512;
@@ -509,20 +510,20 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       mbar_init(&sm.b_full[i], 1);
       mbar_init(&sm.b_empty[i], 1);
       mbar_init(&sm.sdp_full[i], 1);
-      mbar_init(&sm.sdp_empty[i], 128);
+      mbar_init(&sm.sdp_empty[i], kWG);
       mbar_init(&sm.acc_full[i], 1);
-      mbar_init(&sm.acc_empty[i], 128);
+      mbar_init(&sm.acc_empty[i], kWG);
     }
     for (int i = 0; i < kMeta; ++i) {
       mbar_init(&sm.meta_full[i], 1);
-      mbar_init(&sm.meta_empty[i], 1 + 128);   // TMA thread + P/dS threads
+      mbar_init(&sm.meta_empty[i], 1 + kWG);   // TMA thread + P/dS threads
     }
     mbar_init(&sm.kv_full, 1);
     mbar_init(&sm.kv_empty, 1);
-    mbar_init(&sm.pds_full, 128);
+    mbar_init(&sm.pds_full, kWG);
     mbar_init(&sm.pds_empty, 1);
     // consumers of a job descriptor: MMA thread, TMA thread, P/dS threads
-    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 2 + 128); }
+    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 2 + kWG); }
     fence_barrier_init();
   }
   // padded head rows (G..15 of every query) stay zero
@@ -535,7 +536,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
     tmem_alloc(&sm.tmem_base, kTmemCols);
     tmem_relinquish();
   }
-  if (warp == 6 && lane == 0) {
+  if (warp == 10 && lane == 0) {
     prefetch_tmap(&tmq);
     prefetch_tmap(&tmdo);
     prefetch_tmap(&tmk);
@@ -634,7 +635,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         mbar_arrive(&sm.jd_full[js]);
       }
     }
-  } else if (warp == 6) {
+  } else if (warp == 10) {
     // ============================================================ TMA loads
     if (lane == 0) {
       int job = 0, gb = 0;
@@ -753,9 +754,13 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       if (ok && has_pend) issue_acc(pend);
     }
   } else {
-    // ============================================================ P/dS and epilogue (warps 2-5)
+    // ============================================================ P/dS and epilogue (warps 2-9)
+    // thread = TMEM lane (row = (query j, head h)); warpgroup wg takes keys
+    // 32*wg .. 32*wg+31 of the block (columns of S/dP, 64-byte halves of the
+    // P/dS rows); in the epilogue thread = dim and wg takes the same keys.
+    const int wg = (warp - 2) >> 2;
     const int wq = warp & 3;
-    const int lrow = wq * 32 + lane;        // TMEM lane: (query j, head h) row, or dim in the epilogue
+    const int lrow = wq * 32 + lane;
     const int jq = lrow >> 4, h = lrow & 15;
     const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
     const float c2 = p.scale * kLog2e;
@@ -769,6 +774,8 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       if (d.flags & kSentinel) break;
       const int ab = job & 1;
       const int nb = (d.n + kQB - 1) / kQB;
+      const int key_base = d.e * 64 + wg * 32;
+      const int kv_len = d.kv_len;
       for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
         const int s = gb & 1, slot = gb % kMeta;
         if (!(ok = wt(&sm.meta_full[slot], (gb / kMeta) & 1, st, 24))) break;
@@ -778,38 +785,35 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         const int pos = mt.pos[jq];
         const bool rvalid = lse2 != -INFINITY;
         mbar_arrive(&sm.meta_empty[slot]);
+        // keys of this warpgroup valid for this row: key_base + i < lim
+        int lim = rvalid ? min(kv_len, p.causal ? pos + 1 : kv_len) - key_base : 0;
         if (!(ok = wt(&sm.sdp_full[s], (gb >> 1) & 1, st, 21))) break;
         tc_fence_after();
-        uint32_t pk[32], dk[32];
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          float sv[32], dp[32];
-          const uint32_t col = tl + kColSdP + s * 128 + half * 32;
-          tmem_ld16(col, *reinterpret_cast<float(*)[16]>(&sv[0]));
-          tmem_ld16(col + 16, *reinterpret_cast<float(*)[16]>(&sv[16]));
-          tmem_ld16(col + 64, *reinterpret_cast<float(*)[16]>(&dp[0]));
-          tmem_ld16(col + 80, *reinterpret_cast<float(*)[16]>(&dp[16]));
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const int key0 = d.e * 64 + half * 32 + i;
-            const bool v0 = rvalid && key0 < d.kv_len && (!p.causal || key0 <= pos);
-            const bool v1 = rvalid && key0 + 1 < d.kv_len && (!p.causal || key0 + 1 <= pos);
-            const float p0 = v0 ? exp2f(sv[i] * c2 - lse2) : 0.f;
-            const float p1 = v1 ? exp2f(sv[i + 1] * c2 - lse2) : 0.f;
-            pk[half * 16 + i / 2] = pack_bf16x2(p0, p1);
-            dk[half * 16 + i / 2] = pack_bf16x2(p0 * (dp[i] - dl), p1 * (dp[i + 1] - dl));
-          }
-        }
+        float sv[32], dp[32];
+        const uint32_t col = tl + kColSdP + s * 128 + wg * 32;
+        tmem_ld16(col, *reinterpret_cast<float(*)[16]>(&sv[0]));
+        tmem_ld16(col + 16, *reinterpret_cast<float(*)[16]>(&sv[16]));
+        tmem_ld16(col + 64, *reinterpret_cast<float(*)[16]>(&dp[0]));
+        tmem_ld16(col + 80, *reinterpret_cast<float(*)[16]>(&dp[16]));
+        tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(&sm.sdp_empty[s]);
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = i < lim ? ex2(sv[i] * c2 - lse2) : 0.f;
+          const float p1 = i + 1 < lim ? ex2(sv[i + 1] * c2 - lse2) : 0.f;
+          pk[i / 2] = pack_bf16x2(p0, p1);
+          dk[i / 2] = pack_bf16x2(p0 * (dp[i] - dl), p1 * (dp[i + 1] - dl));
+        }
         if (!(ok = wt(&sm.pds_empty, (gb & 1) ^ 1, st, 22))) break;
-        // row lrow: 64 keys = 8 chunks of 16 bytes, 128B swizzle (chunk ^= row & 7)
+        // row lrow: 64 keys = 8 chunks of 16 bytes, 128B swizzle (chunk ^= row & 7);
+        // this warpgroup writes chunks 4*wg .. 4*wg+3
         const uint32_t prow = smem_u32(&sm.pbuf[0]) + lrow * 128;
         const uint32_t drow = smem_u32(&sm.dsbuf[0]) + lrow * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t off = (uint32_t)((c ^ (lrow & 7)) * 16);
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t off = (uint32_t)(((wg * 4 + c) ^ (lrow & 7)) * 16);
           st_shared_v4(prow + off, pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
           st_shared_v4(drow + off, dk[c * 4], dk[c * 4 + 1], dk[c * 4 + 2], dk[c * 4 + 3]);
         }
@@ -817,18 +821,18 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         mbar_arrive(&sm.pds_full);
       }
       if (!ok) break;
-      // epilogue: thread = dim; 64 keys of dV^T and dK^T
+      // epilogue: thread = dim; this warpgroup's 32 keys of dV^T and dK^T
       if (!(ok = wt(&sm.acc_full[ab], (job >> 1) & 1, st, 23))) break;
       tc_fence_after();
       const bool has = nb > 0;
       __nv_bfloat16* dkp = reinterpret_cast<__nv_bfloat16*>(p.dk) + d.b * p.dk_sb + (int64_t)d.hk * p.dk_sh + lrow;
       __nv_bfloat16* dvp = reinterpret_cast<__nv_bfloat16*>(p.dv) + d.b * p.dv_sb + (int64_t)d.hk * p.dv_sh + lrow;
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
+      for (int q2 = 0; q2 < 2; ++q2) {
         float vv[16], kv[16];
         if (has) {
-          tmem_ld16(tl + kColAcc + ab * 128 + q4 * 16, vv);
-          tmem_ld16(tl + kColAcc + ab * 128 + 64 + q4 * 16, kv);
+          tmem_ld16(tl + kColAcc + ab * 128 + wg * 32 + q2 * 16, vv);
+          tmem_ld16(tl + kColAcc + ab * 128 + 64 + wg * 32 + q2 * 16, kv);
           tmem_ld_wait();
         } else {
 #pragma unroll
@@ -837,8 +841,8 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         if (lrow < D) {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int key = d.e * 64 + q4 * 16 + i;
-            if (key < d.kv_len) {
+            const int key = key_base + q2 * 16 + i;
+            if (key < kv_len) {
               const int64_t t = (int64_t)d.kv0 + key;
               if (shared_kv) {
                 dkp[t * p.dk_st] = f2bf(kv[i] * p.scale + vv[i]);

@@ -186,6 +186,14 @@ __host__ __device__ constexpr uint32_t idesc_bf16(uint32_t M, uint32_t N, bool a
          | ((M >> 4) << 24);                       // M / 16
 }
 
+// 2^x with the hardware approximation (one MUFU op; results below 2^-126 flush
+// to zero, which only affects probabilities far below bf16 resolution).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

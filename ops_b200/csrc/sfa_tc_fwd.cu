@@ -440,7 +440,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
           float pr[16];
 #pragma unroll
           for (int h = 0; h < 16; ++h) {
-            pr[h] = valid[i] ? exp2f(s[i][h] - m[h]) : 0.f;
+            pr[h] = valid[i] ? ex2(s[i][h] - m[h]) : 0.f;
             l[h] += pr[h];
           }
           // row = key within the segment; 32-byte rows, 32B swizzle (16-byte
