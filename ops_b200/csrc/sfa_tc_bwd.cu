@@ -45,6 +45,8 @@ constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColSdP = 0;  // kR x (16 S + 16 dP)
 constexpr uint32_t kColDQ = 128; // 2 x 16
 
+static_assert(kR >= 4, "stage-reuse waits on ds_empty/sdp_full assume kR > KS and kR > VS + 1");
+
 struct JobDesc {
   int row, hk, b, tq, kv0, kv_len, pos, nblk, flags;
   int blocks[kMaxTopk];
@@ -64,7 +66,7 @@ struct Smem {
   alignas(1024) uint8_t dO[2][kQBytes];
   alignas(1024) uint8_t ds[kR][128 * kNH * 2];
   JobDesc jd[kJD];
-  uint64_t k_full[kKS], k_empty[kKS], v_full[kVS], v_empty[kVS];
+  uint64_t k_full[kKS], v_full[kVS];
   uint64_t qdo_full[2], qdo_empty[2];
   uint64_t sdp_full[kR], sdp_empty[kR], ds_full[kR], ds_empty[kR];
   uint64_t dq_full[2], dq_empty[2];
@@ -99,8 +101,8 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
   int32_t* st = args.status;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < KS; ++i) { mbar_init(&sm.k_full[i], 1); mbar_init(&sm.k_empty[i], 1); }
-    for (int i = 0; i < VS; ++i) { mbar_init(&sm.v_full[i], 1); mbar_init(&sm.v_empty[i], 1); }
+    for (int i = 0; i < KS; ++i) mbar_init(&sm.k_full[i], 1);
+    for (int i = 0; i < VS; ++i) mbar_init(&sm.v_full[i], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.qdo_full[i], 1);
       mbar_init(&sm.qdo_empty[i], 1);
@@ -207,9 +209,13 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
         }
         for (int c = 0; c < (n + 1) / 2 && ok; ++c, ++g) {
           const int ks = g % KS, vs = g % VS;
-          if (!(ok = wt(&sm.k_empty[ks], ((g / KS) & 1) ^ 1, st, 3))) break;
+          // a K stage is free once the dQ MMAs of tile g-KS retired (the same
+          // commit that frees its dS slot); a V stage once dP of tile g-VS retired
+          // (the commit that hands S/dP to the softmax warps).  Neither barrier
+          // can complete its next phase before this thread loads tile g+1.
+          if (g >= KS && !(ok = wt(&sm.ds_empty[(g - KS) % kR], ((g - KS) / kR) & 1, st, 3))) break;
           load_tile(&tmk, sm.kst[ks], &sm.k_full[ks], d, c);
-          if (!(ok = wt(&sm.v_empty[vs], ((g / VS) & 1) ^ 1, st, 4))) break;
+          if (g >= VS && !(ok = wt(&sm.sdp_full[(g - VS) % kR], ((g - VS) / kR) & 1, st, 4))) break;
           load_tile(&tmv, sm.vst[vs], &sm.v_full[vs], d, c);
         }
       }
@@ -245,8 +251,7 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
         for (int kk = 0; kk < 8; ++kk)
           mma_bf16_ss(dcol, a0 + (uint64_t)(kk * 2048 >> 4), b0 + (uint64_t)(kk * 16 * (kNH * 2) >> 4), id_dq,
                       (pd.first && kk == 0) ? 0u : 1u);
-        mma_commit(&sm.k_empty[pd.ks]);
-        mma_commit(&sm.ds_empty[pd.slot]);
+        mma_commit(&sm.ds_empty[pd.slot]);   // also frees K stage pd.ks
         if (pd.last) {
           mma_commit(&sm.dq_full[pd.ib]);
           mbar_arrive(&sm.jd_empty[pd.js % kJD]);
@@ -293,8 +298,7 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
             const uint64_t oo = (uint64_t)(((k >> 2) * (kNH * 128) + (k & 3) * 32) >> 4);
             mma_bf16_ss(scol + 16, vdesc + vo, odesc + oo, id_sdp, k != 0);
           }
-          mma_commit(&sm.v_empty[vs]);
-          mma_commit(&sm.sdp_full[slot]);
+          mma_commit(&sm.sdp_full[slot]);   // also frees V stage vs
           if (c == nch - 1) mma_commit(&sm.qdo_empty[ib]);
           if (has_pend && !(ok = issue_dq(pend))) break;
           pend = Pending{g, ks, slot, ib, job, c == 0, c == nch - 1};
