@@ -18,15 +18,15 @@
 // producer warps, and the softmax runs on two warpgroups with S held in
 // registers (one TMEM read per score).
 //
-// Warp roles (608 threads, one persistent CTA per SM):
+// Warp roles (352 threads, one persistent CTA per SM):
 //   warp 0      K producer: compacts the row's valid block ids into a job
 //               descriptor, loads Q, gathers 64-key K blocks (4-D TMA box per
 //               block and 64-dim slab, 128B swizzle) into 128-key stages;
-//   warp 18     V producer: the same gathers for V, one job behind;
+//   warp 10     V producer: the same gathers for V, one job behind;
 //   warp 1      MMA issuer (one thread): S^T for job j+1, then PV for job j;
-//   warps 2-17  four softmax warpgroups (thread = key lane of a 128-key tile,
-//               warpgroup w takes tiles 2w, 2w+1) and the epilogue
-//               (thread = dim lane of O^T, warpgroup w takes heads 4w..4w+3):
+//   warps 2-9   two softmax warpgroups (thread = key lane of a 128-key tile,
+//               warpgroup w takes tiles 4w..4w+3) and the epilogue
+//               (thread = dim lane of O^T, warpgroup w takes heads 8w..8w+7):
 //               writes o (bf16) and lse (fp32, natural log).
 // Every wait is bounded (~2 s); on expiry the kernel records a status word and
 // returns.
@@ -44,11 +44,8 @@ using namespace tc;
 
 namespace fwd {
 
-constexpr int kThreads = 608;
-constexpr int kSoftmaxWarps = 16;
-constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
-constexpr int kTilesPerWG = 2;      // 128-key tiles per softmax warpgroup (4 groups x 2 = 8 tiles)
-constexpr int kHeadsPerWG = 4;      // epilogue heads per softmax warpgroup
+constexpr int kThreads = 352;
+constexpr int kSoftmaxThreads = 256;
 constexpr int kSegBlocks = 16;      // 64-key blocks per segment (1024 keys, 8 tiles)
 constexpr int kJD = 4;              // job descriptor ring depth
 constexpr int kNH = 16;             // MMA N: query heads padded to 16
@@ -76,8 +73,8 @@ struct Smem {
   alignas(1024) uint8_t q[2][kQBytes];
   alignas(1024) uint8_t p[kPBytes];
   JobDesc jd[kJD];
-  alignas(16) float red[kSoftmaxWarps + 1][16];
-  alignas(16) float redl[kSoftmaxWarps + 1][16];
+  alignas(16) float red[9][16];
+  alignas(16) float redl[9][16];
   alignas(16) float ml[2][2][16];
   int plist[kMaxTopk];
   uint64_t k_full[kKS], k_empty[kKS], v_full[kVS], v_empty[kVS];
@@ -128,9 +125,8 @@ __device__ __forceinline__ float warp_reduce16(const float (&v)[16], int lane) {
   return op(d, __shfl_xor_sync(0xffffffffu, d, 1));
 }
 
-// Reduce over the softmax threads; every thread gets all 16 results.
-// buf holds the warps' partials in rows 0..kSoftmaxWarps-1 and the final
-// values in row kSoftmaxWarps.
+// Reduce over the 256 softmax threads; every thread gets all 16 results.
+// buf holds the 8 warps' partials in rows 0..7 and the final values in row 8.
 template <bool kMax>
 __device__ __forceinline__ void block_reduce16(float (&v)[16], float (*buf)[16], int w8, int lane, int tid) {
   const float r = warp_reduce16<kMax>(v, lane);
@@ -139,13 +135,13 @@ __device__ __forceinline__ void block_reduce16(float (&v)[16], float (*buf)[16],
   if (tid < 16) {
     float a = buf[0][tid];
 #pragma unroll
-    for (int w = 1; w < kSoftmaxWarps; ++w) a = kMax ? fmaxf(a, buf[w][tid]) : a + buf[w][tid];
-    buf[kSoftmaxWarps][tid] = a;
+    for (int w = 1; w < 8; ++w) a = kMax ? fmaxf(a, buf[w][tid]) : a + buf[w][tid];
+    buf[8][tid] = a;
   }
   named_barrier(1, kSoftmaxThreads);
 #pragma unroll
   for (int h4 = 0; h4 < 4; ++h4) {
-    const float4 x = reinterpret_cast<const float4*>(buf[kSoftmaxWarps])[h4];
+    const float4 x = reinterpret_cast<const float4*>(buf[8])[h4];
     v[4 * h4 + 0] = x.x;
     v[4 * h4 + 1] = x.y;
     v[4 * h4 + 2] = x.z;
@@ -288,7 +284,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
         mbar_arrive(&sm.jd_full[js]);
       }
     }
-  } else if (warp == kSoftmaxWarps + 2) {
+  } else if (warp == 10) {
     // ============================================================ V producer
     if (lane == 0) {
       int job = 0, use = 0;
@@ -382,16 +378,16 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
     }
   } else {
     // ============================================================ softmax / epilogue
-    const int w8 = warp - 2;             // 0..15
-    const int wg = w8 >> 2;              // warpgroup 0..3
+    const int w8 = warp - 2;             // 0..7
+    const int wg = w8 >> 2;              // warpgroup 0 / 1
     const int wq = warp & 3;             // TMEM lane quadrant of this warp
-    const int tid = threadIdx.x - 64;    // 0..511
+    const int tid = threadIdx.x - 64;    // 0..255
     const int lrow = wq * 32 + lane;     // TMEM lane: key (softmax) or dim (epilogue)
     const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
     const float c2 = p.scale * kLog2e;
-    float acc[kHeadsPerWG], mrun[kHeadsPerWG], lrun[kHeadsPerWG];   // epilogue state, heads 4*wg..4*wg+3
+    float acc[8], mrun[8], lrun[8];      // epilogue state for heads 8*wg .. 8*wg+7
 #pragma unroll
-    for (int h = 0; h < kHeadsPerWG; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
+    for (int h = 0; h < 8; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
     bool ok = true;
     auto softmax = [&](int j) -> bool {
       const JobDesc& d = sm.jd[j % kJD];
@@ -400,11 +396,11 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       tc_fence_after();
       const int nch = (d.nblk + 1) / 2;
       const uint32_t ts = tl + kColS + sb * 128;
-      float s[kTilesPerWG][16];
-      bool valid[kTilesPerWG];
+      float s[4][16];
+      bool valid[4];
 #pragma unroll
-      for (int i = 0; i < kTilesPerWG; ++i) {
-        const int c = wg * kTilesPerWG + i;
+      for (int i = 0; i < 4; ++i) {
+        const int c = wg * 4 + i;
         if (c < nch) tmem_ld16(ts + c * kNH, s[i]);
       }
       tmem_ld_wait();
@@ -414,8 +410,8 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
 #pragma unroll
       for (int h = 0; h < 16; ++h) m[h] = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < kTilesPerWG; ++i) {
-        const int c = wg * kTilesPerWG + i;
+      for (int i = 0; i < 4; ++i) {
+        const int c = wg * 4 + i;
         const int bi = 2 * c + (lrow >> 6);
         bool v = c < nch && bi < d.nblk;
         if (v) {
@@ -438,8 +434,8 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       if (!wt(&sm.p_empty, (j & 1) ^ 1, st, 21)) return false;
       const uint32_t pbase = smem_u32(&sm.p[0]);
 #pragma unroll
-      for (int i = 0; i < kTilesPerWG; ++i) {
-        const int c = wg * kTilesPerWG + i;
+      for (int i = 0; i < 4; ++i) {
+        const int c = wg * 4 + i;
         if (c < nch) {
           float pr[16];
 #pragma unroll
@@ -473,18 +469,18 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       const int sb = jj & 1;
       if (d.flags & kFirst) {
 #pragma unroll
-        for (int h = 0; h < kHeadsPerWG; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
+        for (int h = 0; h < 8; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
       }
       if (!wt(&sm.o_full[sb], (jj >> 1) & 1, st, 22)) return false;
       tc_fence_after();
       if (d.nblk > 0) {
         float o[16];
-        tmem_ld16(tl + kColO + sb * kNH, o);   // all 16 heads; this warpgroup keeps 4
+        tmem_ld16(tl + kColO + sb * kNH, o);   // all 16 heads; this warpgroup keeps 8
         tmem_ld_wait();
 #pragma unroll
-        for (int h = 0; h < kHeadsPerWG; ++h) {
-          const int hh = wg * kHeadsPerWG + h;
-          const float ov = wg == 0 ? o[h] : wg == 1 ? o[4 + h] : wg == 2 ? o[8 + h] : o[12 + h];
+        for (int h = 0; h < 8; ++h) {
+          const int hh = wg * 8 + h;
+          const float ov = wg ? o[8 + h] : o[h];
           const float ms = sm.ml[sb][0][hh], ls = sm.ml[sb][1][hh];
           const float M = fmaxf(mrun[h], ms);
           const float a = exp2f(mrun[h] - M), bb = exp2f(ms - M);
@@ -500,8 +496,8 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
                            (int64_t)(d.hk * G) * p.o_sh;
         float* lse = p.lse + d.b * p.l_sb + (int64_t)d.tq * p.l_st + (int64_t)(d.hk * G) * p.l_sh;
 #pragma unroll
-        for (int h = 0; h < kHeadsPerWG; ++h) {
-          const int hh = wg * kHeadsPerWG + h;
+        for (int h = 0; h < 8; ++h) {
+          const int hh = wg * 8 + h;
           if (hh < G) {
             const float s2 = p.attn_sink ? __ldg(p.attn_sink + d.hk * G + hh) * kLog2e : -INFINITY;
             const float M = fmaxf(mrun[h], s2);
