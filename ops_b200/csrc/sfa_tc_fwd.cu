@@ -483,7 +483,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
           const float ov = wg ? o[8 + h] : o[h];
           const float ms = sm.ml[sb][0][hh], ls = sm.ml[sb][1][hh];
           const float M = fmaxf(mrun[h], ms);
-          const float a = exp2f(mrun[h] - M), bb = exp2f(ms - M);
+          const float a = ex2(mrun[h] - M), bb = ex2(ms - M);
           acc[h] = acc[h] * a + ov * bb;
           lrun[h] = lrun[h] * a + ls * bb;
           mrun[h] = M;
@@ -503,9 +503,10 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
             const float M = fmaxf(mrun[h], s2);
             float outv = 0.f, lv = -INFINITY;
             if (M != -INFINITY) {
-              const float lt = lrun[h] * exp2f(mrun[h] - M) + exp2f(s2 - M);
-              outv = acc[h] * exp2f(mrun[h] - M) / lt;
-              lv = (M + log2f(lt)) * kLn2;
+              const float w = ex2(mrun[h] - M);
+              const float lt = lrun[h] * w + ex2(s2 - M);
+              outv = __fdividef(acc[h] * w, lt);
+              lv = (M + lg2(lt)) * kLn2;
             }
             if (lrow < D) o[hh * p.o_sh + lrow] = f2bf(outv);
             if (lrow == h) lse[hh * p.l_sh] = lv;
