@@ -74,13 +74,15 @@ struct Smem {
   alignas(1024) uint8_t p[kPBytes];
   JobDesc jd[kJD];
   alignas(16) float red[9][16];
-  alignas(16) float redl[9][16];
-  alignas(16) float ml[2][2][16];
+  alignas(16) float redl[2][8][16];   // per-warp partial row sums of jobs j (j & 1)
+  alignas(16) float ml[2][16];        // per-job row max (j & 1)
   int plist[kMaxTopk];
   uint64_t k_full[kKS], k_empty[kKS], v_full[kVS], v_empty[kVS];
   uint64_t q_full[2], q_empty[2];
-  uint64_t s_full[2], s_empty[2], p_full, p_empty, o_full[2], o_empty[2];
+  uint64_t s_full[2], s_empty[2], o_full[2], o_empty[2];
+  uint64_t p_full[2], p_empty[2];     // P tiles 0-3 (warpgroup 0) and 4-7 (warpgroup 1)
   uint64_t jd_full[kJD], jd_empty[kJD];
+  uint64_t sm_bar;                    // barrier among the softmax threads
   uint32_t tmem_base;
 };
 
@@ -125,20 +127,30 @@ __device__ __forceinline__ float warp_reduce16(const float (&v)[16], int lane) {
   return op(d, __shfl_xor_sync(0xffffffffu, d, 1));
 }
 
+// Barrier among the softmax threads on an mbarrier, with the same bounded wait
+// as every other hand-off (a bar.sync could not give up if a peer stopped).
+// `use` counts this thread's barrier uses; all softmax threads make the same
+// sequence of uses.
+__device__ __forceinline__ bool softmax_barrier(uint64_t* bar, uint32_t& use, int32_t* status) {
+  mbar_arrive(bar);
+  return wt(bar, (use++) & 1, status, 30);
+}
+
 // Reduce over the 256 softmax threads; every thread gets all 16 results.
 // buf holds the 8 warps' partials in rows 0..7 and the final values in row 8.
 template <bool kMax>
-__device__ __forceinline__ void block_reduce16(float (&v)[16], float (*buf)[16], int w8, int lane, int tid) {
+__device__ __forceinline__ bool block_reduce16(float (&v)[16], float (*buf)[16], int w8, int lane, int tid,
+                                               uint64_t* bar, uint32_t& use, int32_t* status) {
   const float r = warp_reduce16<kMax>(v, lane);
   if ((lane & 1) == 0) buf[w8][(lane >> 1) & 15] = r;
-  named_barrier(1, kSoftmaxThreads);
+  if (!softmax_barrier(bar, use, status)) return false;
   if (tid < 16) {
     float a = buf[0][tid];
 #pragma unroll
     for (int w = 1; w < 8; ++w) a = kMax ? fmaxf(a, buf[w][tid]) : a + buf[w][tid];
     buf[8][tid] = a;
   }
-  named_barrier(1, kSoftmaxThreads);
+  if (!softmax_barrier(bar, use, status)) return false;
 #pragma unroll
   for (int h4 = 0; h4 < 4; ++h4) {
     const float4 x = reinterpret_cast<const float4*>(buf[8])[h4];
@@ -147,6 +159,7 @@ __device__ __forceinline__ void block_reduce16(float (&v)[16], float (*buf)[16],
     v[4 * h4 + 2] = x.z;
     v[4 * h4 + 3] = x.w;
   }
+  return true;
 }
 
 template <int D>
@@ -174,8 +187,11 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       mbar_init(&sm.o_full[i], 1);
       mbar_init(&sm.o_empty[i], kSoftmaxThreads);
     }
-    mbar_init(&sm.p_full, kSoftmaxThreads);
-    mbar_init(&sm.p_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.p_full[i], kSoftmaxThreads / 2);
+      mbar_init(&sm.p_empty[i], 1);
+    }
+    mbar_init(&sm.sm_bar, kSoftmaxThreads);
     // consumers of a job descriptor: MMA thread, V producer, softmax threads
     for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 2 + kSoftmaxThreads); }
     fence_barrier_init();
@@ -316,26 +332,32 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       auto pv = [&](int jj) -> bool {
         const JobDesc& d = sm.jd[jj % kJD];
         const int sb = jj & 1;
-        if (!wt(&sm.p_full, jj & 1, st, 10)) return false;
         if (!wt(&sm.o_empty[sb], ((jj >> 1) & 1) ^ 1, st, 11)) return false;
-        tc_fence_after();
         const uint32_t dcol = tmem + kColO + sb * kNH;
         const uint64_t pdesc = smem_desc(smem_u32(&sm.p[0]), 0, 256, kSw32);
         const int nch = (d.nblk + 1) / 2;
-        for (int c = 0; c < nch; ++c, ++vuse) {
-          const int s = vuse % VS;
-          if (!wt(&sm.v_full[s], (vuse / VS) & 1, st, 12)) return false;
-          tc_fence_after();
-          // descriptors advance by adding the byte offset / 16 to the start-address field
-          const uint64_t a0 = smem_desc(smem_u32(&sm.vst[s][0]), lbo_v, 1024, kSw128);
-          const uint64_t b0 = pdesc + (uint64_t)(c * 128 * (kNH * 2) >> 4);
+        for (int c = 0; c < 8; ++c) {
+          // tiles 0-3 come from softmax warpgroup 0, tiles 4-7 from group 1
+          if (c == 0 || c == 4) {
+            if (!wt(&sm.p_full[c >> 2], jj & 1, st, 10)) return false;
+            tc_fence_after();
+          }
+          if (c < nch) {
+            const int s = vuse % VS;
+            if (!wt(&sm.v_full[s], (vuse / VS) & 1, st, 12)) return false;
+            tc_fence_after();
+            // descriptors advance by adding the byte offset / 16 to the start-address field
+            const uint64_t a0 = smem_desc(smem_u32(&sm.vst[s][0]), lbo_v, 1024, kSw128);
+            const uint64_t b0 = pdesc + (uint64_t)(c * 128 * (kNH * 2) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_bf16_ss(dcol, a0 + (uint64_t)(kk * 2048 >> 4), b0 + (uint64_t)(kk * 16 * (kNH * 2) >> 4), id_o,
-                        (c | kk) != 0);
-          mma_commit(&sm.v_empty[s]);
+            for (int kk = 0; kk < 8; ++kk)
+              mma_bf16_ss(dcol, a0 + (uint64_t)(kk * 2048 >> 4), b0 + (uint64_t)(kk * 16 * (kNH * 2) >> 4), id_o,
+                          (c | kk) != 0);
+            mma_commit(&sm.v_empty[s]);
+            ++vuse;
+          }
+          if (c == 3 || c == 7) mma_commit(&sm.p_empty[c >> 2]);
         }
-        mma_commit(&sm.p_empty);
         mma_commit(&sm.o_full[sb]);
         mbar_arrive(&sm.jd_empty[jj % kJD]);
         return true;
@@ -385,6 +407,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
     const int lrow = wq * 32 + lane;     // TMEM lane: key (softmax) or dim (epilogue)
     const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
     const float c2 = p.scale * kLog2e;
+    uint32_t bar_use = 0;
     float acc[8], mrun[8], lrun[8];      // epilogue state for heads 8*wg .. 8*wg+7
 #pragma unroll
     for (int h = 0; h < 8; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
@@ -427,11 +450,17 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
           }
         }
       }
-      block_reduce16<true>(m, sm.red, w8, lane, tid);
+      if (!block_reduce16<true>(m, sm.red, w8, lane, tid, &sm.sm_bar, bar_use, st)) return false;
+      if (tid < 16) {
+#pragma unroll
+        for (int h = 0; h < 16; ++h)
+          if (h == tid) sm.ml[sb][h] = m[h];
+      }
       float l[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) l[h] = 0.f;
-      if (!wt(&sm.p_empty, (j & 1) ^ 1, st, 21)) return false;
+      // this warpgroup's half of the P buffer is free once PV(j-1) read it
+      if (!wt(&sm.p_empty[wg], (j & 1) ^ 1, st, 21)) return false;
       const uint32_t pbase = smem_u32(&sm.p[0]);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -455,13 +484,11 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
         }
       }
       fence_proxy_async_smem();
-      mbar_arrive(&sm.p_full);
-      block_reduce16<false>(l, sm.redl, w8, lane, tid);
-      if (tid < 16) {
-#pragma unroll
-        for (int h = 0; h < 16; ++h)
-          if (h == tid) { sm.ml[sb][0][h] = m[h]; sm.ml[sb][1][h] = l[h]; }
-      }
+      mbar_arrive(&sm.p_full[wg]);
+      // row sums: per-warp partials only; the epilogue of this job (after the
+      // next job's max reduction, whose barriers order these writes) adds them
+      const float lw = warp_reduce16<false>(l, lane);
+      if ((lane & 1) == 0) sm.redl[sb][w8][(lane >> 1) & 15] = lw;
       return true;
     };
     auto epilogue = [&](int jj) -> bool {
@@ -481,7 +508,10 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
         for (int h = 0; h < 8; ++h) {
           const int hh = wg * 8 + h;
           const float ov = wg ? o[8 + h] : o[h];
-          const float ms = sm.ml[sb][0][hh], ls = sm.ml[sb][1][hh];
+          const float ms = sm.ml[sb][hh];
+          float ls = 0.f;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) ls += sm.redl[sb][w][hh];
           const float M = fmaxf(mrun[h], ms);
           const float a = ex2(mrun[h] - M), bb = ex2(ms - M);
           acc[h] = acc[h] * a + ov * bb;
@@ -525,7 +555,9 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       if (job > 0 && !(ok = epilogue(job - 1))) break;
       ++job;
     }
-    if (ok && job > 0) epilogue(job - 1);
+    // the last job's row-sum partials and max were written by other warps with
+    // no later reduction to order them: one more barrier before its epilogue
+    if (ok && job > 0 && softmax_barrier(&sm.sm_bar, bar_use, st)) epilogue(job - 1);
   }
 
   tc_fence_before();
