@@ -87,6 +87,12 @@ __device__ __forceinline__ bool wt(uint64_t* bar, uint32_t parity, int32_t* stat
   return false;
 }
 
+// The same wait for a whole warp: every lane gets one verdict, so a warp that
+// gives up leaves its later warp-wide instructions together.
+__device__ __forceinline__ bool wtw(uint64_t* bar, uint32_t parity, int32_t* status, int site) {
+  return __all_sync(0xffffffffu, wt(bar, parity, status, site));
+}
+
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
 sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUtensorMap tmq,
@@ -107,15 +113,16 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
       mbar_init(&sm.qdo_full[i], 1);
       mbar_init(&sm.qdo_empty[i], 1);
       mbar_init(&sm.dq_full[i], 1);
-      mbar_init(&sm.dq_empty[i], 128);
+      mbar_init(&sm.dq_empty[i], 4);
     }
     for (int i = 0; i < kR; ++i) {
       mbar_init(&sm.sdp_full[i], 1);
-      mbar_init(&sm.sdp_empty[i], 128);
-      mbar_init(&sm.ds_full[i], 128);
+      mbar_init(&sm.sdp_empty[i], 4);
+      mbar_init(&sm.ds_full[i], 4);
       mbar_init(&sm.ds_empty[i], 1);
     }
-    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 1 + 128); }
+    // counts in warps for the 4 dS/epilogue warps (one arrival per warp)
+    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 1 + 4); }
     fence_barrier_init();
   }
   for (int i = threadIdx.x; i < 2 * Smem<D>::kQBytes / 16; i += kThreads) {
@@ -318,7 +325,7 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
     bool ok = true;
     while (ok) {
       const int js = job % kJD;
-      if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 20))) break;
+      if (!(ok = wtw(&sm.jd_full[js], (job / kJD) & 1, st, 20))) break;
       const JobDesc& d = sm.jd[js];
       if (d.flags & kSentinel) break;
       const int ib = job & 1;
@@ -333,14 +340,14 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
       const int nch = (d.nblk + 1) / 2;
       for (int c = 0; c < nch && ok; ++c, ++g) {
         const int slot = g % kR;
-        if (!(ok = wt(&sm.sdp_full[slot], (g / kR) & 1, st, 21))) break;
+        if (!(ok = wtw(&sm.sdp_full[slot], (g / kR) & 1, st, 21))) break;
         tc_fence_after();
         float s[16], dp[16];
         tmem_ld16(tl + kColSdP + slot * 32, s);
         tmem_ld16(tl + kColSdP + slot * 32 + 16, dp);
         tmem_ld_wait();
         tc_fence_before();
-        mbar_arrive(&sm.sdp_empty[slot]);
+        warp_arrive(&sm.sdp_empty[slot]);
         const int bi = 2 * c + (lrow >> 6);
         bool valid = bi < d.nblk;
         if (valid) {
@@ -353,7 +360,7 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
           const float pr = (valid && lse2[h] != -INFINITY) ? ex2(s[h] * c2 - lse2[h]) : 0.f;
           ds[h] = pr * (dp[h] - dl[h]);
         }
-        if (!(ok = wt(&sm.ds_empty[slot], ((g / kR) & 1) ^ 1, st, 22))) break;
+        if (!(ok = wtw(&sm.ds_empty[slot], ((g / kR) & 1) ^ 1, st, 22))) break;
         const uint32_t off = smem_u32(&sm.ds[slot][0]) + lrow * 32;
         const uint32_t sw = ((lrow >> 2) & 1) << 4;
         st_shared_v4(off + sw, pack_bf16x2(ds[0], ds[1]), pack_bf16x2(ds[2], ds[3]), pack_bf16x2(ds[4], ds[5]),
@@ -361,11 +368,11 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
         st_shared_v4(off + (16 - sw), pack_bf16x2(ds[8], ds[9]), pack_bf16x2(ds[10], ds[11]),
                      pack_bf16x2(ds[12], ds[13]), pack_bf16x2(ds[14], ds[15]));
         fence_proxy_async_smem();
-        mbar_arrive(&sm.ds_full[slot]);
+        warp_arrive(&sm.ds_full[slot]);
       }
       if (!ok) break;
       // epilogue: dq = scale * dQ^T (thread = dim)
-      if (!(ok = wt(&sm.dq_full[ib], (job >> 1) & 1, st, 23))) break;
+      if (!(ok = wtw(&sm.dq_full[ib], (job >> 1) & 1, st, 23))) break;
       tc_fence_after();
       float acc[16];
       if (nch > 0) {
@@ -376,7 +383,7 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
         for (int h = 0; h < 16; ++h) acc[h] = 0.f;
       }
       tc_fence_before();
-      mbar_arrive(&sm.dq_empty[ib]);
+      warp_arrive(&sm.dq_empty[ib]);
       if (lrow < D) {
         __nv_bfloat16* dqp = reinterpret_cast<__nv_bfloat16*>(p.dq) + d.b * p.dq_sb + (int64_t)d.tq * p.dq_st +
                              (int64_t)(d.hk * G) * p.dq_sh + lrow;
@@ -384,7 +391,7 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
         for (int h = 0; h < 16; ++h)
           if (h < G) dqp[h * p.dq_sh] = f2bf(acc[h] * p.scale);
       }
-      mbar_arrive(&sm.jd_empty[js]);
+      warp_arrive(&sm.jd_empty[js]);
       ++job;
     }
   }
@@ -497,6 +504,12 @@ __device__ __forceinline__ bool wt(uint64_t* bar, uint32_t parity, int32_t* stat
   return false;
 }
 
+// The same wait for a whole warp: every lane gets one verdict, so a warp that
+// gives up leaves its later warp-wide instructions together.
+__device__ __forceinline__ bool wtw(uint64_t* bar, uint32_t parity, int32_t* status, int site) {
+  return __all_sync(0xffffffffu, wt(bar, parity, status, site));
+}
+
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
 sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUtensorMap tmq,
@@ -514,20 +527,21 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       mbar_init(&sm.b_full[i], 1);
       mbar_init(&sm.b_empty[i], 1);
       mbar_init(&sm.sdp_full[i], 1);
-      mbar_init(&sm.sdp_empty[i], kWG);
+      mbar_init(&sm.sdp_empty[i], kWG / 32);
       mbar_init(&sm.acc_full[i], 1);
-      mbar_init(&sm.acc_empty[i], kWG);
+      mbar_init(&sm.acc_empty[i], kWG / 32);
     }
+    // counts in warps for the P/dS warps (one arrival per warp)
     for (int i = 0; i < kMeta; ++i) {
       mbar_init(&sm.meta_full[i], 1);
-      mbar_init(&sm.meta_empty[i], 1 + kWG);   // TMA thread + P/dS threads
+      mbar_init(&sm.meta_empty[i], 1 + kWG / 32);   // TMA thread + P/dS warps
     }
     mbar_init(&sm.kv_full, 1);
     mbar_init(&sm.kv_empty, 1);
-    mbar_init(&sm.pds_full, kWG);
+    mbar_init(&sm.pds_full, kWG / 32);
     mbar_init(&sm.pds_empty, 1);
-    // consumers of a job descriptor: MMA thread, TMA thread, P/dS threads
-    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 2 + kWG); }
+    // consumers of a job descriptor: MMA thread, TMA thread, P/dS warps
+    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 2 + kWG / 32); }
     fence_barrier_init();
   }
   // padded head rows (G..15 of every query) stay zero
@@ -773,7 +787,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
     bool ok = true;
     while (ok) {
       const int js = job % kJD;
-      if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 20))) break;
+      if (!(ok = wtw(&sm.jd_full[js], (job / kJD) & 1, st, 20))) break;
       const JobDesc& d = sm.jd[js];
       if (d.flags & kSentinel) break;
       const int ab = job & 1;
@@ -782,16 +796,16 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       const int kv_len = d.kv_len;
       for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
         const int s = gb & 1, slot = gb % kMeta;
-        if (!(ok = wt(&sm.meta_full[slot], (gb / kMeta) & 1, st, 24))) break;
+        if (!(ok = wtw(&sm.meta_full[slot], (gb / kMeta) & 1, st, 24))) break;
         const BatchMeta& mt = sm.meta[slot];
         const float lse2 = mt.lse2[jq][h];
         const float dl = mt.dl[jq][h];
         const int pos = mt.pos[jq];
         const bool rvalid = lse2 != -INFINITY;
-        mbar_arrive(&sm.meta_empty[slot]);
+        warp_arrive(&sm.meta_empty[slot]);
         // keys of this warpgroup valid for this row: key_base + i < lim
         int lim = rvalid ? min(kv_len, p.causal ? pos + 1 : kv_len) - key_base : 0;
-        if (!(ok = wt(&sm.sdp_full[s], (gb >> 1) & 1, st, 21))) break;
+        if (!(ok = wtw(&sm.sdp_full[s], (gb >> 1) & 1, st, 21))) break;
         tc_fence_after();
         float sv[32], dp[32];
         const uint32_t col = tl + kColSdP + s * 128 + wg * 32;
@@ -801,7 +815,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         tmem_ld16(col + 80, *reinterpret_cast<float(*)[16]>(&dp[16]));
         tmem_ld_wait();
         tc_fence_before();
-        mbar_arrive(&sm.sdp_empty[s]);
+        warp_arrive(&sm.sdp_empty[s]);
         uint32_t pk[16], dk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
@@ -810,7 +824,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
           pk[i / 2] = pack_bf16x2(p0, p1);
           dk[i / 2] = pack_bf16x2(p0 * (dp[i] - dl), p1 * (dp[i + 1] - dl));
         }
-        if (!(ok = wt(&sm.pds_empty, (gb & 1) ^ 1, st, 22))) break;
+        if (!(ok = wtw(&sm.pds_empty, (gb & 1) ^ 1, st, 22))) break;
         // row lrow: 64 keys = 8 chunks of 16 bytes, 128B swizzle (chunk ^= row & 7);
         // this warpgroup writes chunks 4*wg .. 4*wg+3
         const uint32_t prow = smem_u32(&sm.pbuf[0]) + lrow * 128;
@@ -822,11 +836,11 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
           st_shared_v4(drow + off, dk[c * 4], dk[c * 4 + 1], dk[c * 4 + 2], dk[c * 4 + 3]);
         }
         fence_proxy_async_smem();
-        mbar_arrive(&sm.pds_full);
+        warp_arrive(&sm.pds_full);
       }
       if (!ok) break;
       // epilogue: thread = dim; this warpgroup's 32 keys of dV^T and dK^T
-      if (!(ok = wt(&sm.acc_full[ab], (job >> 1) & 1, st, 23))) break;
+      if (!(ok = wtw(&sm.acc_full[ab], (job >> 1) & 1, st, 23))) break;
       tc_fence_after();
       const bool has = nb > 0;
       __nv_bfloat16* dkp = reinterpret_cast<__nv_bfloat16*>(p.dk) + d.b * p.dk_sb + (int64_t)d.hk * p.dk_sh + lrow;
@@ -859,8 +873,8 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         }
       }
       tc_fence_before();
-      mbar_arrive(&sm.acc_empty[ab]);
-      mbar_arrive(&sm.jd_empty[js]);
+      warp_arrive(&sm.acc_empty[ab]);
+      warp_arrive(&sm.jd_empty[js]);
       ++job;
     }
   }

@@ -11,19 +11,23 @@
 // with the usual log-sum-exp rescale.
 //
 // Cost model (measured on B200): an M=128, K=16 tcgen05 MMA with N = 16 takes
-// 45 cycles — its A operand (4 KB) is read from shared memory — so with G = 16
-// the forward is bounded by shared-memory bandwidth (TMA writes of the gathered
-// K/V plus MMA operand reads), not by the tensor pipe.  The kernel is organised
-// to keep that port busy: K and V stream through separate rings fed by separate
+// 40-60 cycles — its A operand (4 KB) is read from shared memory — and the
+// MMA queue behind one issuing thread is shallow: anything that thread does
+// between MMAs (a shared-memory load ~140 cycles, a commit ~90, an mbarrier
+// test ~40) leaves the tensor pipe idle.  So two threads issue: one the S^T
+// tiles, one the PV tiles; each one's waits are covered by the other's MMAs
+// (one issuer: 11.7K cycles per 1024-key job with the kernel's commits and
+// waits; two: 6.6K).  K and V stream through separate rings fed by separate
 // producer warps, and the softmax runs on two warpgroups with S held in
 // registers (one TMEM read per score).
 //
-// Warp roles (352 threads, one persistent CTA per SM):
+// Warp roles (384 threads, one persistent CTA per SM):
 //   warp 0      K producer: compacts the row's valid block ids into a job
 //               descriptor, loads Q, gathers 64-key K blocks (4-D TMA box per
 //               block and 64-dim slab, 128B swizzle) into 128-key stages;
-//   warp 10     V producer: the same gathers for V, one job behind;
-//   warp 1      MMA issuer (one thread): S^T for job j+1, then PV for job j;
+//   warp 10     V producer: the same gathers for V;
+//   warp 1      S issuer (one thread): S^T tiles of each job;
+//   warp 11     PV issuer (one thread): O^T += V^T P^T tiles of each job;
 //   warps 2-9   two softmax warpgroups (thread = key lane of a 128-key tile,
 //               warpgroup w takes tiles 4w..4w+3) and the epilogue
 //               (thread = dim lane of O^T, warpgroup w takes heads 8w..8w+7):
@@ -44,7 +48,7 @@ using namespace tc;
 
 namespace fwd {
 
-constexpr int kThreads = 352;
+constexpr int kThreads = 384;
 constexpr int kSoftmaxThreads = 256;
 constexpr int kSegBlocks = 16;      // 64-key blocks per segment (1024 keys, 8 tiles)
 constexpr int kJD = 4;              // job descriptor ring depth
@@ -100,6 +104,12 @@ __device__ __forceinline__ bool wt(uint64_t* bar, uint32_t parity, int32_t* stat
   return false;
 }
 
+// The same wait for a whole warp: every lane gets one verdict, so a warp that
+// gives up leaves its later warp-wide instructions together.
+__device__ __forceinline__ bool wtw(uint64_t* bar, uint32_t parity, int32_t* status, int site) {
+  return __all_sync(0xffffffffu, wt(bar, parity, status, site));
+}
+
 // Sum (kMax = false) or max of v[h] over the 32 lanes of a warp, 16 heads at
 // once with 16 shuffles: halve the head set at each butterfly step.  The result
 // for head (lane >> 1) & 15 is returned (lanes 2h and 2h+1 hold head h).
@@ -132,8 +142,8 @@ __device__ __forceinline__ float warp_reduce16(const float (&v)[16], int lane) {
 // `use` counts this thread's barrier uses; all softmax threads make the same
 // sequence of uses.
 __device__ __forceinline__ bool softmax_barrier(uint64_t* bar, uint32_t& use, int32_t* status) {
-  mbar_arrive(bar);
-  return wt(bar, (use++) & 1, status, 30);
+  warp_arrive(bar);
+  return wtw(bar, (use++) & 1, status, 30);
 }
 
 // Reduce over the 256 softmax threads; every thread gets all 16 results.
@@ -183,17 +193,17 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       mbar_init(&sm.q_full[i], 1);
       mbar_init(&sm.q_empty[i], 1);
       mbar_init(&sm.s_full[i], 1);
-      mbar_init(&sm.s_empty[i], kSoftmaxThreads);
+      mbar_init(&sm.s_empty[i], kSoftmaxThreads / 32);
       mbar_init(&sm.o_full[i], 1);
-      mbar_init(&sm.o_empty[i], kSoftmaxThreads);
+      mbar_init(&sm.o_empty[i], kSoftmaxThreads / 32);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&sm.p_full[i], kSoftmaxThreads / 2);
+      mbar_init(&sm.p_full[i], kSoftmaxThreads / 64);
       mbar_init(&sm.p_empty[i], 1);
     }
-    mbar_init(&sm.sm_bar, kSoftmaxThreads);
-    // consumers of a job descriptor: MMA thread, V producer, softmax threads
-    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 2 + kSoftmaxThreads); }
+    mbar_init(&sm.sm_bar, kSoftmaxThreads / 32);
+    // consumers of a job descriptor: S issuer, PV issuer, V producer, softmax warps
+    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 3 + kSoftmaxThreads / 32); }
     fence_barrier_init();
   }
   // padded query rows (G..15) stay zero for the whole kernel
@@ -320,32 +330,79 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       }
     }
   } else if (warp == 1) {
-    // ============================================================ MMA issuer
+    // ============================================================ S issuer
     if (lane == 0) {
       const uint32_t id_s = idesc_bf16(128, kNH, false, false);
+      int job = 0, item_i = 0, kuse = 0;
+      bool ok = true;
+      while (ok) {
+        const int js = job % kJD;
+        if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 13))) break;
+        // job fields go to registers once: a shared-memory load between MMAs
+        // stalls this thread and leaves the tensor pipe without work
+        const int flags = sm.jd[js].flags, nblk = sm.jd[js].nblk;
+        if (flags & kSentinel) break;
+        const int qs = item_i & 1;
+        if (flags & kFirst)
+          if (!(ok = wt(&sm.q_full[qs], (item_i >> 1) & 1, st, 14))) break;
+        const int sb = job & 1;
+        if (!(ok = wt(&sm.s_empty[sb], ((job >> 1) & 1) ^ 1, st, 15))) break;
+        tc_fence_after();
+        const uint64_t qdesc = smem_desc(smem_u32(&sm.q[qs][0]), 16, 1024, kSw128);
+        const int nch = (nblk + 1) / 2;
+        for (int c = 0; c < nch && ok; ++c, ++kuse) {
+          const int s = kuse % KS;
+          // TMA-filled stage: the mbarrier's complete_tx orders it for the
+          // tensor core (no tcgen05 fence needed)
+          if (!(ok = wt(&sm.k_full[s], (kuse / KS) & 1, st, 16))) break;
+          const uint64_t kdesc = smem_desc(smem_u32(&sm.kst[s][0]), 16, 1024, kSw128);
+          const uint32_t dcol = tmem + kColS + sb * 128 + c * kNH;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k)
+            mma_bf16_ss(dcol, kdesc + (uint64_t)(((k >> 2) * (128 * 128) + (k & 3) * 32) >> 4),
+                        qdesc + (uint64_t)(((k >> 2) * (kNH * 128) + (k & 3) * 32) >> 4), id_s, k != 0);
+          mma_commit(&sm.k_empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&sm.s_full[sb]);
+        if (flags & kLast) {
+          mma_commit(&sm.q_empty[qs]);
+          ++item_i;
+        }
+        mbar_arrive(&sm.jd_empty[js]);
+        ++job;
+      }
+    }
+  } else if (warp == 11) {
+    // ============================================================ PV issuer
+    // A second issuing thread: while one waits (on P, a stage, a barrier) the
+    // other's MMAs keep the tensor pipe busy.
+    if (lane == 0) {
       const uint32_t id_o = idesc_bf16(128, kNH, true, true);
       // A = V tile as MN-major: 64-dim slabs LBO apart (D = 64 repeats the slab;
       // rows 64-127 of O^T are then ignored), 8-key groups 1024 B apart.
       const uint32_t lbo_v = D == 128 ? 128u * 128u : 0u;
-      int job = 0, item_i = 0, kuse = 0, vuse = 0;
+      const uint64_t pdesc = smem_desc(smem_u32(&sm.p[0]), 0, 256, kSw32);
+      int job = 0, vuse = 0;
       bool ok = true;
-      auto pv = [&](int jj) -> bool {
-        const JobDesc& d = sm.jd[jj % kJD];
-        const int sb = jj & 1;
-        if (!wt(&sm.o_empty[sb], ((jj >> 1) & 1) ^ 1, st, 11)) return false;
+      while (ok) {
+        const int js = job % kJD;
+        if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 17))) break;
+        const int flags = sm.jd[js].flags, nblk = sm.jd[js].nblk;
+        if (flags & kSentinel) break;
+        const int sb = job & 1;
+        if (!(ok = wt(&sm.o_empty[sb], ((job >> 1) & 1) ^ 1, st, 11))) break;
         const uint32_t dcol = tmem + kColO + sb * kNH;
-        const uint64_t pdesc = smem_desc(smem_u32(&sm.p[0]), 0, 256, kSw32);
-        const int nch = (d.nblk + 1) / 2;
-        for (int c = 0; c < 8; ++c) {
+        const int nch = (nblk + 1) / 2;
+        for (int c = 0; c < 8 && ok; ++c) {
           // tiles 0-3 come from softmax warpgroup 0, tiles 4-7 from group 1
           if (c == 0 || c == 4) {
-            if (!wt(&sm.p_full[c >> 2], jj & 1, st, 10)) return false;
+            if (!(ok = wt(&sm.p_full[c >> 2], job & 1, st, 10))) break;
             tc_fence_after();
           }
           if (c < nch) {
             const int s = vuse % VS;
-            if (!wt(&sm.v_full[s], (vuse / VS) & 1, st, 12)) return false;
-            tc_fence_after();
+            if (!(ok = wt(&sm.v_full[s], (vuse / VS) & 1, st, 12))) break;
             // descriptors advance by adding the byte offset / 16 to the start-address field
             const uint64_t a0 = smem_desc(smem_u32(&sm.vst[s][0]), lbo_v, 1024, kSw128);
             const uint64_t b0 = pdesc + (uint64_t)(c * 128 * (kNH * 2) >> 4);
@@ -358,45 +415,11 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
           }
           if (c == 3 || c == 7) mma_commit(&sm.p_empty[c >> 2]);
         }
-        mma_commit(&sm.o_full[sb]);
-        mbar_arrive(&sm.jd_empty[jj % kJD]);
-        return true;
-      };
-      while (ok) {
-        const int js = job % kJD;
-        if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 13))) break;
-        const JobDesc& d = sm.jd[js];
-        if (d.flags & kSentinel) break;
-        const int qs = item_i & 1;
-        if (d.flags & kFirst)
-          if (!(ok = wt(&sm.q_full[qs], (item_i >> 1) & 1, st, 14))) break;
-        const int sb = job & 1;
-        if (!(ok = wt(&sm.s_empty[sb], ((job >> 1) & 1) ^ 1, st, 15))) break;
-        tc_fence_after();
-        const uint64_t qdesc = smem_desc(smem_u32(&sm.q[qs][0]), 16, 1024, kSw128);
-        const int nch = (d.nblk + 1) / 2;
-        for (int c = 0; c < nch && ok; ++c, ++kuse) {
-          const int s = kuse % KS;
-          if (!(ok = wt(&sm.k_full[s], (kuse / KS) & 1, st, 16))) break;
-          tc_fence_after();
-          const uint64_t kdesc = smem_desc(smem_u32(&sm.kst[s][0]), 16, 1024, kSw128);
-          const uint32_t dcol = tmem + kColS + sb * 128 + c * kNH;
-#pragma unroll
-          for (int k = 0; k < D / 16; ++k)
-            mma_bf16_ss(dcol, kdesc + (uint64_t)(((k >> 2) * (128 * 128) + (k & 3) * 32) >> 4),
-                        qdesc + (uint64_t)(((k >> 2) * (kNH * 128) + (k & 3) * 32) >> 4), id_s, k != 0);
-          mma_commit(&sm.k_empty[s]);
-        }
         if (!ok) break;
-        mma_commit(&sm.s_full[sb]);
-        if (d.flags & kLast) {
-          mma_commit(&sm.q_empty[qs]);
-          ++item_i;
-        }
-        if (job > 0 && !(ok = pv(job - 1))) break;
+        mma_commit(&sm.o_full[sb]);
+        mbar_arrive(&sm.jd_empty[js]);
         ++job;
       }
-      if (ok && job > 0) pv(job - 1);
     }
   } else {
     // ============================================================ softmax / epilogue
@@ -415,7 +438,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
     auto softmax = [&](int j) -> bool {
       const JobDesc& d = sm.jd[j % kJD];
       const int sb = j & 1;
-      if (!wt(&sm.s_full[sb], (j >> 1) & 1, st, 20)) return false;
+      if (!wtw(&sm.s_full[sb], (j >> 1) & 1, st, 20)) return false;
       tc_fence_after();
       const int nch = (d.nblk + 1) / 2;
       const uint32_t ts = tl + kColS + sb * 128;
@@ -428,7 +451,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       }
       tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(&sm.s_empty[sb]);
+      warp_arrive(&sm.s_empty[sb]);
       float m[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) m[h] = -INFINITY;
@@ -460,7 +483,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
 #pragma unroll
       for (int h = 0; h < 16; ++h) l[h] = 0.f;
       // this warpgroup's half of the P buffer is free once PV(j-1) read it
-      if (!wt(&sm.p_empty[wg], (j & 1) ^ 1, st, 21)) return false;
+      if (!wtw(&sm.p_empty[wg], (j & 1) ^ 1, st, 21)) return false;
       const uint32_t pbase = smem_u32(&sm.p[0]);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -484,7 +507,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
         }
       }
       fence_proxy_async_smem();
-      mbar_arrive(&sm.p_full[wg]);
+      warp_arrive(&sm.p_full[wg]);
       // row sums: per-warp partials only; the epilogue of this job (after the
       // next job's max reduction, whose barriers order these writes) adds them
       const float lw = warp_reduce16<false>(l, lane);
@@ -498,7 +521,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
 #pragma unroll
         for (int h = 0; h < 8; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
       }
-      if (!wt(&sm.o_full[sb], (jj >> 1) & 1, st, 22)) return false;
+      if (!wtw(&sm.o_full[sb], (jj >> 1) & 1, st, 22)) return false;
       tc_fence_after();
       if (d.nblk > 0) {
         float o[16];
@@ -520,7 +543,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
         }
       }
       tc_fence_before();
-      mbar_arrive(&sm.o_empty[sb]);
+      warp_arrive(&sm.o_empty[sb]);
       if (d.flags & kLast) {
         __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.o) + d.b * p.o_sb + (int64_t)d.tq * p.o_st +
                            (int64_t)(d.hk * G) * p.o_sh;
@@ -543,13 +566,13 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
           }
         }
       }
-      mbar_arrive(&sm.jd_empty[jj % kJD]);
+      warp_arrive(&sm.jd_empty[jj % kJD]);
       return true;
     };
     int job = 0;
     while (ok) {
       const int js = job % kJD;
-      if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 23))) break;
+      if (!(ok = wtw(&sm.jd_full[js], (job / kJD) & 1, st, 23))) break;
       if (sm.jd[js].flags & kSentinel) break;
       if (!(ok = softmax(job))) break;
       if (job > 0 && !(ok = epilogue(job - 1))) break;
