@@ -39,7 +39,7 @@ enum : int { kSentinel = 4 };
 // =========================================================================
 namespace dq {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 224;   // producer, S/dP issuer, 4 dS warps, dQ issuer
 constexpr int kR = 4;            // S/dP TMEM slots and dS smem slots
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColSdP = 0;  // kR x (16 S + 16 dP)
@@ -121,8 +121,9 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
       mbar_init(&sm.ds_full[i], 4);
       mbar_init(&sm.ds_empty[i], 1);
     }
-    // counts in warps for the 4 dS/epilogue warps (one arrival per warp)
-    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 1 + 4); }
+    // consumers of a job descriptor: the two issuers and the 4 dS/epilogue
+    // warps (one arrival per warp)
+    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 2 + 4); }
     fence_barrier_init();
   }
   for (int i = threadIdx.x; i < 2 * Smem<D>::kQBytes / 16; i += kThreads) {
@@ -237,48 +238,24 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
       }
     }
   } else if (warp == 1) {
-    // ============================================================ MMA issuer
+    // ============================================================ S/dP issuer
     if (lane == 0) {
       const uint32_t id_sdp = idesc_bf16(128, kNH, false, false);
-      const uint32_t id_dq = idesc_bf16(128, kNH, true, true);
-      const uint32_t lbo_k = D == 128 ? 128u * 128u : 0u;
-      struct Pending { int g, ks, slot, ib, js; bool first, last; };
-      Pending pend{};
-      bool has_pend = false, ok = true;
+      bool ok = true;
       int job = 0, g = 0;
-      auto issue_dq = [&](const Pending& pd) -> bool {
-        if (!wt(&sm.ds_full[pd.slot], (pd.g / kR) & 1, st, 10)) return false;
-        if (pd.first && !wt(&sm.dq_empty[pd.ib], (((pd.js >> 1)) & 1) ^ 1, st, 11)) return false;
-        tc_fence_after();
-        const uint64_t a0 = smem_desc(smem_u32(&sm.kst[pd.ks][0]), lbo_k, 1024, kSw128);
-        const uint64_t b0 = smem_desc(smem_u32(&sm.ds[pd.slot][0]), 0, 256, kSw32);
-        const uint32_t dcol = tmem + kColDQ + pd.ib * kNH;
-        // descriptors advance by adding the byte offset / 16 to the start-address field
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_bf16_ss(dcol, a0 + (uint64_t)(kk * 2048 >> 4), b0 + (uint64_t)(kk * 16 * (kNH * 2) >> 4), id_dq,
-                      (pd.first && kk == 0) ? 0u : 1u);
-        mma_commit(&sm.ds_empty[pd.slot]);   // also frees K stage pd.ks
-        if (pd.last) {
-          mma_commit(&sm.dq_full[pd.ib]);
-          mbar_arrive(&sm.jd_empty[pd.js % kJD]);
-        }
-        return true;
-      };
       while (ok) {
         const int js = job % kJD;
         if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 12))) break;
-        const JobDesc& d = sm.jd[js];
-        if (d.flags & kSentinel) break;
+        // job fields go to registers once: a shared-memory load between MMAs
+        // stalls this thread and leaves the tensor pipe without work
+        const int flags = sm.jd[js].flags, nblk = sm.jd[js].nblk;
+        if (flags & kSentinel) break;
+        mbar_arrive(&sm.jd_empty[js]);
         const int ib = job & 1;
         if (!(ok = wt(&sm.qdo_full[ib], (job >> 1) & 1, st, 13))) break;
-        const int nch = (d.nblk + 1) / 2;
+        const int nch = (nblk + 1) / 2;
         if (nch == 0) {
-          if (has_pend) { if (!(ok = issue_dq(pend))) break; has_pend = false; }
-          if (!(ok = wt(&sm.dq_empty[ib], ((job >> 1) & 1) ^ 1, st, 14))) break;
           mma_commit(&sm.qdo_empty[ib]);
-          mma_commit(&sm.dq_full[ib]);
-          mbar_arrive(&sm.jd_empty[js]);
           ++job;
           continue;
         }
@@ -287,9 +264,10 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
         for (int c = 0; c < nch && ok; ++c, ++g) {
           const int slot = g % kR, ks = g % KS, vs = g % VS;
           if (!(ok = wt(&sm.sdp_empty[slot], ((g / kR) & 1) ^ 1, st, 15))) break;
+          tc_fence_after();
+          // TMA-filled stages: their mbarriers' complete_tx order them for the tensor core
           if (!(ok = wt(&sm.k_full[ks], (g / KS) & 1, st, 16))) break;
           if (!(ok = wt(&sm.v_full[vs], (g / VS) & 1, st, 17))) break;
-          tc_fence_after();
           const uint64_t kdesc = smem_desc(smem_u32(&sm.kst[ks][0]), 16, 1024, kSw128);
           const uint64_t vdesc = smem_desc(smem_u32(&sm.vst[vs][0]), 16, 1024, kSw128);
           const uint32_t scol = tmem + kColSdP + slot * 32;
@@ -307,13 +285,47 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
           }
           mma_commit(&sm.sdp_full[slot]);   // also frees V stage vs
           if (c == nch - 1) mma_commit(&sm.qdo_empty[ib]);
-          if (has_pend && !(ok = issue_dq(pend))) break;
-          pend = Pending{g, ks, slot, ib, job, c == 0, c == nch - 1};
-          has_pend = true;
         }
         ++job;
       }
-      if (ok && has_pend) issue_dq(pend);
+    }
+  } else if (warp == 6) {
+    // ============================================================ dQ issuer
+    // A second issuing thread: while one waits, the other's MMAs keep the
+    // tensor pipe busy.
+    if (lane == 0) {
+      const uint32_t id_dq = idesc_bf16(128, kNH, true, true);
+      const uint32_t lbo_k = D == 128 ? 128u * 128u : 0u;
+      bool ok = true;
+      int job = 0, g = 0;
+      while (ok) {
+        const int js = job % kJD;
+        if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 18))) break;
+        const int flags = sm.jd[js].flags, nblk = sm.jd[js].nblk;
+        if (flags & kSentinel) break;
+        mbar_arrive(&sm.jd_empty[js]);
+        const int ib = job & 1;
+        if (!(ok = wt(&sm.dq_empty[ib], ((job >> 1) & 1) ^ 1, st, 11))) break;
+        tc_fence_after();
+        const int nch = (nblk + 1) / 2;
+        const uint32_t dcol = tmem + kColDQ + ib * kNH;
+        for (int c = 0; c < nch && ok; ++c, ++g) {
+          const int slot = g % kR, ks = g % KS;
+          if (!(ok = wt(&sm.ds_full[slot], (g / kR) & 1, st, 10))) break;
+          tc_fence_after();
+          const uint64_t a0 = smem_desc(smem_u32(&sm.kst[ks][0]), lbo_k, 1024, kSw128);
+          const uint64_t b0 = smem_desc(smem_u32(&sm.ds[slot][0]), 0, 256, kSw32);
+          // descriptors advance by adding the byte offset / 16 to the start-address field
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_bf16_ss(dcol, a0 + (uint64_t)(kk * 2048 >> 4), b0 + (uint64_t)(kk * 16 * (kNH * 2) >> 4), id_dq,
+                        (c == 0 && kk == 0) ? 0u : 1u);
+          mma_commit(&sm.ds_empty[slot]);   // also frees K stage ks
+        }
+        if (!ok) break;
+        mma_commit(&sm.dq_full[ib]);   // with no tiles this hands the epilogue an unwritten dQ: it writes zeros
+        ++job;
+      }
     }
   } else {
     // ============================================================ dS / epilogue
@@ -446,7 +458,7 @@ cudaError_t launch(const SfaParams& p, const float* delta, cudaStream_t stream) 
 // =========================================================================
 namespace dkdv {
 
-constexpr int kThreads = 352;       // warp 0 metadata, 1 MMA, 2-9 P/dS + epilogue, 10 TMA
+constexpr int kThreads = 384;       // warp 0 metadata, 1 S/dP issuer, 2-9 P/dS + epilogue, 10 TMA, 11 dV/dK issuer
 constexpr int kWG = 256;            // P/dS threads: 2 warpgroups, each takes 32 of the 64 keys
 constexpr int kQB = 8;              // queries per batch (x 16 heads = 128 MMA rows)
 constexpr int kMeta = 6;            // batch metadata ring depth
@@ -540,8 +552,8 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
     mbar_init(&sm.kv_empty, 1);
     mbar_init(&sm.pds_full, kWG / 32);
     mbar_init(&sm.pds_empty, 1);
-    // consumers of a job descriptor: MMA thread, TMA thread, P/dS warps
-    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 2 + kWG / 32); }
+    // consumers of a job descriptor: the two issuers, TMA thread, P/dS warps
+    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 3 + kWG / 32); }
     fence_barrier_init();
   }
   // padded head rows (G..15 of every query) stay zero
@@ -694,63 +706,29 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       }
     }
   } else if (warp == 1) {
-    // ============================================================ MMA issuer
+    // ============================================================ S/dP issuer
     if (lane == 0) {
       const uint32_t id_sdp = idesc_bf16(128, 64, false, false);
-      const uint32_t id_acc = idesc_bf16(128, 64, true, true);
-      const uint32_t lbo_rows = D == 128 ? 128u * 128u : 0u;   // 64-dim slabs of the 128-row buffers
-      struct Pending { int gb, s, ab, job; bool first, last; };
-      Pending pend{};
-      bool has_pend = false, ok = true;
+      bool ok = true;
       int job = 0, gb = 0;
-      auto issue_acc = [&](const Pending& pd) -> bool {
-        if (!wt(&sm.pds_full, pd.gb & 1, st, 10)) return false;
-        if (pd.first && !wt(&sm.acc_empty[pd.ab], ((pd.job >> 1) & 1) ^ 1, st, 11)) return false;
-        tc_fence_after();
-        const uint64_t od = smem_desc(smem_u32(&sm.dob[pd.s][0]), lbo_rows, 1024, kSw128);
-        const uint64_t qd = smem_desc(smem_u32(&sm.qb[pd.s][0]), lbo_rows, 1024, kSw128);
-        const uint64_t pdsc = smem_desc(smem_u32(&sm.pbuf[0]), 0, 1024, kSw128);
-        const uint64_t dd = smem_desc(smem_u32(&sm.dsbuf[0]), 0, 1024, kSw128);
-        const uint32_t acc = tmem + kColAcc + pd.ab * 128;
-        // 16 rows per K-step: +2048 bytes = +128 in the start-address field
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t accum = (pd.first && kk == 0) ? 0u : 1u;
-          mma_bf16_ss(acc, od + (uint64_t)(kk * 128), pdsc + (uint64_t)(kk * 128), id_acc, accum);
-          mma_bf16_ss(acc + 64, qd + (uint64_t)(kk * 128), dd + (uint64_t)(kk * 128), id_acc, accum);
-        }
-        mma_commit(&sm.b_empty[pd.s]);
-        mma_commit(&sm.pds_empty);
-        if (pd.last) {
-          mma_commit(&sm.acc_full[pd.ab]);
-          mbar_arrive(&sm.jd_empty[pd.job % kJD]);
-        }
-        return true;
-      };
+      const uint64_t kd = smem_desc(smem_u32(&sm.ke[0]), 16, 1024, kSw128);
+      const uint64_t vd = smem_desc(smem_u32(&sm.ve[0]), 16, 1024, kSw128);
       while (ok) {
         const int js = job % kJD;
         if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 12))) break;
-        const JobDesc& d = sm.jd[js];
-        if (d.flags & kSentinel) break;
-        const int ab = job & 1;
+        // job fields go to registers once: a shared-memory load between MMAs
+        // stalls this thread and leaves the tensor pipe without work
+        const int flags = sm.jd[js].flags, n = sm.jd[js].n;
+        if (flags & kSentinel) break;
+        mbar_arrive(&sm.jd_empty[js]);
+        // K_e / V_e are TMA-filled: the mbarrier's complete_tx orders them for the tensor core
         if (!(ok = wt(&sm.kv_full, job & 1, st, 13))) break;
-        const int nb = (d.n + kQB - 1) / kQB;
-        if (nb == 0) {
-          if (has_pend) { if (!(ok = issue_acc(pend))) break; has_pend = false; }
-          if (!(ok = wt(&sm.acc_empty[ab], ((job >> 1) & 1) ^ 1, st, 14))) break;
-          mma_commit(&sm.kv_empty);
-          mma_commit(&sm.acc_full[ab]);
-          mbar_arrive(&sm.jd_empty[js]);
-          ++job;
-          continue;
-        }
-        const uint64_t kd = smem_desc(smem_u32(&sm.ke[0]), 16, 1024, kSw128);
-        const uint64_t vd = smem_desc(smem_u32(&sm.ve[0]), 16, 1024, kSw128);
+        const int nb = (n + kQB - 1) / kQB;
         for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
           const int s = gb & 1;
           if (!(ok = wt(&sm.sdp_empty[s], ((gb >> 1) & 1) ^ 1, st, 15))) break;
-          if (!(ok = wt(&sm.b_full[s], (gb >> 1) & 1, st, 16))) break;
           tc_fence_after();
+          if (!(ok = wt(&sm.b_full[s], (gb >> 1) & 1, st, 16))) break;
           const uint64_t qd = smem_desc(smem_u32(&sm.qb[s][0]), 16, 1024, kSw128);
           const uint64_t od = smem_desc(smem_u32(&sm.dob[s][0]), 16, 1024, kSw128);
           const uint32_t scol = tmem + kColSdP + s * 128;
@@ -762,14 +740,56 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
             mma_bf16_ss(scol + 64, od + ro, vd + ko, id_sdp, k != 0);
           }
           mma_commit(&sm.sdp_full[s]);
-          if (jb == nb - 1) mma_commit(&sm.kv_empty);
-          if (has_pend && !(ok = issue_acc(pend))) break;
-          pend = Pending{gb, s, ab, job, jb == 0, jb == nb - 1};
-          has_pend = true;
         }
+        if (!ok) break;
+        mma_commit(&sm.kv_empty);
         ++job;
       }
-      if (ok && has_pend) issue_acc(pend);
+    }
+  } else if (warp == 11) {
+    // ============================================================ dV/dK issuer
+    // A second issuing thread: while one waits, the other's MMAs keep the
+    // tensor pipe busy.
+    if (lane == 0) {
+      const uint32_t id_acc = idesc_bf16(128, 64, true, true);
+      const uint32_t lbo_rows = D == 128 ? 128u * 128u : 0u;   // 64-dim slabs of the 128-row buffers
+      const uint64_t pdsc = smem_desc(smem_u32(&sm.pbuf[0]), 0, 1024, kSw128);
+      const uint64_t dd = smem_desc(smem_u32(&sm.dsbuf[0]), 0, 1024, kSw128);
+      bool ok = true;
+      int job = 0, gb = 0;
+      while (ok) {
+        const int js = job % kJD;
+        if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 17))) break;
+        const int flags = sm.jd[js].flags, n = sm.jd[js].n;
+        if (flags & kSentinel) break;
+        mbar_arrive(&sm.jd_empty[js]);
+        const int ab = job & 1;
+        if (!(ok = wt(&sm.acc_empty[ab], ((job >> 1) & 1) ^ 1, st, 11))) break;
+        tc_fence_after();
+        const int nb = (n + kQB - 1) / kQB;
+        const uint32_t acc = tmem + kColAcc + ab * 128;
+        for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
+          const int s = gb & 1;
+          if (!(ok = wt(&sm.pds_full, gb & 1, st, 10))) break;
+          tc_fence_after();
+          const uint64_t od = smem_desc(smem_u32(&sm.dob[s][0]), lbo_rows, 1024, kSw128);
+          const uint64_t qd = smem_desc(smem_u32(&sm.qb[s][0]), lbo_rows, 1024, kSw128);
+          // 16 rows per K-step: +2048 bytes = +128 in the start-address field
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t accum = (jb == 0 && kk == 0) ? 0u : 1u;
+            mma_bf16_ss(acc, od + (uint64_t)(kk * 128), pdsc + (uint64_t)(kk * 128), id_acc, accum);
+            mma_bf16_ss(acc + 64, qd + (uint64_t)(kk * 128), dd + (uint64_t)(kk * 128), id_acc, accum);
+          }
+          // the S/dP MMAs of this batch retired before its P/dS were written, so
+          // this commit frees the batch buffers for both issuers
+          mma_commit(&sm.b_empty[s]);
+          mma_commit(&sm.pds_empty);
+        }
+        if (!ok) break;
+        mma_commit(&sm.acc_full[ab]);   // with no batches the epilogue writes zeros
+        ++job;
+      }
     }
   } else {
     // ============================================================ P/dS and epilogue (warps 2-9)
