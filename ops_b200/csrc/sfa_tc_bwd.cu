@@ -39,7 +39,7 @@ enum : int { kSentinel = 4 };
 // =========================================================================
 namespace dq {
 
-constexpr int kThreads = 224;   // producer, S/dP issuer, 4 dS warps, dQ issuer
+constexpr int kThreads = 256;   // K producer, S/dP issuer, 4 dS warps, dQ issuer, V producer
 constexpr int kR = 4;            // S/dP TMEM slots and dS smem slots
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColSdP = 0;  // kR x (16 S + 16 dP)
@@ -121,9 +121,9 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
       mbar_init(&sm.ds_full[i], 4);
       mbar_init(&sm.ds_empty[i], 1);
     }
-    // consumers of a job descriptor: the two issuers and the 4 dS/epilogue
-    // warps (one arrival per warp)
-    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 2 + 4); }
+    // consumers of a job descriptor: the two issuers, the V producer and the
+    // 4 dS/epilogue warps (one arrival per warp)
+    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 3 + 4); }
     fence_barrier_init();
   }
   for (int i = threadIdx.x; i < 2 * Smem<D>::kQBytes / 16; i += kThreads) {
@@ -146,22 +146,23 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
+  const uint32_t chunk_bytes = 128u * D * 2u;
+  // one 128-key stage = blocks row0 / row1 (a row past the tensor map reads
+  // zeros) x D/64 slabs; coordinates in registers, so no shared-memory load
+  // sits between two TMA issues
+  auto load_chunk = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* full, int row0, int row1, int hk, int b) {
+    mbar_arrive_expect_tx(full, chunk_bytes);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+#pragma unroll
+      for (int cd = 0; cd < D / 64; ++cd)
+        tma_load_4d(dst + cd * 128 * 128 + half * 64 * 128, map, full, cd * 64, hk, half ? row1 : row0, b);
+    }
+  };
   if (warp == 0) {
-    // ============================================================ producer
+    // ============================================================ K producer
     int job = 0, g = 0;
     bool ok = true;
-    const uint32_t chunk_bytes = 128u * D * 2u;
-    auto load_tile = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* full, const JobDesc& d, int c) {
-      mbar_arrive_expect_tx(full, chunk_bytes);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int bi = 2 * c + half;
-        const int row = bi < d.nblk ? d.kv0 + d.blocks[bi] * 64 : args.oob_row;
-#pragma unroll
-        for (int cd = 0; cd < D / 64; ++cd)
-          tma_load_4d(dst + cd * 128 * 128 + half * 64 * 128, map, full, cd * 64, d.hk, row, d.b);
-      }
-    };
     for (int item = blockIdx.x; item < args.nitems && ok; item += gridDim.x, ++job) {
       const int hk = item / args.nrows, row = item - hk * args.nrows;
       const Row r = row_info(p, row);
@@ -171,9 +172,11 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
       JobDesc& d = sm.jd[js];
+      // compact the valid block ids into d.blocks
       int n = 0;
-      for (int s0 = 0; s0 < p.topk; s0 += 32) {
-        const int s = s0 + lane;
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int s = h2 * 32 + lane;
         int e = -1;
         bool valid = false;
         if (s < p.topk) {
@@ -184,6 +187,7 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
         if (valid) d.blocks[n + __popc(m & ((1u << lane) - 1u))] = e;
         n += __popc(m);
       }
+      __syncwarp();
       if (lane < kNH) {
         float l2 = -INFINITY, dlv = 0.f;
         if (lane < G) {
@@ -193,7 +197,6 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
         d.lse2[lane] = l2;
         d.dl[lane] = dlv;
       }
-      __syncwarp();
       if (lane == 0) {
         d.row = row;
         d.hk = hk;
@@ -204,6 +207,9 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
         d.pos = r.pos;
         d.nblk = n;
         d.flags = 0;
+      }
+      __syncwarp();
+      if (lane == 0) {
         mbar_arrive(&sm.jd_full[js]);
         const int ib = job & 1;
         ok = wt(&sm.qdo_empty[ib], ((job >> 1) & 1) ^ 1, st, 2);
@@ -215,16 +221,25 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
             tma_load_4d(&sm.dO[ib][cd * kNH * 128], &tmdo, &sm.qdo_full[ib], cd * 64, hk * G, (int)r.tq, r.b);
           }
         }
-        for (int c = 0; c < (n + 1) / 2 && ok; ++c, ++g) {
-          const int ks = g % KS, vs = g % VS;
+      }
+      if (lane == 0 && ok) {
+        // block ids come from shared memory one tile ahead, so no load sits
+        // between two TMA issues
+        const int nch = (n + 1) / 2;
+        int e0 = n > 0 ? d.blocks[0] : 0, e1 = n > 1 ? d.blocks[1] : 0;
+        for (int c = 0; c < nch && ok; ++c, ++g) {
+          const int row0 = (int)r.kv0 + e0 * 64;
+          const int row1 = 2 * c + 1 < n ? (int)r.kv0 + e1 * 64 : args.oob_row;
+          if (c + 1 < nch) {
+            e0 = d.blocks[2 * c + 2];
+            e1 = d.blocks[2 * c + 3];   // past n: never used
+          }
+          const int ks = g % KS;
           // a K stage is free once the dQ MMAs of tile g-KS retired (the same
-          // commit that frees its dS slot); a V stage once dP of tile g-VS retired
-          // (the commit that hands S/dP to the softmax warps).  Neither barrier
-          // can complete its next phase before this thread loads tile g+1.
-          if (g >= KS && !(ok = wt(&sm.ds_empty[(g - KS) % kR], ((g - KS) / kR) & 1, st, 3))) break;
-          load_tile(&tmk, sm.kst[ks], &sm.k_full[ks], d, c);
-          if (g >= VS && !(ok = wt(&sm.sdp_full[(g - VS) % kR], ((g - VS) / kR) & 1, st, 4))) break;
-          load_tile(&tmv, sm.vst[vs], &sm.v_full[vs], d, c);
+          // commit that frees its dS slot); that barrier cannot complete its
+          // next phase before this thread loads tile g+1
+          if (g >= KS) ok = wt(&sm.ds_empty[(g - KS) % kR], ((g - KS) / kR) & 1, st, 3);
+          if (ok) load_chunk(&tmk, sm.kst[ks], &sm.k_full[ks], row0, row1, hk, r.b);
         }
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -235,6 +250,40 @@ sfa_bwd_dq_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ 
       if (wt(&sm.jd_empty[js], ((job / kJD) & 1) ^ 1, st, 5)) {
         sm.jd[js].flags = kSentinel;
         mbar_arrive(&sm.jd_full[js]);
+      }
+    }
+  } else if (warp == 7) {
+    // ============================================================ V producer
+    // Its own thread: one TMA-issuing thread alone limits the gather rate.
+    if (lane == 0) {
+      int job = 0, g = 0;
+      bool ok = true;
+      while (ok) {
+        const int js = job % kJD;
+        if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 6))) break;
+        const JobDesc& d = sm.jd[js];
+        const int flags = d.flags;
+        if (flags & kSentinel) break;
+        const int n = d.nblk, kv0 = d.kv0, hk = d.hk, b = d.b;
+        const int nch = (n + 1) / 2;
+        int e0 = n > 0 ? d.blocks[0] : 0, e1 = n > 1 ? d.blocks[1] : 0;
+        for (int c = 0; c < nch && ok; ++c, ++g) {
+          const int row0 = kv0 + e0 * 64;
+          const int row1 = 2 * c + 1 < n ? kv0 + e1 * 64 : args.oob_row;
+          if (c + 1 < nch) {
+            e0 = d.blocks[2 * c + 2];
+            e1 = d.blocks[2 * c + 3];   // past n: never used
+          }
+          const int vs = g % VS;
+          // a V stage is free once dP of tile g-VS retired (the commit that
+          // hands S/dP to the dS warps); that barrier cannot complete its next
+          // phase before this thread loads tile g+1
+          if (g >= VS) ok = wt(&sm.sdp_full[(g - VS) % kR], ((g - VS) / kR) & 1, st, 4);
+          if (ok) load_chunk(&tmv, sm.vst[vs], &sm.v_full[vs], row0, row1, hk, b);
+        }
+        if (!ok) break;
+        mbar_arrive(&sm.jd_empty[js]);   // after the last read of the descriptor
+        ++job;
       }
     }
   } else if (warp == 1) {
@@ -458,7 +507,8 @@ cudaError_t launch(const SfaParams& p, const float* delta, cudaStream_t stream) 
 // =========================================================================
 namespace dkdv {
 
-constexpr int kThreads = 384;       // warp 0 metadata, 1 S/dP issuer, 2-9 P/dS + epilogue, 10 TMA, 11 dV/dK issuer
+constexpr int kThreads = 416;       // warp 0 metadata, 1 S/dP issuer, 2-9 P/dS + epilogue, 10 K/V/Q loads,
+                                    // 11 dV/dK issuer, 12 dO loads
 constexpr int kWG = 256;            // P/dS threads: 2 warpgroups, each takes 32 of the 64 keys
 constexpr int kQB = 8;              // queries per batch (x 16 heads = 128 MMA rows)
 constexpr int kMeta = 6;            // batch metadata ring depth
@@ -470,14 +520,12 @@ struct JobDesc {
   int e, b, hk, kv0, kv_len, n, list0, flags;
 };
 
-// Per-batch metadata of the (query, head) rows of one batch, written by the
-// metadata warp ahead of the loads: TMA coordinates of each query, its causal
-// position, and lse/delta of each (query, head).
+// Per-batch metadata of the queries of one batch, written by the metadata warp
+// ahead of the loads: TMA coordinates of each query, its causal position and
+// its row id (lse and delta are fetched by the P/dS threads themselves).
 struct BatchMeta {
-  int tq[kQB], b[kQB], pos[kQB];
+  int tq[kQB], b[kQB], pos[kQB], rowid[kQB];
   int m;                  // queries in the batch
-  float lse2[kQB][kNH];   // -inf marks an absent (query, head) row
-  float dl[kQB][kNH];
 };
 
 template <int D>
@@ -492,7 +540,7 @@ struct Smem {
   alignas(1024) uint8_t dsbuf[128 * 64 * 2];
   JobDesc jd[kJD];
   alignas(16) BatchMeta meta[kMeta];
-  uint64_t b_full[2], b_empty[2], kv_full, kv_empty;
+  uint64_t bq_full[2], bdo_full[2], b_empty[2], kv_full, kv_empty;
   uint64_t meta_full[kMeta], meta_empty[kMeta];
   uint64_t sdp_full[2], sdp_empty[2], pds_full, pds_empty;
   uint64_t acc_full[2], acc_empty[2];
@@ -536,7 +584,8 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&sm.b_full[i], 1);
+      mbar_init(&sm.bq_full[i], 1);
+      mbar_init(&sm.bdo_full[i], 1);
       mbar_init(&sm.b_empty[i], 1);
       mbar_init(&sm.sdp_full[i], 1);
       mbar_init(&sm.sdp_empty[i], kWG / 32);
@@ -546,14 +595,14 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
     // counts in warps for the P/dS warps (one arrival per warp)
     for (int i = 0; i < kMeta; ++i) {
       mbar_init(&sm.meta_full[i], 1);
-      mbar_init(&sm.meta_empty[i], 1 + kWG / 32);   // TMA thread + P/dS warps
+      mbar_init(&sm.meta_empty[i], 2 + kWG / 32);   // the two loader threads + P/dS warps
     }
     mbar_init(&sm.kv_full, 1);
     mbar_init(&sm.kv_empty, 1);
     mbar_init(&sm.pds_full, kWG / 32);
     mbar_init(&sm.pds_empty, 1);
-    // consumers of a job descriptor: the two issuers, TMA thread, P/dS warps
-    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 3 + kWG / 32); }
+    // consumers of a job descriptor: the two issuers, the two loader threads, P/dS warps
+    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 4 + kWG / 32); }
     fence_barrier_init();
   }
   // padded head rows (G..15 of every query) stay zero
@@ -637,22 +686,9 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
           mt.tq[lane] = tq;
           mt.b[lane] = bb;
           mt.pos[lane] = pos;
+          mt.rowid[lane] = rowid;
         }
         if (lane == 0) mt.m = m;
-#pragma unroll
-        for (int it = 0; it < kQB * kNH / 32; ++it) {
-          const int i = it * 32 + lane, j = i >> 4, h = i & 15;
-          const int rj = __shfl_sync(0xffffffffu, rowid, j);
-          const int tj = __shfl_sync(0xffffffffu, tq, j);
-          const int bj = __shfl_sync(0xffffffffu, bb, j);
-          float l2 = -INFINITY, dlv = 0.f;
-          if (j < m && h < G) {
-            l2 = p.lse[bj * p.l_sb + (int64_t)tj * p.l_st + (int64_t)(hk * G + h) * p.l_sh] * kLog2e;
-            dlv = args.delta[(int64_t)rj * p.h_q + hk * G + h];
-          }
-          mt.lse2[j][h] = l2;
-          mt.dl[j][h] = dlv;
-        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.meta_full[slot]);
       }
@@ -665,43 +701,61 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         mbar_arrive(&sm.jd_full[js]);
       }
     }
-  } else if (warp == 10) {
+  } else if (warp == 10 || warp == 12) {
     // ============================================================ TMA loads
+    // Two loader threads: warp 10 gathers K_e / V_e and the batches' Q rows,
+    // warp 12 their dO rows.  Each 16-head row is a 2 KB box and one thread
+    // issues about one box per 100 cycles, so one loader alone would set the
+    // pace.  The batch's coordinates are read into registers up front (no
+    // shared-memory load between two TMA issues).
     if (lane == 0) {
+      const bool is_q = warp == 10;
+      const CUtensorMap* map = is_q ? &tmq : &tmdo;
       int job = 0, gb = 0;
       bool ok = true;
       while (ok) {
         const int js = job % kJD;
-        if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, 5))) break;
+        if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, is_q ? 5 : 8))) break;
         const JobDesc& d = sm.jd[js];
-        if (d.flags & kSentinel) break;
-        if (!(ok = wt(&sm.kv_empty, (job & 1) ^ 1, st, 6))) break;
-        mbar_arrive_expect_tx(&sm.kv_full, 2u * 64u * D * 2u);
+        const int flags = d.flags;
+        if (flags & kSentinel) break;
+        const int hk = d.hk, n = d.n, krow = d.kv0 + d.e * 64, kb = d.b;
+        mbar_arrive(&sm.jd_empty[js]);
+        if (is_q) {
+          if (!(ok = wt(&sm.kv_empty, (job & 1) ^ 1, st, 6))) break;
+          mbar_arrive_expect_tx(&sm.kv_full, 2u * 64u * D * 2u);
 #pragma unroll
-        for (int cd = 0; cd < D / 64; ++cd) {
-          tma_load_4d(&sm.ke[cd * 64 * 128], &tmk, &sm.kv_full, cd * 64, d.hk, d.kv0 + d.e * 64, d.b);
-          tma_load_4d(&sm.ve[cd * 64 * 128], &tmv, &sm.kv_full, cd * 64, d.hk, d.kv0 + d.e * 64, d.b);
+          for (int cd = 0; cd < D / 64; ++cd) {
+            tma_load_4d(&sm.ke[cd * 64 * 128], &tmk, &sm.kv_full, cd * 64, hk, krow, kb);
+            tma_load_4d(&sm.ve[cd * 64 * 128], &tmv, &sm.kv_full, cd * 64, hk, krow, kb);
+          }
         }
-        const int nb = (d.n + kQB - 1) / kQB;
+        const int nb = (n + kQB - 1) / kQB;
         for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
           const int slot = gb % kMeta, s = gb & 1;
-          if (!(ok = wt(&sm.meta_full[slot], (gb / kMeta) & 1, st, 7))) break;
-          if (!(ok = wt(&sm.b_empty[s], ((gb >> 1) & 1) ^ 1, st, 3))) break;
+          if (!(ok = wt(&sm.meta_full[slot], (gb / kMeta) & 1, st, is_q ? 7 : 9))) break;
           const BatchMeta& mt = sm.meta[slot];
           const int m = mt.m;
-          mbar_arrive_expect_tx(&sm.b_full[s], (uint32_t)(2 * m * G * D * 2));
-          for (int j = 0; j < m; ++j) {
-            const int tq = mt.tq[j], bb = mt.b[j];
+          int tq[kQB], bq[kQB];
 #pragma unroll
-            for (int cd = 0; cd < D / 64; ++cd) {
-              tma_load_4d(&sm.qb[s][cd * 128 * 128 + j * 16 * 128], &tmq, &sm.b_full[s], cd * 64, d.hk * G, tq, bb);
-              tma_load_4d(&sm.dob[s][cd * 128 * 128 + j * 16 * 128], &tmdo, &sm.b_full[s], cd * 64, d.hk * G, tq,
-                          bb);
-            }
+          for (int j = 0; j < kQB; ++j) {
+            tq[j] = mt.tq[j];
+            bq[j] = mt.b[j];
           }
           mbar_arrive(&sm.meta_empty[slot]);
+          if (!(ok = wt(&sm.b_empty[s], ((gb >> 1) & 1) ^ 1, st, is_q ? 3 : 19))) break;
+          uint64_t* full = is_q ? &sm.bq_full[s] : &sm.bdo_full[s];
+          uint8_t* buf = is_q ? sm.qb[s] : sm.dob[s];
+          mbar_arrive_expect_tx(full, (uint32_t)(m * G * D * 2));
+#pragma unroll
+          for (int j = 0; j < kQB; ++j) {
+            if (j < m) {
+#pragma unroll
+              for (int cd = 0; cd < D / 64; ++cd)
+                tma_load_4d(buf + cd * 128 * 128 + j * 16 * 128, map, full, cd * 64, hk * G, tq[j], bq[j]);
+            }
+          }
         }
-        mbar_arrive(&sm.jd_empty[js]);
         ++job;
       }
     }
@@ -728,15 +782,21 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
           const int s = gb & 1;
           if (!(ok = wt(&sm.sdp_empty[s], ((gb >> 1) & 1) ^ 1, st, 15))) break;
           tc_fence_after();
-          if (!(ok = wt(&sm.b_full[s], (gb >> 1) & 1, st, 16))) break;
           const uint64_t qd = smem_desc(smem_u32(&sm.qb[s][0]), 16, 1024, kSw128);
           const uint64_t od = smem_desc(smem_u32(&sm.dob[s][0]), 16, 1024, kSw128);
           const uint32_t scol = tmem + kColSdP + s * 128;
+          if (!(ok = wt(&sm.bq_full[s], (gb >> 1) & 1, st, 16))) break;
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
             const uint64_t ro = (uint64_t)(((k >> 2) * (128 * 128) + (k & 3) * 32) >> 4);
             const uint64_t ko = (uint64_t)(((k >> 2) * (64 * 128) + (k & 3) * 32) >> 4);
             mma_bf16_ss(scol, qd + ro, kd + ko, id_sdp, k != 0);
+          }
+          if (!(ok = wt(&sm.bdo_full[s], (gb >> 1) & 1, st, 18))) break;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint64_t ro = (uint64_t)(((k >> 2) * (128 * 128) + (k & 3) * 32) >> 4);
+            const uint64_t ko = (uint64_t)(((k >> 2) * (64 * 128) + (k & 3) * 32) >> 4);
             mma_bf16_ss(scol + 64, od + ro, vd + ko, id_sdp, k != 0);
           }
           mma_commit(&sm.sdp_full[s]);
@@ -818,9 +878,15 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         const int s = gb & 1, slot = gb % kMeta;
         if (!(ok = wtw(&sm.meta_full[slot], (gb / kMeta) & 1, st, 24))) break;
         const BatchMeta& mt = sm.meta[slot];
-        const float lse2 = mt.lse2[jq][h];
-        const float dl = mt.dl[jq][h];
+        // this thread's (query, head) row: lse and delta straight from global
+        // memory (their latency overlaps the wait for S/dP below)
         const int pos = mt.pos[jq];
+        float lse2 = -INFINITY, dl = 0.f;
+        if (jq < mt.m && h < G) {
+          const int hh = d.hk * G + h;
+          lse2 = __ldg(p.lse + mt.b[jq] * p.l_sb + (int64_t)mt.tq[jq] * p.l_st + (int64_t)hh * p.l_sh) * kLog2e;
+          dl = __ldg(args.delta + (int64_t)mt.rowid[jq] * p.h_q + hh);
+        }
         const bool rvalid = lse2 != -INFINITY;
         warp_arrive(&sm.meta_empty[slot]);
         // keys of this warpgroup valid for this row: key_base + i < lim

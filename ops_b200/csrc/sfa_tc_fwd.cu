@@ -224,6 +224,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
+  // the same copy with its coordinates read from a job descriptor
   auto load_tile = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* full, const JobDesc& d, int c) {
     mbar_arrive_expect_tx(full, chunk_bytes);
 #pragma unroll
@@ -234,6 +235,24 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       for (int cd = 0; cd < D / 64; ++cd)
         tma_load_4d(dst + cd * 128 * 128 + half * 64 * 128, map, full, cd * 64, d.hk, row, d.b);
     }
+  };
+
+  // One 128-key stage = two 64-key blocks (TMA rows row0 / row1; a row past the
+  // tensor map reads zeros) x D/64 slabs.  All coordinates are in registers: a
+  // shared-memory load between two TMA issues would stall the producer.
+  auto load_chunk = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* full, int row0, int row1, int hk, int b) {
+    mbar_arrive_expect_tx(full, chunk_bytes);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+#pragma unroll
+      for (int cd = 0; cd < D / 64; ++cd)
+        tma_load_4d(dst + cd * 128 * 128 + half * 64 * 128, map, full, cd * 64, hk, half ? row1 : row0, b);
+    }
+  };
+  // TMA row of block slot i of a segment (block ids in registers; a missing
+  // block reads rows past the tensor map, i.e. zeros)
+  auto blk_row = [&](const int (&rb)[kSegBlocks], int i, int nb, int kv0) {
+    return i < nb ? kv0 + rb[i] * 64 : args.oob_row;
   };
 
   if (warp == 0) {
@@ -257,7 +276,9 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       const Row r = nr;
       const int cur0 = nx0, cur1 = nx1;
       if (item + (int)gridDim.x < args.nitems) fetch(item + gridDim.x, nx0, nx1, nr);
-      int n = 0;
+      // compact the valid block ids: position i of the list lives in lane i & 31
+      // of pl0 (i < 32) or pl1 (i >= 32)
+      int n = 0, pl0 = -1, pl1 = -1;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int e = half ? cur1 : cur0;
@@ -267,6 +288,8 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
         n += __popc(m);
       }
       __syncwarp();
+      if (lane < n) pl0 = sm.plist[lane];
+      if (lane + 32 < n) pl1 = sm.plist[lane + 32];
       const int nseg = n == 0 ? 1 : (n + kSegBlocks - 1) / kSegBlocks;
       if (lane == 0) {
         const int qs = item_i & 1;
@@ -277,11 +300,22 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
           for (int cd = 0; cd < D / 64; ++cd)
             tma_load_4d(&sm.q[qs][cd * kNH * 128], &tmq, &sm.q_full[qs], cd * 64, hk * G, (int)r.tq, r.b);
         }
-        for (int seg = 0; seg < nseg && ok; ++seg, ++job) {
-          const int js = job % kJD;
-          if (!(ok = wt(&sm.jd_empty[js], ((job / kJD) & 1) ^ 1, st, 3))) break;
-          JobDesc& d = sm.jd[js];
-          const int nb = n == 0 ? 0 : min(kSegBlocks, n - seg * kSegBlocks);
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      for (int seg = 0; seg < nseg && ok; ++seg, ++job) {
+        const int js = job % kJD;
+        if (lane == 0) ok = wt(&sm.jd_empty[js], ((job / kJD) & 1) ^ 1, st, 3);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+        JobDesc& d = sm.jd[js];
+        const int nb = n == 0 ? 0 : min(kSegBlocks, n - seg * kSegBlocks);
+        // lane i < nb: block i of this segment (list position seg * 16 + i)
+        const int gi = seg * kSegBlocks + (lane & (kSegBlocks - 1));
+        const int v0 = __shfl_sync(0xffffffffu, pl0, gi & 31);
+        const int v1 = __shfl_sync(0xffffffffu, pl1, gi & 31);
+        const int blk = gi < 32 ? v0 : v1;
+        if (lane < nb) d.blocks[lane] = blk;
+        if (lane == 0) {
           d.row = row;
           d.hk = hk;
           d.b = r.b;
@@ -291,17 +325,30 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
           d.pos = r.pos;
           d.nblk = nb;
           d.flags = (seg == 0 ? kFirst : 0) | (seg == nseg - 1 ? kLast : 0);
-          for (int i = 0; i < nb; ++i) d.blocks[i] = sm.plist[seg * kSegBlocks + i];
+        }
+        // the segment's block ids into lane 0's registers
+        int rb[kSegBlocks];
+#pragma unroll
+        for (int i = 0; i < kSegBlocks; ++i) rb[i] = __shfl_sync(0xffffffffu, blk, i);
+        __syncwarp();
+        if (lane == 0) {
           mbar_arrive(&sm.jd_full[js]);
-          for (int c = 0; c < (nb + 1) / 2 && ok; ++c, ++use) {
-            const int s = use % KS;
-            if (!(ok = wt(&sm.k_empty[s], ((use / KS) & 1) ^ 1, st, 1))) break;
-            load_tile(&tmk, sm.kst[s], &sm.k_full[s], d, c);
+          const int nch = (nb + 1) / 2;
+#pragma unroll
+          for (int c = 0; c < kSegBlocks / 2; ++c) {
+            if (c < nch && ok) {
+              const int s = use % KS;
+              ok = wt(&sm.k_empty[s], ((use / KS) & 1) ^ 1, st, 1);
+              if (ok)
+                load_chunk(&tmk, sm.kst[s], &sm.k_full[s], blk_row(rb, 2 * c, nb, (int)r.kv0),
+                           blk_row(rb, 2 * c + 1, nb, (int)r.kv0), hk, r.b);
+              ++use;
+            }
           }
         }
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        use = __shfl_sync(0xffffffffu, use, 0);
       }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      job = __shfl_sync(0xffffffffu, job, 0);
     }
     if (lane == 0 && ok) {
       const int js = job % kJD;
@@ -312,6 +359,10 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
     }
   } else if (warp == 10) {
     // ============================================================ V producer
+    // Reads each copy's coordinates from the descriptor.  A V producer with
+    // register-resident coordinates issues faster, but together with the K
+    // producer below it measured slower overall (c2: 6.42 vs 5.47 ms): the
+    // extra V gathers in flight delay the K gathers that S^T waits on.
     if (lane == 0) {
       int job = 0, use = 0;
       bool ok = true;
