@@ -41,6 +41,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "SFA fwd+bwd TFLOP/s (selected tokens) & % bf16 tensor peak, 1/2/4/8 B200"
+# DRAM bytes (read + write) per launch from ncu captures of the c2 shape at B=1
+# (profiles/sfa_*_c2_b1.md), scaled x4 to the bench's B=4 launch: each unit's
+# q/dO/o/dq rows are read or written once and its K/V stay in L2.
+NCU_TRAFFIC = {"c2": {"fwd": 4 * (0.154496e9 + 0.101303e9),
+                      "bwd_dq": 4 * (0.296924e9 + 0.112170e9),
+                      "bwd_dkdv": 4 * (1.324235e9 + 0.019223e9)}}
 FALLBACK_BF16_TFLOPS = 1590.0
 
 
@@ -343,6 +349,9 @@ def run_ours(args, cfg):
                    "bwd_dq": two_p * (2 * cfg.Dqk + cfg.Dv) if tc_bwd else fl.bwd,
                    "bwd_dkdv": two_p * (cfg.Dqk + cfg.Dv) if tc_bwd else 0.0}
     dom = max(stages, key=lambda s: stage_ms[s])
+    # K and V rows gathered per (row, kv head): selected keys x (Dqk + Dv) bf16
+    kv_gather = pairs / G * (cfg.Dqk + cfg.Dv) * 2.0
+    gather_bytes = {"fwd": kv_gather, "bwd_dq": kv_gather} if tc_bwd else {}
     ach = stage_flops[dom] / (stage_ms[dom] * 1e-3) / 1e12
     value = flops_all / (step_ms_max * 1e-3) / 1e12
     e2e_v = flops_all / (e_ms_max * 1e-3) / 1e12
@@ -357,7 +366,14 @@ def run_ours(args, cfg):
         "stages_ms": stage_ms,
         "kernel_family": {"fwd": fams.get(fam_f, str(fam_f)), "bwd": fams.get(fam_b, str(fam_b))},
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
-                     "frac": ach / peak, "peak_kind": f"{peak_kind} bf16 burst", "traffic": None},
+                     "frac": ach / peak, "peak_kind": f"{peak_kind} bf16 burst",
+                     "traffic": NCU_TRAFFIC.get(cfg.name, {}).get(dom) if cfg.B == 4 else None,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at B=1, "
+                                       "x4 for the B=4 launch (profiles/)"},
+        # gathered K/V rows per launch (L2 -> shared memory) of the dominant stage
+        "gather": {"kernel": dom, "bytes_per_launch": gather_bytes.get(dom),
+                   "achieved": (gather_bytes[dom] / (stage_ms[dom] * 1e-3) / 1e12) if gather_bytes.get(dom) else None,
+                   "unit": "TB/s"},
         "e2e": {"value": e2e_v, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e_ms_max},
         "clocks": clocks,
