@@ -56,6 +56,16 @@ enum {
   SFA_DKV_ATOMIC = 2     /* query-centric pass with fp32 atomics */
 };
 
+/* dQ algorithm (SfaParams.dq_mode) of the tensor-core backward with the
+ * inverted-index dK/dV pass; other paths always compute dQ in their own pass. */
+enum {
+  SFA_DQ_AUTO = 0,      /* FUSED where it applies */
+  SFA_DQ_SEPARATE = 1,  /* query-centric pass that recomputes S and dP; deterministic */
+  SFA_DQ_FUSED = 2      /* accumulated by the key-centric dK/dV pass from its dS (fp32
+                           reductions into a workspace accumulator, order not fixed);
+                           needs rows * h_q * d_qk * 4 more workspace bytes */
+};
+
 /* Kernel family (SfaParams.kernel); AUTO picks the tensor-core path when it
  * supports the shape and the general CUDA-core path otherwise. */
 enum {
@@ -108,7 +118,8 @@ typedef struct SfaParams {
   int32_t causal;     /* 0 / 1 */
   int32_t dkv_mode;   /* SFA_DKV_* */
   int32_t kernel;     /* SFA_KERNEL_* */
-  int32_t reserved[3];
+  int32_t dq_mode;    /* SFA_DQ_* (was reserved: zero = AUTO) */
+  int32_t reserved[2];
 } SfaParams;
 
 /* Library / ABI identification. */
@@ -147,22 +158,27 @@ int sfa_bwd(const SfaParams* p, void* workspace, size_t workspace_bytes, void* s
  *    (replaces `_get_delta_split`, SFA.py:590-610, and the dsink atomics,
  *    SFA.py:964-970);
  *  - dq: replaces `_attn_bwd_dq_dsink` / `_inner_dq` (SFA.py:613-716, 856-1002);
+ *    with SFA_DQ_FUSED it only clears the dQ accumulator;
  *  - dkdv: replaces `_attn_bwd_dk_dv` / `_inner_dkv` (SFA.py:719-853, 1005-1145);
- *    with SFA_DKV_INVERTED it first builds the block->query index. */
-/* Backward for callers that cannot allocate device memory (no counterpart in the
- * reference).  Same results as sfa_bwd, but the scratch comes from a 32 MiB
- * static device array inside the library instead of a caller workspace; every
- * GPU that loads the library reserves that array until the process exits.
- * Problems whose sfa_bwd_workspace_bytes() exceeds 32 MiB are refused with
- * SFA_ERR_WORKSPACE before anything is launched.  The first call on a device
- * looks up the array's device address; make it before any stream capture.
- * Calls share the array: calls that overlap on the GPU race and must be
- * serialised by the caller. */
-int sfa_bwd_noalloc(const SfaParams* p, void* stream);
+ *    with SFA_DKV_INVERTED it first builds the block->query index; with
+ *    SFA_DQ_FUSED it also accumulates dQ and writes dq.
+ * Run them in this order on one stream. */
 
 int sfa_bwd_preprocess(const SfaParams* p, void* workspace, size_t workspace_bytes, void* stream);
 int sfa_bwd_dq(const SfaParams* p, void* workspace, size_t workspace_bytes, void* stream);
 int sfa_bwd_dkdv(const SfaParams* p, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward for callers that cannot allocate device memory (no counterpart in the
+ * reference).  Same results as sfa_bwd, but the scratch comes from a 32 MiB
+ * static device array inside the library instead of a caller workspace; every
+ * GPU that loads the library reserves that array until the process exits.
+ * With dq_mode SFA_DQ_AUTO, dQ runs as its own pass (SFA_DQ_SEPARATE) when the
+ * fused accumulator would not fit; problems whose workspace still exceeds
+ * 32 MiB are refused with SFA_ERR_WORKSPACE before anything is launched.  The first call on a device
+ * looks up the array's device address; make it before any stream capture.
+ * Calls share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller. */
+int sfa_bwd_noalloc(const SfaParams* p, void* stream);
 
 /* Inverted index alone (for tests): for every (sequence, kv head, block) the
  * list of query rows that selected it, ascending by (query, slot).  Layout in

@@ -21,6 +21,7 @@ SFA_ERR_DEVICE_TIMEOUT = -5
 
 SFA_DKV_AUTO, SFA_DKV_INVERTED, SFA_DKV_ATOMIC = 0, 1, 2
 SFA_KERNEL_AUTO, SFA_KERNEL_TCGEN05, SFA_KERNEL_GENERAL = 0, 1, 2
+SFA_DQ_AUTO, SFA_DQ_SEPARATE, SFA_DQ_FUSED = 0, 1, 2
 
 _c_void_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -40,7 +41,7 @@ class SfaParams(ctypes.Structure):
         ("batch", _i32), ("q_len", _i32), ("kv_len", _i32), ("total_q", _i32), ("total_kv", _i32),
         ("h_q", _i32), ("h_kv", _i32), ("d_qk", _i32), ("d_v", _i32), ("block_size", _i32),
         ("topk", _i32), ("scale", ctypes.c_float), ("causal", _i32), ("dkv_mode", _i32),
-        ("kernel", _i32), ("reserved", _i32 * 3),
+        ("kernel", _i32), ("dq_mode", _i32), ("reserved", _i32 * 2),
     ]
 
 

@@ -103,6 +103,8 @@ static int validate(const SfaParams* p, bool bwd) {
     return fail(SFA_ERR_INVALID_ARGUMENT, "unknown dkv_mode");
   if (p->kernel != SFA_KERNEL_AUTO && p->kernel != SFA_KERNEL_TCGEN05 && p->kernel != SFA_KERNEL_GENERAL)
     return fail(SFA_ERR_INVALID_ARGUMENT, "unknown kernel family");
+  if (bwd && p->dq_mode != SFA_DQ_AUTO && p->dq_mode != SFA_DQ_SEPARATE && p->dq_mode != SFA_DQ_FUSED)
+    return fail(SFA_ERR_INVALID_ARGUMENT, "unknown dq_mode");
   return SFA_OK;
 }
 
@@ -135,7 +137,14 @@ static int resolve_dkv_mode(const SfaParams& p, int family) {
   return SFA_DKV_INVERTED;
 }
 
-BwdLayout bwd_layout(const SfaParams& p, int family, int dkv_mode) {
+// dQ fused into the key-centric pass needs its dS, so only the tensor-core
+// family with the inverted-index dK/dV offers it; AUTO takes it.
+static int resolve_dq_mode(const SfaParams& p, int family, int dkv_mode) {
+  if (family != SFA_KERNEL_TCGEN05 || dkv_mode != SFA_DKV_INVERTED) return SFA_DQ_SEPARATE;
+  return p.dq_mode == SFA_DQ_SEPARATE ? SFA_DQ_SEPARATE : SFA_DQ_FUSED;
+}
+
+BwdLayout bwd_layout(const SfaParams& p, int family, int dkv_mode, int dq_mode) {
   BwdLayout L{};
   const int64_t rows = num_rows_host(p);
   const int64_t kvr = kv_rows_host(p);
@@ -176,6 +185,11 @@ BwdLayout bwd_layout(const SfaParams& p, int family, int dkv_mode) {
     L.sched = off;
     off = align256(off + sizeof(int32_t));
   }
+  L.fused_dq = (family == SFA_KERNEL_TCGEN05 && L.inverted_dkv && dq_mode == SFA_DQ_FUSED);
+  if (L.fused_dq) {
+    L.dq_acc = off;
+    off = align256(off + sizeof(float) * (size_t)rows * p.h_q * p.d_qk);
+  }
   L.total = off;
   return L;
 }
@@ -215,7 +229,8 @@ size_t sfa_bwd_workspace_bytes(const SfaParams* p) {
   std::string why;
   int fam = select_family(*p, true, &why);
   if (fam < 0) return 0;
-  return bwd_layout(*p, fam, resolve_dkv_mode(*p, fam)).total;
+  const int dkv = resolve_dkv_mode(*p, fam);
+  return bwd_layout(*p, fam, dkv, resolve_dq_mode(*p, fam, dkv)).total;
 }
 
 int sfa_fwd(const SfaParams* p, void* workspace, size_t workspace_bytes, void* stream) {
@@ -240,7 +255,7 @@ static int bwd_common(const SfaParams* p, void* ws, size_t ws_bytes, int* fam, i
   *fam = select_family(*p, true, &why);
   if (*fam < 0) return fail(*fam, why);
   *mode = resolve_dkv_mode(*p, *fam);
-  *L = bwd_layout(*p, *fam, *mode);
+  *L = bwd_layout(*p, *fam, *mode, resolve_dq_mode(*p, *fam, *mode));
   if (L->total > 0 && (ws == nullptr || ws_bytes < L->total))
     return fail(SFA_ERR_WORKSPACE, "workspace too small: need " + std::to_string(L->total) + " bytes, got " +
                                        std::to_string(ws_bytes));
@@ -271,7 +286,10 @@ int sfa_bwd_dq(const SfaParams* p, void* workspace, size_t workspace_bytes, void
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const float* delta = reinterpret_cast<const float*>(ws + L.delta);
   cudaError_t e;
-  if (fam == SFA_KERNEL_TCGEN05) {
+  if (L.fused_dq) {
+    // the dK/dV pass accumulates dQ: start from zero
+    e = cudaMemsetAsync(ws + L.dq_acc, 0, sizeof(float) * (size_t)num_rows_host(*p) * p->h_q * p->d_qk, st);
+  } else if (fam == SFA_KERNEL_TCGEN05) {
     e = launch_bwd_dq_tc(*p, delta, st);
   } else {
     // the general kernel computes dq together with the dk/dv atomics
@@ -296,8 +314,10 @@ int sfa_bwd_dkdv(const SfaParams* p, void* workspace, size_t workspace_bytes, vo
   const float* delta = reinterpret_cast<const float*>(ws + L.delta);
   cudaError_t e;
   if (mode == SFA_DKV_INVERTED) {
+    float* dq_acc = L.fused_dq ? reinterpret_cast<float*>(ws + L.dq_acc) : nullptr;
     e = launch_inverted_index(*p, L, ws, st);
-    if (e == cudaSuccess) e = launch_bwd_dkdv_tc(*p, L, ws, delta, st);
+    if (e == cudaSuccess) e = launch_bwd_dkdv_tc(*p, L, ws, delta, dq_acc, st);
+    if (e == cudaSuccess && dq_acc) e = launch_convert_dq(*p, dq_acc, st);
   } else {
     float* dk_acc = reinterpret_cast<float*>(ws + L.dk_acc);
     float* dv_acc = reinterpret_cast<float*>(ws + L.dv_acc);
@@ -330,7 +350,7 @@ int sfa_bwd(const SfaParams* p, void* workspace, size_t workspace_bytes, void* s
 int sfa_build_inverted_index(const SfaParams* p, void* workspace, size_t workspace_bytes, void* stream) {
   int rc = validate(p, true);
   if (rc) return rc;
-  BwdLayout L = bwd_layout(*p, SFA_KERNEL_TCGEN05, SFA_DKV_INVERTED);
+  BwdLayout L = bwd_layout(*p, SFA_KERNEL_TCGEN05, SFA_DKV_INVERTED, SFA_DQ_SEPARATE);
   if (workspace == nullptr || workspace_bytes < L.total)
     return fail(SFA_ERR_WORKSPACE, "workspace too small: need " + std::to_string(L.total) + " bytes");
   cudaError_t e = launch_inverted_index(*p, L, reinterpret_cast<char*>(workspace),
@@ -343,7 +363,7 @@ int sfa_inverted_index_layout(const SfaParams* p, size_t* offsets_off, size_t* e
                               int32_t* units) {
   int rc = validate(p, true);
   if (rc) return rc;
-  BwdLayout L = bwd_layout(*p, SFA_KERNEL_TCGEN05, SFA_DKV_INVERTED);
+  BwdLayout L = bwd_layout(*p, SFA_KERNEL_TCGEN05, SFA_DKV_INVERTED, SFA_DQ_SEPARATE);
   if (offsets_off) *offsets_off = L.inv_offsets;
   if (entries_off) *entries_off = L.inv_entries;
   if (nblk) *nblk = L.nblk;

@@ -28,6 +28,7 @@ struct BwdLayout {
   size_t inv_entries;  // int32 [pairs]                   (inverted path)
   size_t inv_cursor;   // int32 [units * nblk]            (inverted path scratch)
   size_t sched;        // int32 work counter               (inverted path)
+  size_t dq_acc;       // float [rows * h_q * d_qk]       (fused dQ)
   size_t total;
   int pre_ctas;
   int nblk;
@@ -35,11 +36,12 @@ struct BwdLayout {
   int64_t pairs;
   bool atomic_dkv;
   bool inverted_dkv;
+  bool fused_dq;
 };
 
 constexpr int kPreRows = 16;  // query rows per preprocess CTA
 
-BwdLayout bwd_layout(const SfaParams& p, int kernel_family, int dkv_mode);
+BwdLayout bwd_layout(const SfaParams& p, int kernel_family, int dkv_mode, int dq_mode);
 
 // general (CUDA-core) family
 cudaError_t launch_fwd_general(const SfaParams& p, cudaStream_t st);
@@ -52,6 +54,8 @@ int general_head_group(const SfaParams& p);
 // backward preprocessing / epilogues
 cudaError_t launch_preprocess(const SfaParams& p, float* delta, float* dsink_part, int pre_ctas, cudaStream_t st);
 cudaError_t launch_convert_dkdv(const SfaParams& p, const float* dk_acc, const float* dv_acc, cudaStream_t st);
+// dq = bf16(scale * dq_acc), dq_acc fp32 [rows][h_q][d_qk]
+cudaError_t launch_convert_dq(const SfaParams& p, const float* dq_acc, cudaStream_t st);
 
 // inverted block->query index
 cudaError_t launch_inverted_index(const SfaParams& p, const BwdLayout& L, char* ws, cudaStream_t st);
@@ -62,7 +66,8 @@ bool tc_bwd_supported(const SfaParams& p, const char** why);
 cudaError_t launch_fwd_tc(const SfaParams& p, cudaStream_t st);
 cudaError_t launch_bwd_dq_tc(const SfaParams& p, const float* delta, cudaStream_t st);
 bool tc_dkdv_available();
-cudaError_t launch_bwd_dkdv_tc(const SfaParams& p, const BwdLayout& L, char* ws, const float* delta,
+// dq_acc: fused dQ accumulator (fp32 [rows][h_q][d_qk], zeroed) or null
+cudaError_t launch_bwd_dkdv_tc(const SfaParams& p, const BwdLayout& L, char* ws, const float* delta, float* dq_acc,
                                cudaStream_t st);
 
 int device_sm_count();

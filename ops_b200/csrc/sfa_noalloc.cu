@@ -55,7 +55,18 @@ static void* noalloc_scratch_ptr(cudaError_t* err) {
 
 extern "C" int sfa_bwd_noalloc(const SfaParams* p, void* stream) {
   using namespace sfa;
-  const size_t need = sfa_bwd_workspace_bytes(p);
+  size_t need = sfa_bwd_workspace_bytes(p);
+  SfaParams sep;
+  if (need > kNoAllocScratchBytes && p != nullptr && p->dq_mode == SFA_DQ_AUTO) {
+    // the fused dQ's accumulator does not fit: compute dQ in its own pass
+    sep = *p;
+    sep.dq_mode = SFA_DQ_SEPARATE;
+    const size_t need_sep = sfa_bwd_workspace_bytes(&sep);
+    if (need_sep != 0 && need_sep <= kNoAllocScratchBytes) {
+      p = &sep;
+      need = need_sep;
+    }
+  }
   if (need == 0) {
     // invalid or unsupported parameters (or nothing to stage): sfa_bwd reports
     // the reason before launching anything

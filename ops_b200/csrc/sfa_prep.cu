@@ -137,6 +137,50 @@ cudaError_t launch_convert_dkdv(const SfaParams& p, const float* dk_acc, const f
   return cudaGetLastError();
 }
 
+// dq = bf16(scale * acc) for the fused dQ: acc is fp32 [rows][h_q][d_qk]; four
+// consecutive dims per thread (d_qk % 4 == 0), written as one 8-byte store when
+// the dq rows allow it (kVec), else element by element.
+template <bool kVec>
+__global__ void convert_dq_kernel(SfaParams p, const float* __restrict__ acc) {
+  const int D = p.d_qk;
+  const int64_t rows = p.cu_seqlens_q == nullptr ? (int64_t)p.batch * p.q_len : (int64_t)p.total_q;
+  const int64_t n4 = rows * p.h_q * (D / 4);
+  __nv_bfloat16* dq = reinterpret_cast<__nv_bfloat16*>(p.dq);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const int d = (int)(i % (D / 4)) * 4;
+    const int64_t rh = i / (D / 4);
+    const int h = (int)(rh % p.h_q);
+    const int row = (int)(rh / p.h_q);
+    int64_t b = 0, t = row;
+    if (p.cu_seqlens_q == nullptr) { b = row / p.q_len; t = row - b * p.q_len; }
+    const float4 v = reinterpret_cast<const float4*>(acc)[i];
+    __nv_bfloat16* o = dq + b * p.dq_sb + t * p.dq_st + h * p.dq_sh + d;
+    if (kVec) {
+      uint2 w;
+      w.x = pack_bf16x2_rn(v.x * p.scale, v.y * p.scale);
+      w.y = pack_bf16x2_rn(v.z * p.scale, v.w * p.scale);
+      *reinterpret_cast<uint2*>(o) = w;
+    } else {
+      o[0] = f2bf(v.x * p.scale);
+      o[1] = f2bf(v.y * p.scale);
+      o[2] = f2bf(v.z * p.scale);
+      o[3] = f2bf(v.w * p.scale);
+    }
+  }
+}
+
+cudaError_t launch_convert_dq(const SfaParams& p, const float* dq_acc, cudaStream_t st) {
+  const int grid = device_sm_count() * 8;
+  const bool vec = (reinterpret_cast<uintptr_t>(p.dq) % 8 == 0) && p.dq_sb % 4 == 0 && p.dq_st % 4 == 0 &&
+                   p.dq_sh % 4 == 0;
+  if (vec)
+    convert_dq_kernel<true><<<grid, 256, 0, st>>>(p, dq_acc);
+  else
+    convert_dq_kernel<false><<<grid, 256, 0, st>>>(p, dq_acc);
+  note_launch();
+  return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------------------
 // inverted index: for unit u = (sequence, kv head) and block e, the query rows
 // that selected e.  Order inside a list: (sub-chunk of 32 rows, slot, lane) —

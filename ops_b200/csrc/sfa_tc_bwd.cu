@@ -19,6 +19,12 @@
 // dK^T/dV^T stay in TMEM for the whole block; each key block is written once,
 // in a fixed order (no atomics): deterministic.  Replaces `_attn_bwd_dk_dv` /
 // `_inner_dkv` (SFA.py:719-853, 1005-1145) and its fp32 atomics (SFA.py:853).
+//
+// Fused dQ (SFA_DQ_FUSED): the same pass also forms
+//     dQ^T += K_e^T . dS^T                            (M = 128 dims, N = 128 rows)
+// per batch and adds it to an fp32 [rows][h_q][d_qk] accumulator with
+// coalesced fp32 reductions (a warp covers 32 dims of one row); the dQ pass
+// above, which recomputes S and dP at N = 16, is then not run.
 #include "sfa_common.cuh"
 #include "sfa_internal.h"
 #include "sfa_tc_common.cuh"
@@ -514,7 +520,8 @@ constexpr int kQB = 8;              // queries per batch (x 16 heads = 128 MMA r
 constexpr int kMeta = 6;            // batch metadata ring depth
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColSdP = 0;     // 2 slots x (64 S + 64 dP)
-constexpr uint32_t kColAcc = 256;   // 2 buffers x (64 dV^T + 64 dK^T)
+constexpr uint32_t kColAcc = 256;   // 2 buffers x (64 dV^T + 64 dK^T); 1 buffer with the fused dQ
+constexpr uint32_t kColDQ = 384;    // fused dQ: dQ^T partial of one batch (128 dims x 128 rows)
 
 struct JobDesc {
   int e, b, hk, kv0, kv_len, n, list0, flags;
@@ -544,6 +551,7 @@ struct Smem {
   uint64_t meta_full[kMeta], meta_empty[kMeta];
   uint64_t sdp_full[2], sdp_empty[2], pds_full, pds_empty;
   uint64_t acc_full[2], acc_empty[2];
+  uint64_t dq_full, dq_empty;         // fused dQ partial (TMEM) hand-off
   uint64_t jd_full[kJD], jd_empty[kJD];
   uint32_t tmem_base;
 };
@@ -551,6 +559,7 @@ struct Smem {
 struct Args {
   SfaParams p;
   const float* delta;
+  float* dq_acc;            // fused dQ: fp32 [rows][h_q][d_qk] accumulator (zeroed by the host), else null
   const int32_t* offsets;   // [units * nblk + 1]
   const int32_t* entries;   // query rows
   int* sched;               // work counter (zeroed by the host)
@@ -570,7 +579,7 @@ __device__ __forceinline__ bool wtw(uint64_t* bar, uint32_t parity, int32_t* sta
   return __all_sync(0xffffffffu, wt(bar, parity, status, site));
 }
 
-template <int D>
+template <int D, bool kDQ>
 __global__ void __launch_bounds__(kThreads, 1)
 sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUtensorMap tmq,
                        const __grid_constant__ CUtensorMap tmdo, const __grid_constant__ CUtensorMap tmk,
@@ -601,6 +610,8 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
     mbar_init(&sm.kv_empty, 1);
     mbar_init(&sm.pds_full, kWG / 32);
     mbar_init(&sm.pds_empty, 1);
+    mbar_init(&sm.dq_full, 1);
+    mbar_init(&sm.dq_empty, kWG / 32);
     // consumers of a job descriptor: the two issuers, the two loader threads, P/dS warps
     for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 4 + kWG / 32); }
     fence_barrier_init();
@@ -802,19 +813,29 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
           mma_commit(&sm.sdp_full[s]);
         }
         if (!ok) break;
-        mma_commit(&sm.kv_empty);
+        // K_e / V_e are free once their last reader retires: these S/dP MMAs,
+        // or with the fused dQ the dQ MMAs of the job's last batch (the other
+        // issuer commits then)
+        if (!kDQ || nb == 0) mma_commit(&sm.kv_empty);
         ++job;
       }
     }
   } else if (warp == 11) {
-    // ============================================================ dV/dK issuer
+    // ============================================================ dV/dK (and dQ) issuer
     // A second issuing thread: while one waits, the other's MMAs keep the
     // tensor pipe busy.
     if (lane == 0) {
       const uint32_t id_acc = idesc_bf16(128, 64, true, true);
+      // fused dQ: dQ^T[dims, rows] = K_e^T[dims, keys] . dS^T[keys, rows]
+      // (A = K_e read MN-major: 64-dim slabs 8 KB apart, 8-key groups 1 KB
+      // apart; B = dS read K-major: 8-row groups 1 KB apart)
+      const uint32_t id_dq = idesc_bf16(128, 128, true, false);
       const uint32_t lbo_rows = D == 128 ? 128u * 128u : 0u;   // 64-dim slabs of the 128-row buffers
       const uint64_t pdsc = smem_desc(smem_u32(&sm.pbuf[0]), 0, 1024, kSw128);
       const uint64_t dd = smem_desc(smem_u32(&sm.dsbuf[0]), 0, 1024, kSw128);
+      const uint64_t kdq = smem_desc(smem_u32(&sm.ke[0]), D == 128 ? 64u * 128u : 0u, 1024, kSw128);
+      const uint64_t ddq = smem_desc(smem_u32(&sm.dsbuf[0]), 16, 1024, kSw128);
+      constexpr int kNAcc = kDQ ? 1 : 2;   // accumulator buffers
       bool ok = true;
       int job = 0, gb = 0;
       while (ok) {
@@ -823,8 +844,8 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         const int flags = sm.jd[js].flags, n = sm.jd[js].n;
         if (flags & kSentinel) break;
         mbar_arrive(&sm.jd_empty[js]);
-        const int ab = job & 1;
-        if (!(ok = wt(&sm.acc_empty[ab], ((job >> 1) & 1) ^ 1, st, 11))) break;
+        const int ab = job % kNAcc, use = job / kNAcc;
+        if (!(ok = wt(&sm.acc_empty[ab], (use & 1) ^ 1, st, 11))) break;
         tc_fence_after();
         const int nb = (n + kQB - 1) / kQB;
         const uint32_t acc = tmem + kColAcc + ab * 128;
@@ -841,12 +862,23 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
             mma_bf16_ss(acc, od + (uint64_t)(kk * 128), pdsc + (uint64_t)(kk * 128), id_acc, accum);
             mma_bf16_ss(acc + 64, qd + (uint64_t)(kk * 128), dd + (uint64_t)(kk * 128), id_acc, accum);
           }
+          if (kDQ) {
+            // the P/dS warps read the previous batch's partial out of TMEM after
+            // handing over this batch's P/dS
+            if (!(ok = wt(&sm.dq_empty, (gb & 1) ^ 1, st, 19))) break;
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)   // 16 keys per step: +2048 B of K_e, +32 B of dS rows
+              mma_bf16_ss(tmem + kColDQ, kdq + (uint64_t)(kk * 128), ddq + (uint64_t)(kk * 2), id_dq, kk != 0);
+            mma_commit(&sm.dq_full);
+          }
           // the S/dP MMAs of this batch retired before its P/dS were written, so
           // this commit frees the batch buffers for both issuers
           mma_commit(&sm.b_empty[s]);
           mma_commit(&sm.pds_empty);
         }
         if (!ok) break;
+        if (kDQ && nb > 0) mma_commit(&sm.kv_empty);   // the dQ MMAs read K_e
         mma_commit(&sm.acc_full[ab]);   // with no batches the epilogue writes zeros
         ++job;
       }
@@ -863,14 +895,44 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
     const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
     const float c2 = p.scale * kLog2e;
     const bool shared_kv = p.dk == p.dv;
+    constexpr int kNAcc = kDQ ? 1 : 2;
     int job = 0, gb = 0;
     bool ok = true;
+    // fused dQ: the partial of batch `pend_gb` waits in TMEM until the next
+    // batch's P/dS are handed over; thread = dim, warpgroup wg takes rows
+    // 64*wg .. 64*wg+63 = queries 4*wg .. 4*wg+3 (16 heads each)
+    bool pend = false;
+    int pend_gb = 0, pend_hk = 0, pend_rid[4] = {-1, -1, -1, -1};
+    auto drain_dq = [&]() -> bool {
+      if (!kDQ || !pend) return true;
+      pend = false;
+      if (!wtw(&sm.dq_full, pend_gb & 1, st, 25)) return false;
+      tc_fence_after();
+      float part[4][16];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tmem_ld16(tl + kColDQ + wg * 64 + i * 16, part[i]);
+      tmem_ld_wait();
+      tc_fence_before();
+      warp_arrive(&sm.dq_empty);
+      if (lrow < D) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (pend_rid[i] >= 0) {
+            float* dst = args.dq_acc + ((int64_t)pend_rid[i] * p.h_q + pend_hk * G) * D + lrow;
+#pragma unroll
+            for (int hh = 0; hh < 16; ++hh)
+              if (hh < G) atomicAdd(dst + hh * D, part[i][hh]);   // one 128-byte row per warp
+          }
+        }
+      }
+      return true;
+    };
     while (ok) {
       const int js = job % kJD;
       if (!(ok = wtw(&sm.jd_full[js], (job / kJD) & 1, st, 20))) break;
       const JobDesc& d = sm.jd[js];
       if (d.flags & kSentinel) break;
-      const int ab = job & 1;
+      const int ab = job % kNAcc, use = job / kNAcc;
       const int nb = (d.n + kQB - 1) / kQB;
       const int key_base = d.e * 64 + wg * 32;
       const int kv_len = d.kv_len;
@@ -888,6 +950,12 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
           dl = __ldg(args.delta + (int64_t)mt.rowid[jq] * p.h_q + hh);
         }
         const bool rvalid = lse2 != -INFINITY;
+        int rid[4] = {-1, -1, -1, -1};
+        if (kDQ) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (wg * 4 + i < mt.m) rid[i] = mt.rowid[wg * 4 + i];
+        }
         warp_arrive(&sm.meta_empty[slot]);
         // keys of this warpgroup valid for this row: key_base + i < lim
         int lim = rvalid ? min(kv_len, p.causal ? pos + 1 : kv_len) - key_base : 0;
@@ -923,10 +991,18 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         }
         fence_proxy_async_smem();
         warp_arrive(&sm.pds_full);
+        if (kDQ) {
+          if (!(ok = drain_dq())) break;   // the previous batch's partial
+          pend = true;
+          pend_gb = gb;
+          pend_hk = d.hk;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) pend_rid[i] = rid[i];
+        }
       }
       if (!ok) break;
       // epilogue: thread = dim; this warpgroup's 32 keys of dV^T and dK^T
-      if (!(ok = wtw(&sm.acc_full[ab], (job >> 1) & 1, st, 23))) break;
+      if (!(ok = wtw(&sm.acc_full[ab], use & 1, st, 23))) break;
       tc_fence_after();
       const bool has = nb > 0;
       __nv_bfloat16* dkp = reinterpret_cast<__nv_bfloat16*>(p.dk) + d.b * p.dk_sb + (int64_t)d.hk * p.dk_sh + lrow;
@@ -963,6 +1039,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       warp_arrive(&sm.jd_empty[js]);
       ++job;
     }
+    if (ok) drain_dq();   // the last batch's partial
   }
 
   tc_fence_before();
@@ -971,8 +1048,9 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
-template <int D>
-cudaError_t launch(const SfaParams& p, const BwdLayout& L, char* ws, const float* delta, cudaStream_t stream) {
+template <int D, bool kDQ>
+cudaError_t launch(const SfaParams& p, const BwdLayout& L, char* ws, const float* delta, float* dq_acc,
+                   cudaStream_t stream) {
   CUtensorMap tq, tdo, tk, tv;
   const int G = p.h_q / p.h_kv;
   const bool vl = p.cu_seqlens_q != nullptr;
@@ -993,6 +1071,7 @@ cudaError_t launch(const SfaParams& p, const BwdLayout& L, char* ws, const float
   Args a;
   a.p = p;
   a.delta = delta;
+  a.dq_acc = dq_acc;
   a.offsets = reinterpret_cast<const int32_t*>(ws + L.inv_offsets);
   a.entries = reinterpret_cast<const int32_t*>(ws + L.inv_entries);
   a.sched = reinterpret_cast<int*>(ws + L.sched);
@@ -1005,10 +1084,10 @@ cudaError_t launch(const SfaParams& p, const BwdLayout& L, char* ws, const float
   if (e != cudaSuccess) return e;
   static_assert(sizeof(Smem<D>) + 1024 <= 227 * 1024, "shared memory budget");
   const size_t smem = sizeof(Smem<D>) + 1024;
-  e = cudaFuncSetAttribute(sfa_bwd_dkdv_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  e = cudaFuncSetAttribute(sfa_bwd_dkdv_tc_kernel<D, kDQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int grid = a.nitems < device_sm_count() ? a.nitems : device_sm_count();
-  sfa_bwd_dkdv_tc_kernel<D><<<grid, kThreads, smem, stream>>>(a, tq, tdo, tk, tv);
+  sfa_bwd_dkdv_tc_kernel<D, kDQ><<<grid, kThreads, smem, stream>>>(a, tq, tdo, tk, tv);
   note_launch();
   return cudaGetLastError();
 }
@@ -1028,9 +1107,13 @@ cudaError_t launch_bwd_dq_tc(const SfaParams& p, const float* delta, cudaStream_
   return p.d_qk == 128 ? bwd::dq::launch<128>(p, delta, st) : bwd::dq::launch<64>(p, delta, st);
 }
 
-cudaError_t launch_bwd_dkdv_tc(const SfaParams& p, const BwdLayout& L, char* ws, const float* delta,
+cudaError_t launch_bwd_dkdv_tc(const SfaParams& p, const BwdLayout& L, char* ws, const float* delta, float* dq_acc,
                                cudaStream_t st) {
-  return p.d_qk == 128 ? bwd::dkdv::launch<128>(p, L, ws, delta, st) : bwd::dkdv::launch<64>(p, L, ws, delta, st);
+  if (dq_acc)
+    return p.d_qk == 128 ? bwd::dkdv::launch<128, true>(p, L, ws, delta, dq_acc, st)
+                         : bwd::dkdv::launch<64, true>(p, L, ws, delta, dq_acc, st);
+  return p.d_qk == 128 ? bwd::dkdv::launch<128, false>(p, L, ws, delta, nullptr, st)
+                       : bwd::dkdv::launch<64, false>(p, L, ws, delta, nullptr, st);
 }
 
 }  // namespace sfa

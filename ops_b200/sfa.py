@@ -34,6 +34,7 @@ from ._lib import SfaParams
 
 _DKV = {"auto": _lib.SFA_DKV_AUTO, "inverted": _lib.SFA_DKV_INVERTED, "atomic": _lib.SFA_DKV_ATOMIC}
 _KERNEL = {"auto": _lib.SFA_KERNEL_AUTO, "tcgen05": _lib.SFA_KERNEL_TCGEN05, "general": _lib.SFA_KERNEL_GENERAL}
+_DQ = {"auto": _lib.SFA_DQ_AUTO, "separate": _lib.SFA_DQ_SEPARATE, "fused": _lib.SFA_DQ_FUSED}
 
 
 @dataclass(frozen=True)
@@ -47,6 +48,7 @@ class _Cfg:
     dkv_mode: int
     kernel: int
     shared_kv: bool
+    dq_mode: int = 0
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -109,6 +111,7 @@ def build_params(q, k, v, idx, o, lse, cfg: _Cfg, sink=None, cu_q=None, cu_k=Non
     P.causal = 1 if cfg.causal else 0
     P.dkv_mode = cfg.dkv_mode
     P.kernel = cfg.kernel
+    P.dq_mode = cfg.dq_mode
     return P
 
 
@@ -178,7 +181,8 @@ def sparse_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bl
                            cu_seqlens: Optional[torch.Tensor] = None, attn_sink: Optional[torch.Tensor] = None,
                            causal: bool = True, cu_seqlens_k: Optional[torch.Tensor] = None,
                            max_seqlen_q: Optional[int] = None, max_seqlen_k: Optional[int] = None,
-                           dkv_mode: str = "auto", kernel: str = "auto") -> Tuple[torch.Tensor, torch.Tensor]:
+                           dkv_mode: str = "auto", kernel: str = "auto",
+                           dq_mode: str = "auto") -> Tuple[torch.Tensor, torch.Tensor]:
     """Block-sparse attention over selected kv blocks; returns ``(o, lse)``.
 
     Dense: ``q [B,T,Hq,Dqk]``, ``k [B,Tk,Hk,Dqk]``, ``v [B,Tk,Hk,Dv]``,
@@ -188,6 +192,8 @@ def sparse_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bl
     natural-log log-sum-exp ``[.., Hq]`` (fp32); it carries no gradient.
     ``attn_sink`` (``[Hq]`` fp32) adds ``exp(sink)`` to every denominator.
     If ``k is v`` their rows are shared and one gradient ``dk + dv`` flows back.
+    ``dkv_mode`` ("inverted" | "atomic"), ``dq_mode`` ("separate" | "fused") and
+    ``kernel`` ("tcgen05" | "general") override the launch table ("auto").
     """
     _check_inputs(q, k, v, block_indices)
     if block_size <= 0:
@@ -207,7 +213,7 @@ def sparse_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bl
         scale = 1.0 / math.sqrt(q.shape[-1])
     shared = k is v
     cfg = _Cfg(int(block_size), float(scale), bool(causal), varlen, int(max_seqlen_q), int(max_seqlen_k),
-               _DKV[dkv_mode], _KERNEL[kernel], shared)
+               _DKV[dkv_mode], _KERNEL[kernel], shared, _DQ[dq_mode])
     sink = None if attn_sink is None else attn_sink.float()
     kk = _inner_contig(k)
     vv = kk if shared else _inner_contig(v)

@@ -56,7 +56,7 @@ def assert_lse(got, ref):
 
 
 def run_op(q, k, v, idx, bs, scale=None, sink=None, causal=True, do=None, cu_q=None, cu_k=None,
-           max_q=None, max_k=None, dkv_mode="auto", kernel="auto", shared_kv=False):
+           max_q=None, max_k=None, dkv_mode="auto", kernel="auto", shared_kv=False, dq_mode="auto"):
     """CUDA op forward (+ backward if do is given).  Returns dict of CPU tensors."""
     import ops_b200
     dev = torch.device("cuda")
@@ -71,7 +71,7 @@ def run_op(q, k, v, idx, bs, scale=None, sink=None, causal=True, do=None, cu_q=N
     o, lse = ops_b200.sparse_flash_attention(
         qg, kg, vg, idx.to(dev), bs, scale, cu_seqlens=None if cu_q is None else cu_q.to(dev), attn_sink=sg,
         causal=causal, cu_seqlens_k=None if cu_k is None else cu_k.to(dev), max_seqlen_q=max_q,
-        max_seqlen_k=max_k, dkv_mode=dkv_mode, kernel=kernel)
+        max_seqlen_k=max_k, dkv_mode=dkv_mode, kernel=kernel, dq_mode=dq_mode)
     out = dict(o=o.detach().cpu(), lse=lse.detach().cpu())
     if do is not None:
         o.backward(do.to(dev))

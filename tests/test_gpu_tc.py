@@ -29,6 +29,23 @@ def test_tc_forward_backward(cfg):
     check_all(got, ref)
 
 
+@pytest.mark.parametrize("dq_mode", ["separate", "fused"])
+@pytest.mark.parametrize("cfg,shared", [
+    (W.scaled(W.CONFIGS["c2"], B=2, T=1024, Hq=32, Hk=2, S=8), False),
+    (W.scaled(W.CONFIGS["c2"], B=1, T=2048, Hq=8, Hk=1, S=16, Dqk=64, Dv=64), False),
+    (W.scaled(W.CONFIGS["c2"], B=1, T=1500, Hq=12, Hk=1, S=12), True),
+], ids=["g16_d128", "g8_d64", "g12_shared_kv"])
+def test_tc_dq_modes(cfg, shared, dq_mode):
+    # dQ in its own query-centric pass, or accumulated by the key-centric dK/dV
+    # pass (fp32 reductions): both against the oracle
+    d, s = _case(cfg, 13)
+    v = d["k"] if shared else d["v"]
+    got = run_op(d["q"], d["k"], v, d["idx"], cfg.bs, cfg.scale, s, True, d["do"], kernel="tcgen05",
+                 dkv_mode="inverted", shared_kv=shared, dq_mode=dq_mode)
+    ref = run_oracle(d["q"], d["k"], v, d["idx"], cfg.bs, cfg.scale, s, True, d["do"], o_for_bwd=got["o"])
+    check_all(got, ref, shared_kv=shared)
+
+
 def test_tc_forward_decode_varlen():
     cfg = W.scaled(W.CONFIGS["c5"], n_seqs=8, kv_min=200, kv_max=5000, Hq=16, Hk=2, S=32)
     d = W.make_inputs(cfg, "cpu", 4)
