@@ -245,6 +245,9 @@ def run_ours(args, cfg):
     P = S.build_params(q, k, v, idx, o, lse, scfg, None, None, None, do, dq, dk, dv, None)
     fam_f = lib.sfa_select_kernel(ctypes.byref(P), 0)
     fam_b = lib.sfa_select_kernel(ctypes.byref(P), 1)
+    dkv_mode, dq_mode = ctypes.c_int32(), ctypes.c_int32()
+    _lib.check(min(0, lib.sfa_bwd_plan(ctypes.byref(P), ctypes.byref(dkv_mode), ctypes.byref(dq_mode))), "plan")
+    fused_dq = dq_mode.value == _lib.SFA_DQ_FUSED
     nbytes = lib.sfa_bwd_workspace_bytes(ctypes.byref(P))
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -344,14 +347,21 @@ def run_ours(args, cfg):
     # algorithmic FLOPs owned by each stage (recomputation not counted)
     two_p = 2.0 * pairs
     tc_bwd = fam_b == _lib.SFA_KERNEL_TCGEN05
+    # with the fused dQ the dK/dV stage also owns dQ = dS.K (2P.Dqk) and the dQ
+    # stage only clears the accumulator
     stage_flops = {"fwd": fl.fwd,
                    "bwd_preprocess": 0.0,
-                   "bwd_dq": two_p * (2 * cfg.Dqk + cfg.Dv) if tc_bwd else fl.bwd,
-                   "bwd_dkdv": two_p * (cfg.Dqk + cfg.Dv) if tc_bwd else 0.0}
+                   "bwd_dq": 0.0 if fused_dq else (two_p * (2 * cfg.Dqk + cfg.Dv) if tc_bwd else fl.bwd),
+                   "bwd_dkdv": (two_p * (2 * cfg.Dqk + cfg.Dv) if fused_dq else two_p * (cfg.Dqk + cfg.Dv))
+                   if tc_bwd else 0.0}
     dom = max(stages, key=lambda s: stage_ms[s])
     # K and V rows gathered per (row, kv head): selected keys x (Dqk + Dv) bf16
     kv_gather = pairs / G * (cfg.Dqk + cfg.Dv) * 2.0
-    gather_bytes = {"fwd": kv_gather, "bwd_dq": kv_gather} if tc_bwd else {}
+    # dK/dV: each selected (block, query) gathers the query's G heads of q and dO
+    qdo_gather = pairs / cfg.bs * (cfg.Dqk + cfg.Dv) * 2.0
+    gather_bytes = {"fwd": kv_gather, "bwd_dkdv": qdo_gather} if tc_bwd else {}
+    if tc_bwd and not fused_dq:
+        gather_bytes["bwd_dq"] = kv_gather
     ach = stage_flops[dom] / (stage_ms[dom] * 1e-3) / 1e12
     value = flops_all / (step_ms_max * 1e-3) / 1e12
     e2e_v = flops_all / (e_ms_max * 1e-3) / 1e12
@@ -364,7 +374,9 @@ def run_ours(args, cfg):
         "tokens_per_s": cfg.B * cfg.T * world / (step_ms_max * 1e-3),
         "selected_pairs_per_rank": pairs,
         "stages_ms": stage_ms,
-        "kernel_family": {"fwd": fams.get(fam_f, str(fam_f)), "bwd": fams.get(fam_b, str(fam_b))},
+        "kernel_family": {"fwd": fams.get(fam_f, str(fam_f)), "bwd": fams.get(fam_b, str(fam_b)),
+                          "dkv": {1: "inverted", 2: "atomic"}.get(dkv_mode.value),
+                          "dq": {1: "separate", 2: "fused"}.get(dq_mode.value)},
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
                      "frac": ach / peak, "peak_kind": f"{peak_kind} bf16 burst",
                      "traffic": NCU_TRAFFIC.get(cfg.name, {}).get(dom) if cfg.B == 4 else None,

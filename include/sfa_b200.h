@@ -137,6 +137,12 @@ unsigned long long sfa_kernel_launches(void);
  * a negative error code if the shape is unsupported. */
 int sfa_select_kernel(const SfaParams* p, int is_backward);
 
+/* The backward's resolved algorithms for these params: *dkv_mode gets
+ * SFA_DKV_INVERTED or SFA_DKV_ATOMIC, *dq_mode SFA_DQ_SEPARATE or SFA_DQ_FUSED
+ * (the launch-table counterpart of SFA.py:51-59; no reference entry point).
+ * Returns the kernel family or a negative error code. */
+int sfa_bwd_plan(const SfaParams* p, int32_t* dkv_mode, int32_t* dq_mode);
+
 /* Workspace (device bytes) the forward / backward need for these params. */
 size_t sfa_fwd_workspace_bytes(const SfaParams* p);
 size_t sfa_bwd_workspace_bytes(const SfaParams* p);

@@ -51,6 +51,7 @@ EXPORTS = {
     "sfa_last_error_string": ([], ctypes.c_char_p),
     "sfa_kernel_launches": ([], ctypes.c_ulonglong),
     "sfa_select_kernel": ([ctypes.POINTER(SfaParams), _i32], _i32),
+    "sfa_bwd_plan": ([ctypes.POINTER(SfaParams), ctypes.POINTER(_i32), ctypes.POINTER(_i32)], _i32),
     "sfa_fwd_workspace_bytes": ([ctypes.POINTER(SfaParams)], ctypes.c_size_t),
     "sfa_bwd_workspace_bytes": ([ctypes.POINTER(SfaParams)], ctypes.c_size_t),
     "sfa_fwd": ([ctypes.POINTER(SfaParams), _c_void_p, ctypes.c_size_t, _c_void_p], _i32),

@@ -219,6 +219,18 @@ int sfa_select_kernel(const SfaParams* p, int is_backward) {
   return fam;
 }
 
+int sfa_bwd_plan(const SfaParams* p, int32_t* dkv_mode, int32_t* dq_mode) {
+  int rc = validate(p, true);
+  if (rc) return rc;
+  std::string why;
+  const int fam = select_family(*p, true, &why);
+  if (fam < 0) return fail(fam, why);
+  const int dkv = resolve_dkv_mode(*p, fam);
+  if (dkv_mode) *dkv_mode = dkv;
+  if (dq_mode) *dq_mode = resolve_dq_mode(*p, fam, dkv);
+  return fam;
+}
+
 size_t sfa_fwd_workspace_bytes(const SfaParams* p) {
   (void)p;
   return 0;

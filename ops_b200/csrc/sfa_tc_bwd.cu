@@ -515,6 +515,7 @@ namespace dkdv {
 
 constexpr int kThreads = 416;       // warp 0 metadata, 1 S/dP issuer, 2-9 P/dS + epilogue, 10 K/V/Q loads,
                                     // 11 dV/dK issuer, 12 dO loads
+constexpr int kThreadsDQ = 544;     // + warps 13-16: fused-dQ reducers
 constexpr int kWG = 256;            // P/dS threads: 2 warpgroups, each takes 32 of the 64 keys
 constexpr int kQB = 8;              // queries per batch (x 16 heads = 128 MMA rows)
 constexpr int kMeta = 6;            // batch metadata ring depth
@@ -580,7 +581,7 @@ __device__ __forceinline__ bool wtw(uint64_t* bar, uint32_t parity, int32_t* sta
 }
 
 template <int D, bool kDQ>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kDQ ? kThreadsDQ : kThreads, 1)
 sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUtensorMap tmq,
                        const __grid_constant__ CUtensorMap tmdo, const __grid_constant__ CUtensorMap tmk,
                        const __grid_constant__ CUtensorMap tmv) {
@@ -604,20 +605,24 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
     // counts in warps for the P/dS warps (one arrival per warp)
     for (int i = 0; i < kMeta; ++i) {
       mbar_init(&sm.meta_full[i], 1);
-      mbar_init(&sm.meta_empty[i], 2 + kWG / 32);   // the two loader threads + P/dS warps
+      mbar_init(&sm.meta_empty[i], 2 + kWG / 32 + (kDQ ? 4 : 0));   // loader threads, P/dS warps, reducers
     }
     mbar_init(&sm.kv_full, 1);
     mbar_init(&sm.kv_empty, 1);
     mbar_init(&sm.pds_full, kWG / 32);
     mbar_init(&sm.pds_empty, 1);
     mbar_init(&sm.dq_full, 1);
-    mbar_init(&sm.dq_empty, kWG / 32);
-    // consumers of a job descriptor: the two issuers, the two loader threads, P/dS warps
-    for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 4 + kWG / 32); }
+    mbar_init(&sm.dq_empty, 4);   // the 4 reducer warps
+    // consumers of a job descriptor: the two issuers, the two loader threads,
+    // P/dS warps and (fused dQ) the reducer warps
+    for (int i = 0; i < kJD; ++i) {
+      mbar_init(&sm.jd_full[i], 1);
+      mbar_init(&sm.jd_empty[i], 4 + kWG / 32 + (kDQ ? 4 : 0));
+    }
     fence_barrier_init();
   }
   // padded head rows (G..15 of every query) stay zero
-  for (int i = threadIdx.x; i < 2 * Smem<D>::kBatchBytes / 16; i += kThreads) {
+  for (int i = threadIdx.x; i < 2 * Smem<D>::kBatchBytes / 16; i += blockDim.x) {
     reinterpret_cast<uint4*>(&sm.qb[0][0])[i] = make_uint4(0, 0, 0, 0);
     reinterpret_cast<uint4*>(&sm.dob[0][0])[i] = make_uint4(0, 0, 0, 0);
   }
@@ -863,8 +868,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
             mma_bf16_ss(acc + 64, qd + (uint64_t)(kk * 128), dd + (uint64_t)(kk * 128), id_acc, accum);
           }
           if (kDQ) {
-            // the P/dS warps read the previous batch's partial out of TMEM after
-            // handing over this batch's P/dS
+            // the reducer warps have read the previous batch's partial out of TMEM
             if (!(ok = wt(&sm.dq_empty, (gb & 1) ^ 1, st, 19))) break;
             tc_fence_after();
 #pragma unroll
@@ -883,6 +887,58 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         ++job;
       }
     }
+  } else if (kDQ && warp >= 13) {
+    // ============================================================ fused-dQ reducers (warps 13-16)
+    // thread = dim (TMEM lane); per batch the dQ^T partial's 128 columns are
+    // the batch's 8 queries x 16 heads; each warp adds 32 dims of one
+    // (query, head) row per instruction: coalesced 128-byte fp32 reductions.
+    const int wq = warp & 3;
+    const int dim = wq * 32 + lane;
+    const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
+    int job = 0, gb = 0;
+    bool ok = true;
+    while (ok) {
+      const int js = job % kJD;
+      if (!(ok = wtw(&sm.jd_full[js], (job / kJD) & 1, st, 26))) break;
+      const JobDesc& d = sm.jd[js];
+      if (d.flags & kSentinel) break;
+      const int hk = d.hk, nb = (d.n + kQB - 1) / kQB;
+      warp_arrive(&sm.jd_empty[js]);
+      for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
+        const int slot = gb % kMeta;
+        if (!(ok = wtw(&sm.meta_full[slot], (gb / kMeta) & 1, st, 27))) break;
+        const BatchMeta& mt = sm.meta[slot];
+        const int m = mt.m;
+        int rid[kQB];
+#pragma unroll
+        for (int j = 0; j < kQB; ++j) rid[j] = j < m ? mt.rowid[j] : -1;
+        warp_arrive(&sm.meta_empty[slot]);
+        if (!(ok = wtw(&sm.dq_full, gb & 1, st, 25))) break;
+        tc_fence_after();
+        // two queries (32 columns) per round keeps the live registers low
+#pragma unroll
+        for (int j0 = 0; j0 < kQB; j0 += 2) {
+          float part[2][16];
+          tmem_ld16(tl + kColDQ + j0 * 16, part[0]);
+          tmem_ld16(tl + kColDQ + (j0 + 1) * 16, part[1]);
+          tmem_ld_wait();
+          if (dim < D) {
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+              if (rid[j0 + jj] >= 0) {
+                float* dst = args.dq_acc + ((int64_t)rid[j0 + jj] * p.h_q + hk * G) * D + dim;
+#pragma unroll
+                for (int hh = 0; hh < 16; ++hh)
+                  if (hh < G) atomicAdd(dst + hh * D, part[jj][hh]);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        warp_arrive(&sm.dq_empty);
+      }
+      ++job;
+    }
   } else {
     // ============================================================ P/dS and epilogue (warps 2-9)
     // thread = TMEM lane (row = (query j, head h)); warpgroup wg takes keys
@@ -898,35 +954,6 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
     constexpr int kNAcc = kDQ ? 1 : 2;
     int job = 0, gb = 0;
     bool ok = true;
-    // fused dQ: the partial of batch `pend_gb` waits in TMEM until the next
-    // batch's P/dS are handed over; thread = dim, warpgroup wg takes rows
-    // 64*wg .. 64*wg+63 = queries 4*wg .. 4*wg+3 (16 heads each)
-    bool pend = false;
-    int pend_gb = 0, pend_hk = 0, pend_rid[4] = {-1, -1, -1, -1};
-    auto drain_dq = [&]() -> bool {
-      if (!kDQ || !pend) return true;
-      pend = false;
-      if (!wtw(&sm.dq_full, pend_gb & 1, st, 25)) return false;
-      tc_fence_after();
-      float part[4][16];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) tmem_ld16(tl + kColDQ + wg * 64 + i * 16, part[i]);
-      tmem_ld_wait();
-      tc_fence_before();
-      warp_arrive(&sm.dq_empty);
-      if (lrow < D) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          if (pend_rid[i] >= 0) {
-            float* dst = args.dq_acc + ((int64_t)pend_rid[i] * p.h_q + pend_hk * G) * D + lrow;
-#pragma unroll
-            for (int hh = 0; hh < 16; ++hh)
-              if (hh < G) atomicAdd(dst + hh * D, part[i][hh]);   // one 128-byte row per warp
-          }
-        }
-      }
-      return true;
-    };
     while (ok) {
       const int js = job % kJD;
       if (!(ok = wtw(&sm.jd_full[js], (job / kJD) & 1, st, 20))) break;
@@ -950,12 +977,6 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
           dl = __ldg(args.delta + (int64_t)mt.rowid[jq] * p.h_q + hh);
         }
         const bool rvalid = lse2 != -INFINITY;
-        int rid[4] = {-1, -1, -1, -1};
-        if (kDQ) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            if (wg * 4 + i < mt.m) rid[i] = mt.rowid[wg * 4 + i];
-        }
         warp_arrive(&sm.meta_empty[slot]);
         // keys of this warpgroup valid for this row: key_base + i < lim
         int lim = rvalid ? min(kv_len, p.causal ? pos + 1 : kv_len) - key_base : 0;
@@ -991,14 +1012,6 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         }
         fence_proxy_async_smem();
         warp_arrive(&sm.pds_full);
-        if (kDQ) {
-          if (!(ok = drain_dq())) break;   // the previous batch's partial
-          pend = true;
-          pend_gb = gb;
-          pend_hk = d.hk;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) pend_rid[i] = rid[i];
-        }
       }
       if (!ok) break;
       // epilogue: thread = dim; this warpgroup's 32 keys of dV^T and dK^T
@@ -1039,7 +1052,6 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       warp_arrive(&sm.jd_empty[js]);
       ++job;
     }
-    if (ok) drain_dq();   // the last batch's partial
   }
 
   tc_fence_before();
@@ -1087,7 +1099,7 @@ cudaError_t launch(const SfaParams& p, const BwdLayout& L, char* ws, const float
   e = cudaFuncSetAttribute(sfa_bwd_dkdv_tc_kernel<D, kDQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int grid = a.nitems < device_sm_count() ? a.nitems : device_sm_count();
-  sfa_bwd_dkdv_tc_kernel<D, kDQ><<<grid, kThreads, smem, stream>>>(a, tq, tdo, tk, tv);
+  sfa_bwd_dkdv_tc_kernel<D, kDQ><<<grid, kDQ ? kThreadsDQ : kThreads, smem, stream>>>(a, tq, tdo, tk, tv);
   note_launch();
   return cudaGetLastError();
 }

@@ -84,3 +84,22 @@ def test_oversized_head_dims_are_unsupported_by_general_family():
     lib = _lib.load()
     P = _params(d_qk=8192, d_v=8192, kernel=_lib.SFA_KERNEL_GENERAL)
     assert lib.sfa_select_kernel(ctypes.byref(P), 0) == _lib.SFA_ERR_UNSUPPORTED
+
+
+def test_backward_plan_is_consistent_with_the_launch_table():
+    # without a GPU the tensor-core family is unavailable: the general family
+    # always takes the atomic dK/dV pass with dQ in the same (separate) pass
+    lib = _lib.load()
+    fake = 0x20000
+    P = _params(dout=fake, dq=fake, dk=fake, dv=fake + 0x1000)
+    dkv, dq = ctypes.c_int32(-9), ctypes.c_int32(-9)
+    fam = lib.sfa_bwd_plan(ctypes.byref(P), ctypes.byref(dkv), ctypes.byref(dq))
+    assert fam == lib.sfa_select_kernel(ctypes.byref(P), 1)
+    if fam == _lib.SFA_KERNEL_GENERAL:
+        assert (dkv.value, dq.value) == (_lib.SFA_DKV_ATOMIC, _lib.SFA_DQ_SEPARATE)
+    else:
+        assert dkv.value in (_lib.SFA_DKV_INVERTED, _lib.SFA_DKV_ATOMIC)
+        assert dq.value in (_lib.SFA_DQ_SEPARATE, _lib.SFA_DQ_FUSED)
+    P.dq_mode = 5
+    assert lib.sfa_bwd_plan(ctypes.byref(P), ctypes.byref(dkv), ctypes.byref(dq)) == _lib.SFA_ERR_INVALID_ARGUMENT
+    assert "dq_mode" in lib.sfa_last_error_string().decode()
