@@ -8,6 +8,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 #include <string>
@@ -178,6 +179,7 @@ BwdLayout bwd_layout(const SfaParams& p, int family, int dkv_mode, int dq_mode) 
     const int rows_per_warp = 128, warps = 8;
     int64_t nsub = (p.q_len + rows_per_warp - 1) / rows_per_warp;
     int64_t nsub_pad = ((nsub + warps - 1) / warps) * warps;
+    L.inv_nsub = (int)nsub_pad;
     int64_t ncount = nlists * nsub_pad;
     int64_t ntiles = (ncount + 2047) / 2048;
     L.inv_cursor = off;
@@ -186,9 +188,25 @@ BwdLayout bwd_layout(const SfaParams& p, int family, int dkv_mode, int dq_mode) 
     off = align256(off + sizeof(int32_t));
   }
   L.fused_dq = (family == SFA_KERNEL_TCGEN05 && L.inverted_dkv && dq_mode == SFA_DQ_FUSED);
+  L.nranges = 1;
+  L.sub_per_range = L.inv_nsub;
   if (L.fused_dq) {
     L.dq_acc = off;
     off = align256(off + sizeof(float) * (size_t)rows * p.h_q * p.d_qk);
+    // Row ranges of kRangeRows queries: the CTAs working at one time then touch
+    // one range's q/dO rows and dQ accumulator rows, which stay in L2; each
+    // range leaves an fp32 dK/dV partial per block, summed in range order.
+    // (at most 64 ranges: longer sequences get longer ranges)
+    constexpr int kRangeRows = 2048, kMaxRanges = 64;
+    const int64_t nsub = (p.q_len + 127) / 128;
+    L.sub_per_range = (int)std::max<int64_t>(kRangeRows / 128, (nsub + kMaxRanges - 1) / kMaxRanges);
+    L.nranges = (int)((nsub + L.sub_per_range - 1) / L.sub_per_range);
+    if (L.nranges > 1) {
+      L.dkv_part = off;
+      off = align256(off + sizeof(float) * (size_t)L.units * L.nblk * L.nranges * 2 * 64 * p.d_qk);
+    } else {
+      L.nranges = 1;
+    }
   }
   L.total = off;
   return L;
@@ -329,6 +347,7 @@ int sfa_bwd_dkdv(const SfaParams* p, void* workspace, size_t workspace_bytes, vo
     float* dq_acc = L.fused_dq ? reinterpret_cast<float*>(ws + L.dq_acc) : nullptr;
     e = launch_inverted_index(*p, L, ws, st);
     if (e == cudaSuccess) e = launch_bwd_dkdv_tc(*p, L, ws, delta, dq_acc, st);
+    if (e == cudaSuccess && L.nranges > 1) e = launch_reduce_dkdv_ranges(*p, L, ws, st);
     if (e == cudaSuccess && dq_acc) e = launch_convert_dq(*p, dq_acc, st);
   } else {
     float* dk_acc = reinterpret_cast<float*>(ws + L.dk_acc);

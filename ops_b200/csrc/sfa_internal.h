@@ -29,7 +29,11 @@ struct BwdLayout {
   size_t inv_cursor;   // int32 [units * nblk]            (inverted path scratch)
   size_t sched;        // int32 work counter               (inverted path)
   size_t dq_acc;       // float [rows * h_q * d_qk]       (fused dQ)
+  size_t dkv_part;     // float [units*nblk*nranges][2][64][d_qk] (row-range split)
   size_t total;
+  int inv_nsub;        // 128-row sub-chunks per unit in the index counts (padded)
+  int sub_per_range;   // sub-chunks per row range of the key-centric pass
+  int nranges;         // row ranges (1: no split)
   int pre_ctas;
   int nblk;
   int units;
@@ -54,6 +58,8 @@ int general_head_group(const SfaParams& p);
 // backward preprocessing / epilogues
 cudaError_t launch_preprocess(const SfaParams& p, float* delta, float* dsink_part, int pre_ctas, cudaStream_t st);
 cudaError_t launch_convert_dkdv(const SfaParams& p, const float* dk_acc, const float* dv_acc, cudaStream_t st);
+// dk/dv from the row-range partials of the key-centric pass, summed in range order
+cudaError_t launch_reduce_dkdv_ranges(const SfaParams& p, const BwdLayout& L, const char* ws, cudaStream_t st);
 // dq = bf16(scale * dq_acc), dq_acc fp32 [rows][h_q][d_qk]
 cudaError_t launch_convert_dq(const SfaParams& p, const float* dq_acc, cudaStream_t st);
 

@@ -137,6 +137,64 @@ cudaError_t launch_convert_dkdv(const SfaParams& p, const float* dk_acc, const f
   return cudaGetLastError();
 }
 
+// dk/dv of one (unit, block) from the key-centric pass's row-range partials
+// (fp32 [range][dK|dV][key][dim]); only ranges whose list part is non-empty
+// wrote a partial, and they are added in range order — deterministic.
+__global__ void reduce_dkdv_ranges_kernel(SfaParams p, const float* __restrict__ part,
+                                          const int32_t* __restrict__ starts, const int32_t* __restrict__ offsets,
+                                          int nblk, int nsub, int sub_per_range, int nranges) {
+  __shared__ int have[64];
+  const int ue = blockIdx.x;
+  const int u = ue / nblk, e = ue - u * nblk;
+  const int seq = u / p.h_kv, hk = u - seq * p.h_kv;
+  int kv0 = 0, kv_len = p.kv_len, b = seq;
+  if (p.cu_seqlens_q != nullptr) {
+    kv0 = __ldg(p.cu_seqlens_k + seq);
+    kv_len = __ldg(p.cu_seqlens_k + seq + 1) - kv0;
+    b = 0;
+  }
+  if (e * 64 >= kv_len) return;
+  for (int r = threadIdx.x; r < nranges; r += blockDim.x) {
+    const int64_t sb = (int64_t)ue * nsub;
+    const int s0 = r * sub_per_range, s1 = s0 + sub_per_range;
+    const int end = s1 < nsub ? starts[sb + s1] : offsets[ue + 1];
+    have[r] = end > starts[sb + s0];
+  }
+  __syncthreads();
+  const int D = p.d_qk;
+  const bool shared_kv = p.dk == p.dv;
+  for (int i = threadIdx.x; i < 64 * D; i += blockDim.x) {
+    const int key = i / D, dim = i - key * D;
+    if (e * 64 + key >= kv_len) continue;
+    float sk = 0.f, sv = 0.f;
+    for (int r = 0; r < nranges; ++r) {
+      if (!have[r]) continue;
+      const float* pr = part + ((int64_t)ue * nranges + r) * (2 * 64 * D);
+      sk += pr[i];
+      sv += pr[64 * D + i];
+    }
+    const int64_t t = (int64_t)kv0 + e * 64 + key;
+    __nv_bfloat16* dk = reinterpret_cast<__nv_bfloat16*>(p.dk) + b * p.dk_sb + t * p.dk_st + hk * p.dk_sh + dim;
+    if (shared_kv) {
+      *dk = f2bf(sk * p.scale + sv);
+    } else {
+      *dk = f2bf(sk * p.scale);
+      reinterpret_cast<__nv_bfloat16*>(p.dv)[b * p.dv_sb + t * p.dv_st + hk * p.dv_sh + dim] = f2bf(sv);
+    }
+  }
+}
+
+cudaError_t launch_reduce_dkdv_ranges(const SfaParams& p, const BwdLayout& L, const char* ws, cudaStream_t st) {
+  if (L.nranges > 64) return cudaErrorInvalidValue;
+  const int nlists = L.units * L.nblk;
+  if (nlists == 0) return cudaSuccess;
+  reduce_dkdv_ranges_kernel<<<nlists, 256, 0, st>>>(
+      p, reinterpret_cast<const float*>(ws + L.dkv_part), reinterpret_cast<const int32_t*>(ws + L.inv_cursor),
+      reinterpret_cast<const int32_t*>(ws + L.inv_offsets), L.nblk, L.inv_nsub, L.sub_per_range, L.nranges);
+  note_launch();
+  return cudaGetLastError();
+}
+
 // dq = bf16(scale * acc) for the fused dQ: acc is fp32 [rows][h_q][d_qk]; four
 // consecutive dims per thread (d_qk % 4 == 0), written as one 8-byte store when
 // the dq rows allow it (kVec), else element by element.

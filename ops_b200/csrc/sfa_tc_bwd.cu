@@ -526,6 +526,7 @@ constexpr uint32_t kColDQ = 384;    // fused dQ: dQ^T partial of one batch (128 
 
 struct JobDesc {
   int e, b, hk, kv0, kv_len, n, list0, flags;
+  int64_t part;   // row-range split: this job's fp32 dK/dV partial slot, else -1
 };
 
 // Per-batch metadata of the queries of one batch, written by the metadata warp
@@ -563,6 +564,14 @@ struct Args {
   float* dq_acc;            // fused dQ: fp32 [rows][h_q][d_qk] accumulator (zeroed by the host), else null
   const int32_t* offsets;   // [units * nblk + 1]
   const int32_t* entries;   // query rows
+  // Row ranges: with nranges > 1 a job is (range, unit, block) and covers the
+  // block's queries in rows [r*range_rows, (r+1)*range_rows) of its sequence;
+  // starts[] (the index builder's scanned sub-chunk counts) gives where each
+  // range starts in the list; the job writes an fp32 dK/dV partial to
+  // part[(unit*nblk + block)*nranges + r] and a reduction sums the ranges.
+  const int32_t* starts;    // [units * nblk * nsub] list position of each 128-row sub-chunk
+  float* part;              // [units * nblk * nranges][2][64][D] (dK then dV), or null
+  int nsub, sub_per_range, nranges;
   int* sched;               // work counter (zeroed by the host)
   int units, nblk, nitems;
   int32_t* status;
@@ -654,7 +663,9 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       if (lane == 0) item = atomicAdd(args.sched, 1);
       item = __shfl_sync(0xffffffffu, item, 0);
       if (item >= args.nitems) break;
-      const int u = item / args.nblk, e = item - u * args.nblk;
+      const int per_range = args.units * args.nblk;
+      const int r = item / per_range, ue = item - r * per_range;
+      const int u = ue / args.nblk, e = ue - u * args.nblk;
       const int seq = u / p.h_kv, hk = u - seq * p.h_kv;
       int kv0 = 0, kv_len = p.kv_len, b = seq;
       if (p.cu_seqlens_q != nullptr) {
@@ -663,8 +674,20 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         b = 0;
       }
       if (e * 64 >= kv_len) continue;   // past this sequence's last block
-      const int list0 = __ldg(args.offsets + (int64_t)u * args.nblk + e);
-      const int n = __ldg(args.offsets + (int64_t)u * args.nblk + e + 1) - list0;
+      int list0, n;
+      if (args.nranges > 1) {
+        // [start of range r, start of range r+1) inside the block's list
+        const int64_t sb = ((int64_t)u * args.nblk + e) * args.nsub;
+        const int s0 = r * args.sub_per_range, s1 = s0 + args.sub_per_range;
+        list0 = __ldg(args.starts + sb + s0);
+        const int end = s1 < args.nsub ? __ldg(args.starts + sb + s1)
+                                        : __ldg(args.offsets + (int64_t)u * args.nblk + e + 1);
+        n = end - list0;
+        if (n == 0) continue;   // no query of this range: no partial (the reduction skips it)
+      } else {
+        list0 = __ldg(args.offsets + (int64_t)u * args.nblk + e);
+        n = __ldg(args.offsets + (int64_t)u * args.nblk + e + 1) - list0;
+      }
       const int js = job % kJD;
       if (lane == 0) {
         ok = wt(&sm.jd_empty[js], ((job / kJD) & 1) ^ 1, st, 1);
@@ -678,6 +701,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
           d.n = n;
           d.list0 = list0;
           d.flags = 0;
+          d.part = args.nranges > 1 ? ((int64_t)u * args.nblk + e) * args.nranges + r : -1;
           mbar_arrive(&sm.jd_full[js]);
         }
       }
@@ -1031,7 +1055,17 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
 #pragma unroll
           for (int i = 0; i < 16; ++i) { vv[i] = 0.f; kv[i] = 0.f; }
         }
-        if (lrow < D) {
+        if (lrow < D && d.part >= 0) {
+          // one row range's partial, fp32 [dK|dV][key][dim]: a warp writes 32
+          // consecutive dims of one key per store
+          float* pk = args.part + d.part * (2 * 64 * D) + lrow;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int key = wg * 32 + q2 * 16 + i;
+            pk[key * D] = kv[i];
+            pk[(64 + key) * D] = vv[i];
+          }
+        } else if (lrow < D) {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int key = key_base + q2 * 16 + i;
@@ -1089,7 +1123,12 @@ cudaError_t launch(const SfaParams& p, const BwdLayout& L, char* ws, const float
   a.sched = reinterpret_cast<int*>(ws + L.sched);
   a.units = L.units;
   a.nblk = L.nblk;
-  a.nitems = L.units * L.nblk;
+  a.starts = reinterpret_cast<const int32_t*>(ws + L.inv_cursor);
+  a.nsub = L.inv_nsub;
+  a.nranges = L.nranges;
+  a.sub_per_range = L.sub_per_range;
+  a.part = L.nranges > 1 ? reinterpret_cast<float*>(ws + L.dkv_part) : nullptr;
+  a.nitems = L.nranges * L.units * L.nblk;
   a.status = device_status_ptr();
   if (a.nitems == 0) return cudaSuccess;
   e = cudaMemsetAsync(a.sched, 0, sizeof(int), stream);

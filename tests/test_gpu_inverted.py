@@ -75,12 +75,13 @@ def test_inverted_index_lists_match_cpu():
     assert torch.equal(ws[ent_o.value: ent_o.value + 4 * total], ws2[ent_o.value: ent_o.value + 4 * total])
 
 
-@pytest.mark.parametrize("dq_mode", ["separate", "fused"])
-def test_key_centric_dkdv_is_deterministic(dq_mode):
-    # dk/dv are written once per block in a fixed order in both dQ modes; dq is
+@pytest.mark.parametrize("dq_mode,T", [("separate", 2048), ("fused", 2048), ("fused", 5000)])
+def test_key_centric_dkdv_is_deterministic(dq_mode, T):
+    # dk/dv are written once per block in a fixed order in both dQ modes (with
+    # T > 2048 the fused pass sums per-row-range partials in range order); dq is
     # bitwise reproducible only from its own pass (the fused dQ adds fp32
     # partials in arrival order)
-    cfg = W.scaled(W.CONFIGS["c2"], B=1, T=2048, Hq=32, Hk=2, S=16)
+    cfg = W.scaled(W.CONFIGS["c2"], B=1, T=T, Hq=32, Hk=2, S=16)
     d = W.make_inputs(cfg, "cpu", 8)
     a = run_op(d["q"], d["k"], d["v"], d["idx"], 64, None, None, True, d["do"], kernel="tcgen05",
                dkv_mode="inverted", dq_mode=dq_mode)

@@ -97,3 +97,31 @@ def test_tc_reference_sbhd_strides():
     got = run_op(qb, kvb, kvb, idx, 64, None, None, True, None, kernel="tcgen05")
     ref = run_oracle(qb.contiguous(), kvb.contiguous(), kvb.contiguous(), idx, 64, None, None, True)
     check_all(got, ref, grads=False)
+
+
+@pytest.mark.parametrize("dq_mode", ["separate", "fused"])
+def test_tc_long_rows_and_varlen_row_ranges(dq_mode):
+    # q_len > 2048 splits the fused key-centric pass into row ranges whose
+    # dK/dV partials are summed afterwards: dense and varlen (sequences of
+    # different lengths, bottom-right causal alignment, blocks of 64)
+    cfg = W.scaled(W.CONFIGS["c2"], B=1, T=5000, Hq=16, Hk=1, S=16)
+    d, s = _case(cfg, 17)
+    got = run_op(d["q"], d["k"], d["v"], d["idx"], cfg.bs, cfg.scale, s, True, d["do"], kernel="tcgen05",
+                 dkv_mode="inverted", dq_mode=dq_mode)
+    ref = run_oracle(d["q"], d["k"], d["v"], d["idx"], cfg.bs, cfg.scale, s, True, d["do"], o_for_bwd=got["o"])
+    check_all(got, ref)
+
+    g = torch.Generator().manual_seed(23)
+    q_lens, k_lens = [3000, 700, 2500], [3000, 900, 2600]
+    cu_q = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0)), dtype=torch.int32)
+    cu_k = torch.tensor([0] + list(torch.tensor(k_lens).cumsum(0)), dtype=torch.int32)
+    Hq, Hk, D, bs, S = 16, 2, 128, 64, 12
+    q = torch.randn(int(cu_q[-1]), Hq, D, generator=g).bfloat16()
+    k = torch.randn(int(cu_k[-1]), Hk, D, generator=g).bfloat16()
+    v = torch.randn(int(cu_k[-1]), Hk, D, generator=g).bfloat16()
+    do = torch.randn(int(cu_q[-1]), Hq, D, generator=g).bfloat16()
+    idx = torch.randint(-1, 47, (int(cu_q[-1]), Hk, S), generator=g, dtype=torch.int32)
+    got = run_op(q, k, v, idx, bs, None, None, True, do, cu_q, cu_k, max(q_lens), max(k_lens), kernel="tcgen05",
+                 dkv_mode="inverted", dq_mode=dq_mode)
+    ref = run_oracle(q, k, v, idx, bs, None, None, True, do, cu_q, cu_k, o_for_bwd=got["o"])
+    check_all(got, ref)
