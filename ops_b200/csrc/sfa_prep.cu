@@ -68,6 +68,63 @@ preprocess_kernel(SfaParams p, float* __restrict__ delta, float* __restrict__ ds
   }
 }
 
+// The same delta with 16-byte loads: 16 lanes per (row, head), each lane 8
+// consecutive elements per step (d_v % 8 == 0, 16-byte aligned rows and
+// strides), two (row, head) pairs per warp.  The dsink partials follow as above.
+__global__ void __launch_bounds__(kPreThreads)
+preprocess_vec_kernel(SfaParams p, float* __restrict__ delta, float* __restrict__ dsink_part) {
+  extern __shared__ float sdelta[];  // [kPreRows][h_q]
+  const int rows = num_rows(p);
+  const int row0 = blockIdx.x * kPreRows;
+  const int hw = threadIdx.x >> 4, l16 = threadIdx.x & 15;   // half-warp = one (row, head)
+  const int nhw = kPreThreads / 16;
+  const int Dv = p.d_v;
+  for (int pr = hw; pr < kPreRows * p.h_q; pr += nhw) {
+    const int rl = pr / p.h_q, h = pr - rl * p.h_q;
+    const int row = row0 + rl;
+    float acc = 0.f;
+    if (row < rows) {
+      const Row r = row_info(p, row);
+      const uint4* o = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.o) + r.b * p.o_sb +
+                                                      r.tq * p.o_st + (int64_t)h * p.o_sh);
+      const uint4* dO = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.dout) +
+                                                       r.b * p.do_sb + r.tq * p.do_st + (int64_t)h * p.do_sh);
+      for (int c = l16; c < Dv / 8; c += 16) {
+        const uint4 a = __ldg(o + c), b = __ldg(dO + c);
+        const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&av[k]));
+          const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bv[k]));
+          acc = fmaf(x.x, y.x, acc);
+          acc = fmaf(x.y, y.y, acc);
+        }
+      }
+    }
+#pragma unroll
+    for (int off = 8; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (l16 == 0) {
+      if (row < rows) delta[(int64_t)row * p.h_q + h] = acc;
+      sdelta[pr] = acc;
+    }
+  }
+  __syncthreads();
+  if (dsink_part == nullptr) return;
+  for (int h = threadIdx.x; h < p.h_q; h += kPreThreads) {
+    float sink2 = __ldg(p.attn_sink + h) * kLog2e;
+    float acc = 0.f;
+    for (int rl = 0; rl < kPreRows; ++rl) {
+      int row = row0 + rl;
+      if (row >= rows) break;
+      Row r = row_info(p, row);
+      float lse = p.lse[r.b * p.l_sb + r.tq * p.l_st + (int64_t)h * p.l_sh];
+      if (lse == -INFINITY) continue;
+      acc -= exp2f(sink2 - lse * kLog2e) * sdelta[rl * p.h_q + h];
+    }
+    dsink_part[(int64_t)blockIdx.x * p.h_q + h] = acc;
+  }
+}
+
 __global__ void dsink_reduce_kernel(const float* __restrict__ part, int nparts, int hq, float* __restrict__ dsink) {
   // one warp per head, fixed-order pairwise tree over lanes: deterministic
   int h = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
@@ -89,7 +146,16 @@ cudaError_t launch_preprocess(const SfaParams& p, float* delta, float* dsink_par
   cudaError_t e = cudaFuncSetAttribute(preprocess_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   float* part = (p.dsink && p.attn_sink) ? dsink_part : nullptr;
-  preprocess_kernel<<<pre_ctas, kPreThreads, smem, st>>>(p, delta, part);
+  const bool vec = p.d_v % 8 == 0 && reinterpret_cast<uintptr_t>(p.o) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(p.dout) % 16 == 0 && p.o_sb % 8 == 0 && p.o_st % 8 == 0 &&
+                   p.o_sh % 8 == 0 && p.do_sb % 8 == 0 && p.do_st % 8 == 0 && p.do_sh % 8 == 0;
+  if (vec) {
+    e = cudaFuncSetAttribute(preprocess_vec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    preprocess_vec_kernel<<<pre_ctas, kPreThreads, smem, st>>>(p, delta, part);
+  } else {
+    preprocess_kernel<<<pre_ctas, kPreThreads, smem, st>>>(p, delta, part);
+  }
   note_launch();
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -167,11 +233,19 @@ __global__ void reduce_dkdv_ranges_kernel(SfaParams p, const float* __restrict__
     const int key = i / D, dim = i - key * D;
     if (e * 64 + key >= kv_len) continue;
     float sk = 0.f, sv = 0.f;
-    for (int r = 0; r < nranges; ++r) {
-      if (!have[r]) continue;
-      const float* pr = part + ((int64_t)ue * nranges + r) * (2 * 64 * D);
-      sk += pr[i];
-      sv += pr[64 * D + i];
+    // ranges in order, four loads in flight at a time
+    for (int r0 = 0; r0 < nranges; r0 += 4) {
+      float a[4], c[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int r = r0 + k;
+        const bool use = r < nranges && have[r];
+        const float* pr = part + ((int64_t)ue * nranges + (use ? r : 0)) * (2 * 64 * D);
+        a[k] = use ? pr[i] : 0.f;
+        c[k] = use ? pr[64 * D + i] : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) { sk += a[k]; sv += c[k]; }
     }
     const int64_t t = (int64_t)kv0 + e * 64 + key;
     __nv_bfloat16* dk = reinterpret_cast<__nv_bfloat16*>(p.dk) + b * p.dk_sb + t * p.dk_st + hk * p.dk_sh + dim;
