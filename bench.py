@@ -396,6 +396,121 @@ def run_ours(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+def run_decode(args, cfg):
+    """Forward-only configurations (c5: varlen decode, one query per sequence):
+    a step is one sfa_fwd over the batch; HBM-bound, so the line reports the
+    gathered K/V bytes per second against the measured copy bandwidth."""
+    import torch
+    import torch.distributed as dist
+
+    import ops_b200
+    from ops_b200 import _lib
+    from ops_b200 import sfa as S
+    from ops_b200 import workloads as W
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    lib = _lib.load()
+    d = W.make_decode(cfg, dev, seed=rank_seed(rank))
+    q, k, v, idx, cu_q, cu_k = d["q"], d["k"], d["v"], d["idx"], d["cu_q"], d["cu_k"]
+    keys = W.count_pairs(idx, cfg.bs, 1, 0, kv_lens=d["kv_lens"])        # valid (query, kv head, key)
+    G = cfg.Hq // cfg.Hk
+    gathered = keys * (cfg.Dqk + cfg.Dv) * 2.0                             # K and V rows read
+    flops = 2.0 * keys * G * (cfg.Dqk + cfg.Dv)
+    o = torch.empty(q.shape[0], cfg.Hq, cfg.Dv, dtype=q.dtype, device=dev)
+    lse = torch.empty(q.shape[0], cfg.Hq, dtype=torch.float32, device=dev)
+    scfg = S._Cfg(cfg.bs, cfg.scale, True, True, 1, d["max_k"], _lib.SFA_DKV_AUTO, _lib.SFA_KERNEL_AUTO, False)
+    P = S.build_params(q, k, v, idx, o, lse, scfg, None, cu_q, cu_k)
+    fam = lib.sfa_select_kernel(ctypes.byref(P), 0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+    for _ in range(args.warmup):
+        _lib.check(lib.sfa_fwd(ctypes.byref(P), None, 0, sptr), "sfa_fwd")
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    n0 = lib.sfa_kernel_launches()
+    t_wall0 = time.time()
+    for a, b in evs:
+        flush.zero_()
+        a.record(stream)
+        _lib.check(lib.sfa_fwd(ctypes.byref(P), None, 0, sptr), "sfa_fwd")
+        b.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    n1 = lib.sfa_kernel_launches()
+    step_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    # e2e through the public API with host buffers
+    host = {n: t.cpu().pin_memory() for n, t in (("q", q), ("k", k), ("v", v), ("idx", idx))}
+    o_h = torch.empty(tuple(o.shape), dtype=o.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = o_h.numel() * o_h.element_size()
+    cu_qd, cu_kd = cu_q.to(dev), cu_k.to(dev)
+
+    def e2e_step():
+        qd, kd, vd, ixd = (host[n].to(dev, non_blocking=True) for n in ("q", "k", "v", "idx"))
+        oo, _ = ops_b200.sparse_flash_attention(qd, kd, vd, ixd, cfg.bs, cu_seqlens=cu_qd, cu_seqlens_k=cu_kd,
+                                                max_seqlen_q=1, max_seqlen_k=d["max_k"])
+        o_h.copy_(oo, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    e_ms = 0.0
+    for _ in range(max(1, min(args.steps, 3))):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize()
+        e_ms += a.elapsed_time(b)
+    e_ms /= max(1, min(args.steps, 3))
+    sampler.stop()
+    clocks = sampler.summary(t_wall0, t_wall1)
+    step_ms_max, e_ms_max, bytes_all = reduce_over_ranks(step_ms, e_ms, gathered, dev)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    hbm = None
+    try:
+        hbm = float(json.load(open(os.path.join(os.path.dirname(os.path.abspath(__file__)),
+                                                "MEASURED_PEAKS.json")))["hbm_gbs"])
+        hbm_kind = "measured copy"
+    except Exception:
+        hbm, hbm_kind = 6650.0, "fallback"
+    gbs = gathered / (step_ms * 1e-3) / 1e9
+    line = {
+        "metric": "SFA decode forward GB/s (gathered K/V rows), B200", "value": bytes_all / (step_ms_max * 1e-3) / 1e9,
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms_max,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{cfg.name}: varlen decode forward, {cfg.n_seqs} sequences/rank x 1 query, kv "
+                               f"lengths U[{cfg.kv_min}, {cfg.kv_max}], Hq={cfg.Hq}, Hk={cfg.Hk}, Dqk={cfg.Dqk}, "
+                               f"Dv={cfg.Dv}, block_size={cfg.bs}, S={cfg.S} uniform blocks, q/k/v ~ N(0,1)",
+                   "global_batch": cfg.n_seqs * world, "parallelism": f"dp{world} (independent sequence shards)",
+                   "l2": "flushed between timed steps (256 MiB memset)"},
+        "tflops": flops / (step_ms * 1e-3) / 1e12,
+        "kernel_family": {1: "tcgen05", 2: "general"}.get(fam, str(fam)),
+        "roofline": {"bound": "hbm", "kernel": "fwd", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": gbs / hbm, "peak_kind": hbm_kind, "traffic": None},
+        "e2e": {"value": bytes_all / (e_ms_max * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e_ms_max},
+        "clocks": clocks,
+        "gpu_launches": int(n1 - n0),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -412,7 +527,12 @@ def main():
     if args.batch:
         cfg = W.scaled(cfg, B=args.batch)
     if cfg.fwd_only:
-        raise SystemExit("bench.py times fwd+bwd; config %s is forward-only" % args.config)
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "forward-only decode config; the reference arm "
+                              "times the fwd+bwd configurations"}))
+            return
+        run_decode(args, cfg)
+        return
     if args.impl == "reference":
         run_reference(args, cfg)
     else:
