@@ -229,31 +229,42 @@ __global__ void reduce_dkdv_ranges_kernel(SfaParams p, const float* __restrict__
   __syncthreads();
   const int D = p.d_qk;
   const bool shared_kv = p.dk == p.dv;
-  for (int i = threadIdx.x; i < 64 * D; i += blockDim.x) {
+  // four consecutive dims per thread (d_qk % 4 == 0): 16-byte loads of the partials
+  for (int i4 = threadIdx.x; i4 < 16 * D; i4 += blockDim.x) {
+    const int i = i4 * 4;
     const int key = i / D, dim = i - key * D;
     if (e * 64 + key >= kv_len) continue;
-    float sk = 0.f, sv = 0.f;
+    float4 sk = make_float4(0.f, 0.f, 0.f, 0.f), sv = sk;
     // ranges in order, four loads in flight at a time
     for (int r0 = 0; r0 < nranges; r0 += 4) {
-      float a[4], c[4];
+      float4 a[4], c[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const int r = r0 + k;
         const bool use = r < nranges && have[r];
         const float* pr = part + ((int64_t)ue * nranges + (use ? r : 0)) * (2 * 64 * D);
-        a[k] = use ? pr[i] : 0.f;
-        c[k] = use ? pr[64 * D + i] : 0.f;
+        a[k] = use ? *reinterpret_cast<const float4*>(pr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        c[k] = use ? *reinterpret_cast<const float4*>(pr + 64 * D + i) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
-      for (int k = 0; k < 4; ++k) { sk += a[k]; sv += c[k]; }
+      for (int k = 0; k < 4; ++k) {
+        sk.x += a[k].x; sk.y += a[k].y; sk.z += a[k].z; sk.w += a[k].w;
+        sv.x += c[k].x; sv.y += c[k].y; sv.z += c[k].z; sv.w += c[k].w;
+      }
     }
     const int64_t t = (int64_t)kv0 + e * 64 + key;
     __nv_bfloat16* dk = reinterpret_cast<__nv_bfloat16*>(p.dk) + b * p.dk_sb + t * p.dk_st + hk * p.dk_sh + dim;
+    const float k4[4] = {sk.x, sk.y, sk.z, sk.w}, v4[4] = {sv.x, sv.y, sv.z, sv.w};
     if (shared_kv) {
-      *dk = f2bf(sk * p.scale + sv);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) dk[q] = f2bf(k4[q] * p.scale + v4[q]);
     } else {
-      *dk = f2bf(sk * p.scale);
-      reinterpret_cast<__nv_bfloat16*>(p.dv)[b * p.dv_sb + t * p.dv_st + hk * p.dv_sh + dim] = f2bf(sv);
+      __nv_bfloat16* dv = reinterpret_cast<__nv_bfloat16*>(p.dv) + b * p.dv_sb + t * p.dv_st + hk * p.dv_sh + dim;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        dk[q] = f2bf(k4[q] * p.scale);
+        dv[q] = f2bf(v4[q]);
+      }
     }
   }
 }
@@ -269,29 +280,34 @@ cudaError_t launch_reduce_dkdv_ranges(const SfaParams& p, const BwdLayout& L, co
   return cudaGetLastError();
 }
 
-// dq = bf16(scale * acc) for the fused dQ: acc is fp32 [rows][h_q][d_qk]; four
-// consecutive dims per thread (d_qk % 4 == 0), written as one 8-byte store when
-// the dq rows allow it (kVec), else element by element.
+// dq = bf16(scale * acc) for the fused dQ: acc is fp32 [rows][h_q][d_qk].
+// kVec: eight consecutive dims per thread (d_qk % 8 == 0), one 16-byte store
+// (16-byte aligned dq rows); otherwise four dims and element stores.
 template <bool kVec>
 __global__ void convert_dq_kernel(SfaParams p, const float* __restrict__ acc) {
+  constexpr int kE = kVec ? 8 : 4;
   const int D = p.d_qk;
   const int64_t rows = p.cu_seqlens_q == nullptr ? (int64_t)p.batch * p.q_len : (int64_t)p.total_q;
-  const int64_t n4 = rows * p.h_q * (D / 4);
+  const int64_t n = rows * p.h_q * (D / kE);
   __nv_bfloat16* dq = reinterpret_cast<__nv_bfloat16*>(p.dq);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
-    const int d = (int)(i % (D / 4)) * 4;
-    const int64_t rh = i / (D / 4);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int d = (int)(i % (D / kE)) * kE;
+    const int64_t rh = i / (D / kE);
     const int h = (int)(rh % p.h_q);
     const int row = (int)(rh / p.h_q);
     int64_t b = 0, t = row;
     if (p.cu_seqlens_q == nullptr) { b = row / p.q_len; t = row - b * p.q_len; }
-    const float4 v = reinterpret_cast<const float4*>(acc)[i];
+    const float4* src = reinterpret_cast<const float4*>(acc + rh * D + d);
     __nv_bfloat16* o = dq + b * p.dq_sb + t * p.dq_st + h * p.dq_sh + d;
+    const float4 v = __ldg(src);
     if (kVec) {
-      uint2 w;
-      w.x = pack_bf16x2_rn(v.x * p.scale, v.y * p.scale);
-      w.y = pack_bf16x2_rn(v.z * p.scale, v.w * p.scale);
-      *reinterpret_cast<uint2*>(o) = w;
+      const float4 w = __ldg(src + 1);
+      uint4 u;
+      u.x = pack_bf16x2_rn(v.x * p.scale, v.y * p.scale);
+      u.y = pack_bf16x2_rn(v.z * p.scale, v.w * p.scale);
+      u.z = pack_bf16x2_rn(w.x * p.scale, w.y * p.scale);
+      u.w = pack_bf16x2_rn(w.z * p.scale, w.w * p.scale);
+      *reinterpret_cast<uint4*>(o) = u;
     } else {
       o[0] = f2bf(v.x * p.scale);
       o[1] = f2bf(v.y * p.scale);
@@ -303,8 +319,8 @@ __global__ void convert_dq_kernel(SfaParams p, const float* __restrict__ acc) {
 
 cudaError_t launch_convert_dq(const SfaParams& p, const float* dq_acc, cudaStream_t st) {
   const int grid = device_sm_count() * 8;
-  const bool vec = (reinterpret_cast<uintptr_t>(p.dq) % 8 == 0) && p.dq_sb % 4 == 0 && p.dq_st % 4 == 0 &&
-                   p.dq_sh % 4 == 0;
+  const bool vec = p.d_qk % 8 == 0 && (reinterpret_cast<uintptr_t>(p.dq) % 16 == 0) && p.dq_sb % 8 == 0 &&
+                   p.dq_st % 8 == 0 && p.dq_sh % 8 == 0;
   if (vec)
     convert_dq_kernel<true><<<grid, 256, 0, st>>>(p, dq_acc);
   else
