@@ -522,11 +522,14 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--batch", type=int, default=0, help="override the per-rank batch (profiling runs)")
+    ap.add_argument("--seq", type=int, default=0, help="override the sequence length (scaled secondary configs)")
     args = ap.parse_args()
     from ops_b200 import workloads as W
     cfg = W.CONFIGS[args.config]
     if args.batch:
         cfg = W.scaled(cfg, B=args.batch)
+    if args.seq:
+        cfg = W.scaled(cfg, T=args.seq)
     if cfg.fwd_only:
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "forward-only decode config; the reference arm "
