@@ -515,7 +515,7 @@ namespace dkdv {
 
 constexpr int kThreads = 416;       // warp 0 metadata, 1 S/dP issuer, 2-9 P/dS + epilogue, 10 K/V/Q loads,
                                     // 11 dV/dK issuer, 12 dO loads
-constexpr int kThreadsDQ = 544;     // + warps 13-16: fused-dQ reducers
+constexpr int kThreadsDQ = 672;     // + warps 13-20: fused-dQ reducers (two per TMEM lane quadrant)
 constexpr int kWG = 256;            // P/dS threads: 2 warpgroups, each takes 32 of the 64 keys
 constexpr int kQB = 8;              // queries per batch (x 16 heads = 128 MMA rows)
 constexpr int kMeta = 6;            // batch metadata ring depth
@@ -614,19 +614,19 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
     // counts in warps for the P/dS warps (one arrival per warp)
     for (int i = 0; i < kMeta; ++i) {
       mbar_init(&sm.meta_full[i], 1);
-      mbar_init(&sm.meta_empty[i], 2 + kWG / 32 + (kDQ ? 4 : 0));   // loader threads, P/dS warps, reducers
+      mbar_init(&sm.meta_empty[i], 2 + kWG / 32 + (kDQ ? 8 : 0));   // loader threads, P/dS warps, reducers
     }
     mbar_init(&sm.kv_full, 1);
     mbar_init(&sm.kv_empty, 1);
     mbar_init(&sm.pds_full, kWG / 32);
     mbar_init(&sm.pds_empty, 1);
     mbar_init(&sm.dq_full, 1);
-    mbar_init(&sm.dq_empty, 4);   // the 4 reducer warps
+    mbar_init(&sm.dq_empty, 8);   // the 8 reducer warps
     // consumers of a job descriptor: the two issuers, the two loader threads,
     // P/dS warps and (fused dQ) the reducer warps
     for (int i = 0; i < kJD; ++i) {
       mbar_init(&sm.jd_full[i], 1);
-      mbar_init(&sm.jd_empty[i], 4 + kWG / 32 + (kDQ ? 4 : 0));
+      mbar_init(&sm.jd_empty[i], 4 + kWG / 32 + (kDQ ? 8 : 0));
     }
     fence_barrier_init();
   }
@@ -912,11 +912,15 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       }
     }
   } else if (kDQ && warp >= 13) {
-    // ============================================================ fused-dQ reducers (warps 13-16)
+    // ============================================================ fused-dQ reducers (warps 13-20)
     // thread = dim (TMEM lane); per batch the dQ^T partial's 128 columns are
-    // the batch's 8 queries x 16 heads; each warp adds 32 dims of one
-    // (query, head) row per instruction: coalesced 128-byte fp32 reductions.
+    // the batch's 8 queries x 16 heads, and each quadrant has two reducer
+    // warps: warps 13-16 take queries 0-3, warps 17-20 queries 4-7.  A warp
+    // reads its 64 columns at once and releases the partial before issuing
+    // its reductions, so the next batch's dQ MMAs need not wait for them; each
+    // reduction adds 32 dims of one (query, head) row: coalesced 128 bytes.
     const int wq = warp & 3;
+    const int q0 = ((warp - 13) >> 2) * 4;   // first query of this warp's half
     const int dim = wq * 32 + lane;
     const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
     int job = 0, gb = 0;
@@ -933,33 +937,29 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         if (!(ok = wtw(&sm.meta_full[slot], (gb / kMeta) & 1, st, 27))) break;
         const BatchMeta& mt = sm.meta[slot];
         const int m = mt.m;
-        int rid[kQB];
+        int rid[4];
 #pragma unroll
-        for (int j = 0; j < kQB; ++j) rid[j] = j < m ? mt.rowid[j] : -1;
+        for (int j = 0; j < 4; ++j) rid[j] = q0 + j < m ? mt.rowid[q0 + j] : -1;
         warp_arrive(&sm.meta_empty[slot]);
         if (!(ok = wtw(&sm.dq_full, gb & 1, st, 25))) break;
         tc_fence_after();
-        // two queries (32 columns) per round keeps the live registers low
+        float part[4][16];
 #pragma unroll
-        for (int j0 = 0; j0 < kQB; j0 += 2) {
-          float part[2][16];
-          tmem_ld16(tl + kColDQ + j0 * 16, part[0]);
-          tmem_ld16(tl + kColDQ + (j0 + 1) * 16, part[1]);
-          tmem_ld_wait();
-          if (dim < D) {
+        for (int j = 0; j < 4; ++j) tmem_ld16(tl + kColDQ + (q0 + j) * 16, part[j]);
+        tmem_ld_wait();
+        tc_fence_before();
+        warp_arrive(&sm.dq_empty);
+        if (dim < D) {
 #pragma unroll
-            for (int jj = 0; jj < 2; ++jj) {
-              if (rid[j0 + jj] >= 0) {
-                float* dst = args.dq_acc + ((int64_t)rid[j0 + jj] * p.h_q + hk * G) * D + dim;
+          for (int j = 0; j < 4; ++j) {
+            if (rid[j] >= 0) {
+              float* dst = args.dq_acc + ((int64_t)rid[j] * p.h_q + hk * G) * D + dim;
 #pragma unroll
-                for (int hh = 0; hh < 16; ++hh)
-                  if (hh < G) atomicAdd(dst + hh * D, part[jj][hh]);
-              }
+              for (int hh = 0; hh < 16; ++hh)
+                if (hh < G) atomicAdd(dst + hh * D, part[j][hh]);
             }
           }
         }
-        tc_fence_before();
-        warp_arrive(&sm.dq_empty);
       }
       ++job;
     }
