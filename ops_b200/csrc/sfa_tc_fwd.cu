@@ -77,9 +77,8 @@ struct Smem {
   alignas(1024) uint8_t q[2][kQBytes];
   alignas(1024) uint8_t p[kPBytes];
   JobDesc jd[kJD];
-  alignas(16) float red[9][16];
-  alignas(16) float redl[2][8][16];   // per-warp partial row sums of jobs j (j & 1)
-  alignas(16) float ml[2][16];        // per-job row max (j & 1)
+  alignas(16) float red[10][16];      // row max: 8 warp partials, the results of even / odd jobs
+  alignas(16) float reds[9][16];      // row sum of the previous job: 8 warp partials, the result
   int plist[kMaxTopk];
   uint64_t k_full[kKS], k_empty[kKS], v_full[kVS], v_empty[kVS];
   uint64_t q_full[2], q_empty[2];
@@ -146,30 +145,51 @@ __device__ __forceinline__ bool softmax_barrier(uint64_t* bar, uint32_t& use, in
   return wtw(bar, (use++) & 1, status, 30);
 }
 
-// Reduce over the 256 softmax threads; every thread gets all 16 results.
-// buf holds the 8 warps' partials in rows 0..7 and the final values in row 8.
+// One reduction round over the 256 softmax threads: the row max of job j
+// (v: all 16 heads in, the maxima over all threads out; also kept in row
+// 8 + (j & 1) of bm) together with the row sums of job j-1 (lw: this warp's
+// partial for head (lane >> 1) & 15; the totals land in row 8 of bs).  bm / bs
+// hold the 8 warps' partials in rows 0..7; the first softmax warp combines
+// them (lanes 0-15 the maxima, 16-31 the sums, each in a fixed order).
+// kMax = false reduces the sums only.
 template <bool kMax>
-__device__ __forceinline__ bool block_reduce16(float (&v)[16], float (*buf)[16], int w8, int lane, int tid,
-                                               uint64_t* bar, uint32_t& use, int32_t* status) {
-  const float r = warp_reduce16<kMax>(v, lane);
-  if ((lane & 1) == 0) buf[w8][(lane >> 1) & 15] = r;
+__device__ __forceinline__ bool reduce_round(float (&v)[16], float lw, int j, float (*bm)[16], float (*bs)[16],
+                                             int w8, int lane, int tid, uint64_t* bar, uint32_t& use,
+                                             int32_t* status) {
+  if constexpr (kMax) {
+    const float r = warp_reduce16<true>(v, lane);
+    if ((lane & 1) == 0) bm[w8][(lane >> 1) & 15] = r;
+  }
+  if ((lane & 1) == 0) bs[w8][(lane >> 1) & 15] = lw;
   if (!softmax_barrier(bar, use, status)) return false;
-  if (tid < 16) {
-    float a = buf[0][tid];
+  if (tid < 32 && (kMax || tid >= 16)) {
+    const bool mx = tid < 16;
+    const int h = tid & 15;
+    float (*b)[16] = mx ? bm : bs;
+    float a = b[0][h];
 #pragma unroll
-    for (int w = 1; w < 8; ++w) a = kMax ? fmaxf(a, buf[w][tid]) : a + buf[w][tid];
-    buf[8][tid] = a;
+    for (int w = 1; w < 8; ++w) a = mx ? fmaxf(a, b[w][h]) : a + b[w][h];
+    b[mx ? 8 + (j & 1) : 8][h] = a;
   }
   if (!softmax_barrier(bar, use, status)) return false;
+  if constexpr (kMax) {
 #pragma unroll
-  for (int h4 = 0; h4 < 4; ++h4) {
-    const float4 x = reinterpret_cast<const float4*>(buf[8])[h4];
-    v[4 * h4 + 0] = x.x;
-    v[4 * h4 + 1] = x.y;
-    v[4 * h4 + 2] = x.z;
-    v[4 * h4 + 3] = x.w;
+    for (int h4 = 0; h4 < 4; ++h4) {
+      const float4 x = reinterpret_cast<const float4*>(bm[8 + (j & 1)])[h4];
+      v[4 * h4 + 0] = x.x;
+      v[4 * h4 + 1] = x.y;
+      v[4 * h4 + 2] = x.z;
+      v[4 * h4 + 3] = x.w;
+    }
   }
   return true;
+}
+
+// Eight consecutive floats of a reduction result row (16-byte aligned).
+__device__ __forceinline__ void load8(const float* src, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(src)[0], b = reinterpret_cast<const float4*>(src)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
 template <int D>
@@ -485,16 +505,46 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
     float acc[8], mrun[8], lrun[8];      // epilogue state for heads 8*wg .. 8*wg+7
 #pragma unroll
     for (int h = 0; h < 8; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
-    bool ok = true;
-    auto softmax = [&](int j) -> bool {
+    // What this thread needs of a job, copied out of its descriptor one job
+    // ahead: under the gathers' shared-memory traffic one load round trip costs
+    // ~2K cycles, so none may sit on the softmax -> epilogue chain.
+    // w: flags (bits 0-2), vmask (4-7: bit i set when this thread's key of
+    // tile 4*wg + i is selected), nblk (8-15), kv head (16-31)
+    struct JobRegs {
+      uint32_t w;
+      int b, tq;
+      __device__ int flags() const { return (int)(w & 7u); }
+      __device__ uint32_t vmask() const { return (w >> 4) & 15u; }
+      __device__ int nblk() const { return (int)((w >> 8) & 255u); }
+      __device__ int hk() const { return (int)(w >> 16); }
+    };
+    auto load_job = [&](int j, JobRegs& r) {
       const JobDesc& d = sm.jd[j % kJD];
+      const int nblk = d.nblk, kv_len = d.kv_len, pos = d.pos;
+      uint32_t vm = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int bi = 2 * (wg * 4 + i) + (lrow >> 6);
+        // slots past nblk hold stale ids: unsigned arithmetic, and bi < nblk decides
+        const int key = (int)((uint32_t)d.blocks[bi] * 64u) + (lrow & 63);
+        if (bi < nblk && key < kv_len && (!p.causal || key <= pos)) vm |= 1u << i;
+      }
+      r.w = (uint32_t)d.flags | (vm << 4) | ((uint32_t)nblk << 8) | ((uint32_t)d.hk << 16);
+      r.b = d.b;
+      r.tq = d.tq;
+    };
+    bool ok = true;
+    float lw_prev = 0.f;                 // this warp's row-sum partial of the previous job
+    // softmax of job j: P tiles to shared memory; returns this warp's row-sum
+    // partial of job j (lw_out) and, loaded last so that their latency hides
+    // behind what follows, this warpgroup's 8 row maxima and row sums of job j-1
+    auto softmax = [&](int j, const JobRegs& r, float& lw_out, float (&mprev)[8], float (&lprev)[8]) -> bool {
       const int sb = j & 1;
       if (!wtw(&sm.s_full[sb], (j >> 1) & 1, st, 20)) return false;
       tc_fence_after();
-      const int nch = (d.nblk + 1) / 2;
+      const int nch = (r.nblk() + 1) / 2;
       const uint32_t ts = tl + kColS + sb * 128;
       float s[4][16];
-      bool valid[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int c = wg * 4 + i;
@@ -508,15 +558,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       for (int h = 0; h < 16; ++h) m[h] = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int c = wg * 4 + i;
-        const int bi = 2 * c + (lrow >> 6);
-        bool v = c < nch && bi < d.nblk;
-        if (v) {
-          const int key = d.blocks[bi] * 64 + (lrow & 63);
-          v = key < d.kv_len && (!p.causal || key <= d.pos);
-        }
-        valid[i] = v;
-        if (v) {
+        if ((r.vmask() >> i) & 1u) {
 #pragma unroll
           for (int h = 0; h < 16; ++h) {
             s[i][h] *= c2;
@@ -524,12 +566,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
           }
         }
       }
-      if (!block_reduce16<true>(m, sm.red, w8, lane, tid, &sm.sm_bar, bar_use, st)) return false;
-      if (tid < 16) {
-#pragma unroll
-        for (int h = 0; h < 16; ++h)
-          if (h == tid) sm.ml[sb][h] = m[h];
-      }
+      if (!reduce_round<true>(m, lw_prev, j, sm.red, sm.reds, w8, lane, tid, &sm.sm_bar, bar_use, st)) return false;
       float l[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) l[h] = 0.f;
@@ -540,10 +577,11 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       for (int i = 0; i < 4; ++i) {
         const int c = wg * 4 + i;
         if (c < nch) {
+          const bool valid = (r.vmask() >> i) & 1u;
           float pr[16];
 #pragma unroll
           for (int h = 0; h < 16; ++h) {
-            pr[h] = valid[i] ? ex2(s[i][h] - m[h]) : 0.f;
+            pr[h] = valid ? ex2(s[i][h] - m[h]) : 0.f;
             l[h] += pr[h];
           }
           // row = key within the segment; 32-byte rows, 32B swizzle (16-byte
@@ -559,56 +597,59 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       }
       fence_proxy_async_smem();
       warp_arrive(&sm.p_full[wg]);
-      // row sums: per-warp partials only; the epilogue of this job (after the
-      // next job's max reduction, whose barriers order these writes) adds them
-      const float lw = warp_reduce16<false>(l, lane);
-      if ((lane & 1) == 0) sm.redl[sb][w8][(lane >> 1) & 15] = lw;
+      // row 8 + ((j-1) & 1) of red and row 8 of reds stay until the next round's
+      // first barrier, which this thread reaches only after its epilogue of job j-1
+      load8(&sm.red[8 + ((j - 1) & 1)][wg * 8], mprev);
+      load8(&sm.reds[8][wg * 8], lprev);
+      lw_out = warp_reduce16<false>(l, lane);
       return true;
     };
-    auto epilogue = [&](int jj) -> bool {
-      const JobDesc& d = sm.jd[jj % kJD];
+    auto epilogue = [&](int jj, const JobRegs& r, const float (&mj)[8], const float (&lsj)[8]) -> bool {
       const int sb = jj & 1;
-      if (d.flags & kFirst) {
+      const int flags = r.flags(), hk = r.hk();
+      float s2v[8];                      // sink logits (log2 units), L1-resident
+      if (flags & kLast) {
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          const int hh = wg * 8 + h;
+          s2v[h] = (p.attn_sink && hh < G) ? __ldg(p.attn_sink + hk * G + hh) * kLog2e : -INFINITY;
+        }
+      }
+      if (flags & kFirst) {
 #pragma unroll
         for (int h = 0; h < 8; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
       }
       if (!wtw(&sm.o_full[sb], (jj >> 1) & 1, st, 22)) return false;
       tc_fence_after();
-      if (d.nblk > 0) {
+      if (r.nblk() > 0) {
         float o[16];
         tmem_ld16(tl + kColO + sb * kNH, o);   // all 16 heads; this warpgroup keeps 8
         tmem_ld_wait();
 #pragma unroll
         for (int h = 0; h < 8; ++h) {
-          const int hh = wg * 8 + h;
           const float ov = wg ? o[8 + h] : o[h];
-          const float ms = sm.ml[sb][hh];
-          float ls = 0.f;
-#pragma unroll
-          for (int w = 0; w < 8; ++w) ls += sm.redl[sb][w][hh];
-          const float M = fmaxf(mrun[h], ms);
-          const float a = ex2(mrun[h] - M), bb = ex2(ms - M);
+          const float M = fmaxf(mrun[h], mj[h]);
+          const float a = ex2(mrun[h] - M), bb = ex2(mj[h] - M);
           acc[h] = acc[h] * a + ov * bb;
-          lrun[h] = lrun[h] * a + ls * bb;
+          lrun[h] = lrun[h] * a + lsj[h] * bb;
           mrun[h] = M;
         }
       }
       tc_fence_before();
       warp_arrive(&sm.o_empty[sb]);
-      if (d.flags & kLast) {
-        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.o) + d.b * p.o_sb + (int64_t)d.tq * p.o_st +
-                           (int64_t)(d.hk * G) * p.o_sh;
-        float* lse = p.lse + d.b * p.l_sb + (int64_t)d.tq * p.l_st + (int64_t)(d.hk * G) * p.l_sh;
+      if (flags & kLast) {
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.o) + r.b * p.o_sb + (int64_t)r.tq * p.o_st +
+                           (int64_t)(hk * G) * p.o_sh;
+        float* lse = p.lse + r.b * p.l_sb + (int64_t)r.tq * p.l_st + (int64_t)(hk * G) * p.l_sh;
 #pragma unroll
         for (int h = 0; h < 8; ++h) {
           const int hh = wg * 8 + h;
           if (hh < G) {
-            const float s2 = p.attn_sink ? __ldg(p.attn_sink + d.hk * G + hh) * kLog2e : -INFINITY;
-            const float M = fmaxf(mrun[h], s2);
+            const float M = fmaxf(mrun[h], s2v[h]);
             float outv = 0.f, lv = -INFINITY;
             if (M != -INFINITY) {
               const float w = ex2(mrun[h] - M);
-              const float lt = lrun[h] * w + ex2(s2 - M);
+              const float lt = lrun[h] * w + ex2(s2v[h] - M);
               outv = __fdividef(acc[h] * w, lt);
               lv = (M + lg2(lt)) * kLn2;
             }
@@ -620,18 +661,33 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       warp_arrive(&sm.jd_empty[jj % kJD]);
       return true;
     };
+    // job j's softmax, then the next descriptor's copy, then job j-1's epilogue
+    // (its O^T accumulates meanwhile)
+    JobRegs cur{}, prev{};
     int job = 0;
-    while (ok) {
-      const int js = job % kJD;
-      if (!(ok = wtw(&sm.jd_full[js], (job / kJD) & 1, st, 23))) break;
-      if (sm.jd[js].flags & kSentinel) break;
-      if (!(ok = softmax(job))) break;
-      if (job > 0 && !(ok = epilogue(job - 1))) break;
+    if ((ok = wtw(&sm.jd_full[0], 0, st, 23))) load_job(0, cur);
+    while (ok && !(cur.flags() & kSentinel)) {
+      float lw, mprev[8], lprev[8];
+      if (!(ok = softmax(job, cur, lw, mprev, lprev))) break;
+      const int jn = job + 1;
+      JobRegs nxt;
+      if (!(ok = wtw(&sm.jd_full[jn % kJD], (jn / kJD) & 1, st, 23))) break;
+      load_job(jn, nxt);
+      if (job > 0 && !(ok = epilogue(job - 1, prev, mprev, lprev))) break;
+      prev = cur;
+      cur = nxt;
+      lw_prev = lw;
       ++job;
     }
-    // the last job's row-sum partials and max were written by other warps with
-    // no later reduction to order them: one more barrier before its epilogue
-    if (ok && job > 0 && softmax_barrier(&sm.sm_bar, bar_use, st)) epilogue(job - 1);
+    // the last job's row sums still need their reduction round
+    if (ok && job > 0) {
+      float unused[16], mlast[8], llast[8];
+      if (reduce_round<false>(unused, lw_prev, job, sm.red, sm.reds, w8, lane, tid, &sm.sm_bar, bar_use, st)) {
+        load8(&sm.red[8 + ((job - 1) & 1)][wg * 8], mlast);
+        load8(&sm.reds[8][wg * 8], llast);
+        epilogue(job - 1, prev, mlast, llast);
+      }
+    }
   }
 
   tc_fence_before();
@@ -682,6 +738,7 @@ bool tc_fwd_supported(const SfaParams& p, const char** why) {
   if (p.topk > fwd::kMaxTopk) { *why = "topk must be <= 64"; return false; }
   if (p.d_qk != p.d_v || (p.d_qk != 64 && p.d_qk != 128)) { *why = "head dim must be 64 or 128 (D_qk == D_v)"; return false; }
   if (G > fwd::kNH) { *why = "query heads per kv head must be <= 16"; return false; }
+  if (p.h_kv > 65535) { *why = "at most 65535 kv heads"; return false; }
   if (!tma_compatible(p.q, p.q_sb, p.q_st, p.q_sh) || !tma_compatible(p.k, p.k_sb, p.k_st, p.k_sh) ||
       !tma_compatible(p.v, p.v_sb, p.v_st, p.v_sh)) {
     *why = "q/k/v need 16-byte aligned base and strides";
