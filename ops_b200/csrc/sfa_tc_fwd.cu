@@ -553,6 +553,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       tmem_ld_wait();
       tc_fence_before();
       warp_arrive(&sm.s_empty[sb]);
+      // the max of the raw scores (c2 > 0); the scale folds into the exponent's FMA
       float m[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) m[h] = -INFINITY;
@@ -560,16 +561,16 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       for (int i = 0; i < 4; ++i) {
         if ((r.vmask() >> i) & 1u) {
 #pragma unroll
-          for (int h = 0; h < 16; ++h) {
-            s[i][h] *= c2;
-            m[h] = fmaxf(m[h], s[i][h]);
-          }
+          for (int h = 0; h < 16; ++h) m[h] = fmaxf(m[h], s[i][h]);
         }
       }
       if (!reduce_round<true>(m, lw_prev, j, sm.red, sm.reds, w8, lane, tid, &sm.sm_bar, bar_use, st)) return false;
       float l[16];
 #pragma unroll
-      for (int h = 0; h < 16; ++h) l[h] = 0.f;
+      for (int h = 0; h < 16; ++h) {
+        l[h] = 0.f;
+        m[h] *= -c2;                     // finite for every head once a key is selected
+      }
       // this warpgroup's half of the P buffer is free once PV(j-1) read it
       if (!wtw(&sm.p_empty[wg], (j & 1) ^ 1, st, 21)) return false;
       const uint32_t pbase = smem_u32(&sm.p[0]);
@@ -581,7 +582,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
           float pr[16];
 #pragma unroll
           for (int h = 0; h < 16; ++h) {
-            pr[h] = valid ? ex2(s[i][h] - m[h]) : 0.f;
+            pr[h] = valid ? ex2(fmaf(s[i][h], c2, m[h])) : 0.f;
             l[h] += pr[h];
           }
           // row = key within the segment; 32-byte rows, 32B swizzle (16-byte
@@ -604,59 +605,70 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       lw_out = warp_reduce16<false>(l, lane);
       return true;
     };
+    // mj: the raw-score maxima of job jj (scaled here), lsj: its row sums
     auto epilogue = [&](int jj, const JobRegs& r, const float (&mj)[8], const float (&lsj)[8]) -> bool {
       const int sb = jj & 1;
       const int flags = r.flags(), hk = r.hk();
-      float s2v[8];                      // sink logits (log2 units), L1-resident
-      if (flags & kLast) {
-#pragma unroll
-        for (int h = 0; h < 8; ++h) {
-          const int hh = wg * 8 + h;
-          s2v[h] = (p.attn_sink && hh < G) ? __ldg(p.attn_sink + hk * G + hh) * kLog2e : -INFINITY;
-        }
-      }
-      if (flags & kFirst) {
-#pragma unroll
-        for (int h = 0; h < 8; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
-      }
+      // lane l handles the per-head scalars of head 8*wg + (l & 7)
+      const int hl = wg * 8 + (lane & 7);
+      float s2 = -INFINITY;              // sink logit, log2 units (L1-resident)
+      if ((flags & kLast) && p.attn_sink && hl < G) s2 = __ldg(p.attn_sink + hk * G + hl) * kLog2e;
       if (!wtw(&sm.o_full[sb], (jj >> 1) & 1, st, 22)) return false;
       tc_fence_after();
       if (r.nblk() > 0) {
         float o[16];
         tmem_ld16(tl + kColO + sb * kNH, o);   // all 16 heads; this warpgroup keeps 8
         tmem_ld_wait();
+        if (flags & kFirst) {
 #pragma unroll
-        for (int h = 0; h < 8; ++h) {
-          const float ov = wg ? o[8 + h] : o[h];
-          const float M = fmaxf(mrun[h], mj[h]);
-          const float a = ex2(mrun[h] - M), bb = ex2(mj[h] - M);
-          acc[h] = acc[h] * a + ov * bb;
-          lrun[h] = lrun[h] * a + lsj[h] * bb;
-          mrun[h] = M;
+          for (int h = 0; h < 8; ++h) {
+            acc[h] = wg ? o[8 + h] : o[h];
+            lrun[h] = lsj[h];
+            mrun[h] = mj[h] * c2;
+          }
+        } else {
+#pragma unroll
+          for (int h = 0; h < 8; ++h) {
+            const float ov = wg ? o[8 + h] : o[h];
+            const float ms = mj[h] * c2;
+            const float M = fmaxf(mrun[h], ms);
+            const float a = ex2(mrun[h] - M), bb = ex2(ms - M);
+            acc[h] = acc[h] * a + ov * bb;
+            lrun[h] = lrun[h] * a + lsj[h] * bb;
+            mrun[h] = M;
+          }
         }
+      } else if (flags & kFirst) {
+#pragma unroll
+        for (int h = 0; h < 8; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
       }
       tc_fence_before();
       warp_arrive(&sm.o_empty[sb]);
       if (flags & kLast) {
+        // the head's running max / sum are the same in every thread: each lane
+        // finishes one head and the scale goes out by shuffle
+        float mh = mrun[0], lh = lrun[0];
+#pragma unroll
+        for (int h = 1; h < 8; ++h)
+          if ((lane & 7) == h) { mh = mrun[h]; lh = lrun[h]; }
+        const float M = fmaxf(mh, s2);
+        float inv = 0.f, lv = -INFINITY;
+        if (M != -INFINITY) {
+          const float w = ex2(mh - M);
+          const float lt = lh * w + ex2(s2 - M);
+          inv = __fdividef(w, lt);
+          lv = (M + lg2(lt)) * kLn2;
+        }
         __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.o) + r.b * p.o_sb + (int64_t)r.tq * p.o_st +
                            (int64_t)(hk * G) * p.o_sh;
         float* lse = p.lse + r.b * p.l_sb + (int64_t)r.tq * p.l_st + (int64_t)(hk * G) * p.l_sh;
 #pragma unroll
         for (int h = 0; h < 8; ++h) {
           const int hh = wg * 8 + h;
-          if (hh < G) {
-            const float M = fmaxf(mrun[h], s2v[h]);
-            float outv = 0.f, lv = -INFINITY;
-            if (M != -INFINITY) {
-              const float w = ex2(mrun[h] - M);
-              const float lt = lrun[h] * w + ex2(s2v[h] - M);
-              outv = __fdividef(acc[h] * w, lt);
-              lv = (M + lg2(lt)) * kLn2;
-            }
-            if (lrow < D) o[hh * p.o_sh + lrow] = f2bf(outv);
-            if (lrow == h) lse[hh * p.l_sh] = lv;
-          }
+          const float sc = __shfl_sync(0xffffffffu, inv, h);
+          if (hh < G && lrow < D) o[hh * p.o_sh + lrow] = f2bf(acc[h] * sc);
         }
+        if (wq == 0 && lane < 8 && hl < G) lse[hl * p.l_sh] = lv;
       }
       warp_arrive(&sm.jd_empty[jj % kJD]);
       return true;
@@ -739,6 +751,7 @@ bool tc_fwd_supported(const SfaParams& p, const char** why) {
   if (p.d_qk != p.d_v || (p.d_qk != 64 && p.d_qk != 128)) { *why = "head dim must be 64 or 128 (D_qk == D_v)"; return false; }
   if (G > fwd::kNH) { *why = "query heads per kv head must be <= 16"; return false; }
   if (p.h_kv > 65535) { *why = "at most 65535 kv heads"; return false; }
+  if (!(p.scale > 0.f)) { *why = "needs a positive softmax scale"; return false; }
   if (!tma_compatible(p.q, p.q_sb, p.q_st, p.q_sh) || !tma_compatible(p.k, p.k_sb, p.k_st, p.k_sh) ||
       !tma_compatible(p.v, p.v_sb, p.v_st, p.v_sh)) {
     *why = "q/k/v need 16-byte aligned base and strides";
