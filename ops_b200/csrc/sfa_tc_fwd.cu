@@ -67,8 +67,11 @@ struct JobDesc {
 
 template <int D>
 struct Smem {
-  static constexpr int kKS = D == 128 ? 3 : 6;      // K ring stages (128 keys each)
-  static constexpr int kVS = D == 128 ? 2 : 4;      // V ring stages
+  // K ring stages (128 keys each) and V ring stages.  D = 128: one K stage
+  // less and one V stage more measured 4.61 vs 4.91 ms (c2) in the same space:
+  // PV starts when the softmax hands over P, so its V must already be in flight.
+  static constexpr int kKS = D == 128 ? 2 : 6;
+  static constexpr int kVS = D == 128 ? 3 : 4;
   static constexpr int kStageBytes = 128 * D * 2;
   static constexpr int kQBytes = kNH * D * 2;
   static constexpr int kPBytes = kSegBlocks * 64 * kNH * 2;
@@ -77,8 +80,8 @@ struct Smem {
   alignas(1024) uint8_t q[2][kQBytes];
   alignas(1024) uint8_t p[kPBytes];
   JobDesc jd[kJD];
-  alignas(16) float red[10][16];      // row max: 8 warp partials, the results of even / odd jobs
-  alignas(16) float reds[9][16];      // row sum of the previous job: 8 warp partials, the result
+  alignas(16) int bmax[4][16];        // row max of job j in buffer j % 4 (order-preserving ints)
+  alignas(16) float bsum[2][16][8];   // row-sum partials of job j-1 in buffer j & 1: [head][warp]
   int plist[kMaxTopk];
   uint64_t k_full[kKS], k_empty[kKS], v_full[kVS], v_empty[kVS];
   uint64_t q_full[2], q_empty[2];
@@ -145,51 +148,63 @@ __device__ __forceinline__ bool softmax_barrier(uint64_t* bar, uint32_t& use, in
   return wtw(bar, (use++) & 1, status, 30);
 }
 
-// One reduction round over the 256 softmax threads: the row max of job j
-// (v: all 16 heads in, the maxima over all threads out; also kept in row
-// 8 + (j & 1) of bm) together with the row sums of job j-1 (lw: this warp's
-// partial for head (lane >> 1) & 15; the totals land in row 8 of bs).  bm / bs
-// hold the 8 warps' partials in rows 0..7; the first softmax warp combines
-// them (lanes 0-15 the maxima, 16-31 the sums, each in a fixed order).
-// kMax = false reduces the sums only.
-template <bool kMax>
-__device__ __forceinline__ bool reduce_round(float (&v)[16], float lw, int j, float (*bm)[16], float (*bs)[16],
-                                             int w8, int lane, int tid, uint64_t* bar, uint32_t& use,
-                                             int32_t* status) {
-  if constexpr (kMax) {
-    const float r = warp_reduce16<true>(v, lane);
-    if ((lane & 1) == 0) bm[w8][(lane >> 1) & 15] = r;
-  }
-  if ((lane & 1) == 0) bs[w8][(lane >> 1) & 15] = lw;
-  if (!softmax_barrier(bar, use, status)) return false;
-  if (tid < 32 && (kMax || tid >= 16)) {
-    const bool mx = tid < 16;
-    const int h = tid & 15;
-    float (*b)[16] = mx ? bm : bs;
-    float a = b[0][h];
-#pragma unroll
-    for (int w = 1; w < 8; ++w) a = mx ? fmaxf(a, b[w][h]) : a + b[w][h];
-    b[mx ? 8 + (j & 1) : 8][h] = a;
-  }
-  if (!softmax_barrier(bar, use, status)) return false;
-  if constexpr (kMax) {
-#pragma unroll
-    for (int h4 = 0; h4 < 4; ++h4) {
-      const float4 x = reinterpret_cast<const float4*>(bm[8 + (j & 1)])[h4];
-      v[4 * h4 + 0] = x.x;
-      v[4 * h4 + 1] = x.y;
-      v[4 * h4 + 2] = x.z;
-      v[4 * h4 + 3] = x.w;
-    }
-  }
-  return true;
+// Floats as ints with the same order, so that a shared-memory integer max
+// reduces them (no NaNs here).
+__device__ __forceinline__ int f2ord(float f) {
+  const int i = __float_as_int(f);
+  return i >= 0 ? i : i ^ 0x7FFFFFFF;
+}
+__device__ __forceinline__ float ord2f(int i) { return __int_as_float(i >= 0 ? i : i ^ 0x7FFFFFFF); }
+
+__device__ __forceinline__ void red_max_shared(const int* addr, int v) {
+  asm volatile("red.shared.max.s32 [%0], %1;" ::"r"(smem_u32(addr)), "r"(v) : "memory");
 }
 
-// Eight consecutive floats of a reduction result row (16-byte aligned).
+// Four ordered ints of a max row back to floats (16-byte aligned).
+__device__ __forceinline__ void load_max4(const int* src, float* v) {
+  const int4 x = *reinterpret_cast<const int4*>(src);
+  v[0] = ord2f(x.x);
+  v[1] = ord2f(x.y);
+  v[2] = ord2f(x.z);
+  v[3] = ord2f(x.w);
+}
+
+// Eight consecutive floats (16-byte aligned).
 __device__ __forceinline__ void load8(const float* src, float (&v)[8]) {
   const float4 a = reinterpret_cast<const float4*>(src)[0], b = reinterpret_cast<const float4*>(src)[1];
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
   v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// One reduction round over the 256 softmax threads, with a single barrier:
+// the row max of job j (v: all 16 heads in; the maxima over all threads out)
+// by shared-memory integer max into bmax[j % 4], and this warp's row-sum
+// partial of job j-1 (lw, for head (lane >> 1) & 15) into bsum[j & 1][head][warp].
+// Buffer lifetimes (every thread reads a buffer before it arrives at the
+// barrier of the round that recycles it):
+//   bmax[j % 4]  written in round j, read after its barrier and again at the
+//                end of softmax(j+1) (for the epilogue of j); the first warp
+//                resets it after the barrier of round j+2, and round j+4
+//                writes it after the barrier of round j+3;
+//   bsum[j & 1]  written in round j, read at the end of softmax(j) (for the
+//                epilogue of j-1); round j+2 rewrites it.
+// kMax = false: the sum partials only (the last job's).
+template <bool kMax>
+__device__ __forceinline__ bool reduce_round(float (&v)[16], float lw, int j, int (*bmax)[16], float (*bsum)[16][8],
+                                             int w8, int lane, int tid, uint64_t* bar, uint32_t& use,
+                                             int32_t* status) {
+  if constexpr (kMax) {
+    const float r = warp_reduce16<true>(v, lane);
+    if ((lane & 1) == 0) red_max_shared(&bmax[j % 4][(lane >> 1) & 15], f2ord(r));
+  }
+  if ((lane & 1) == 0) bsum[j & 1][(lane >> 1) & 15][w8] = lw;
+  if (!softmax_barrier(bar, use, status)) return false;
+  if constexpr (kMax) {
+    if (tid < 16) bmax[(j + 2) % 4][tid] = f2ord(-INFINITY);
+#pragma unroll
+    for (int h4 = 0; h4 < 4; ++h4) load_max4(&bmax[j % 4][4 * h4], &v[4 * h4]);
+  }
+  return true;
 }
 
 template <int D>
@@ -226,6 +241,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
     for (int i = 0; i < kJD; ++i) { mbar_init(&sm.jd_full[i], 1); mbar_init(&sm.jd_empty[i], 3 + kSoftmaxThreads / 32); }
     fence_barrier_init();
   }
+  if (threadIdx.x < 64) sm.bmax[threadIdx.x / 16][threadIdx.x % 16] = f2ord(-INFINITY);
   // padded query rows (G..15) stay zero for the whole kernel
   for (int i = threadIdx.x; i < 2 * Smem<D>::kQBytes / 16; i += kThreads)
     reinterpret_cast<uint4*>(&sm.q[0][0])[i] = make_uint4(0, 0, 0, 0);
@@ -502,9 +518,9 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
     const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
     const float c2 = p.scale * kLog2e;
     uint32_t bar_use = 0;
-    float acc[8], mrun[8], lrun[8];      // epilogue state for heads 8*wg .. 8*wg+7
+    float acc[8], mrun[8];               // epilogue state for heads 8*wg .. 8*wg+7
 #pragma unroll
-    for (int h = 0; h < 8; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
+    for (int h = 0; h < 8; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; }
     // What this thread needs of a job, copied out of its descriptor one job
     // ahead: under the gathers' shared-memory traffic one load round trip costs
     // ~2K cycles, so none may sit on the softmax -> epilogue chain.
@@ -535,9 +551,12 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
     };
     bool ok = true;
     float lw_prev = 0.f;                 // this warp's row-sum partial of the previous job
+    const int hl = wg * 8 + (lane & 7);  // lane l finishes head 8*wg + (l & 7) in the epilogue
+    float lrun_l = 0.f;                  // running row sum of head hl
     // softmax of job j: P tiles to shared memory; returns this warp's row-sum
     // partial of job j (lw_out) and, loaded last so that their latency hides
-    // behind what follows, this warpgroup's 8 row maxima and row sums of job j-1
+    // behind what follows, this warpgroup's 8 row maxima of job j-1 (raw
+    // scores) and the 8 warp partials of its row sum for head hl (lprev)
     auto softmax = [&](int j, const JobRegs& r, float& lw_out, float (&mprev)[8], float (&lprev)[8]) -> bool {
       const int sb = j & 1;
       if (!wtw(&sm.s_full[sb], (j >> 1) & 1, st, 20)) return false;
@@ -564,7 +583,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
           for (int h = 0; h < 16; ++h) m[h] = fmaxf(m[h], s[i][h]);
         }
       }
-      if (!reduce_round<true>(m, lw_prev, j, sm.red, sm.reds, w8, lane, tid, &sm.sm_bar, bar_use, st)) return false;
+      if (!reduce_round<true>(m, lw_prev, j, sm.bmax, sm.bsum, w8, lane, tid, &sm.sm_bar, bar_use, st)) return false;
       float l[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) {
@@ -598,19 +617,17 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
       }
       fence_proxy_async_smem();
       warp_arrive(&sm.p_full[wg]);
-      // row 8 + ((j-1) & 1) of red and row 8 of reds stay until the next round's
-      // first barrier, which this thread reaches only after its epilogue of job j-1
-      load8(&sm.red[8 + ((j - 1) & 1)][wg * 8], mprev);
-      load8(&sm.reds[8][wg * 8], lprev);
+      load_max4(&sm.bmax[(j + 3) % 4][wg * 8], &mprev[0]);      // job j-1
+      load_max4(&sm.bmax[(j + 3) % 4][wg * 8 + 4], &mprev[4]);
+      load8(&sm.bsum[j & 1][hl][0], lprev);
       lw_out = warp_reduce16<false>(l, lane);
       return true;
     };
-    // mj: the raw-score maxima of job jj (scaled here), lsj: its row sums
+    // mj: the raw-score maxima of job jj (scaled here); lsj: the 8 warp
+    // partials of its row sum for head hl, added in a fixed order
     auto epilogue = [&](int jj, const JobRegs& r, const float (&mj)[8], const float (&lsj)[8]) -> bool {
       const int sb = jj & 1;
       const int flags = r.flags(), hk = r.hk();
-      // lane l handles the per-head scalars of head 8*wg + (l & 7)
-      const int hl = wg * 8 + (lane & 7);
       float s2 = -INFINITY;              // sink logit, log2 units (L1-resident)
       if ((flags & kLast) && p.attn_sink && hl < G) s2 = __ldg(p.attn_sink + hk * G + hl) * kLog2e;
       if (!wtw(&sm.o_full[sb], (jj >> 1) & 1, st, 22)) return false;
@@ -619,14 +636,18 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
         float o[16];
         tmem_ld16(tl + kColO + sb * kNH, o);   // all 16 heads; this warpgroup keeps 8
         tmem_ld_wait();
+        float ls = lsj[0];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) ls += lsj[w];
         if (flags & kFirst) {
 #pragma unroll
           for (int h = 0; h < 8; ++h) {
             acc[h] = wg ? o[8 + h] : o[h];
-            lrun[h] = lsj[h];
             mrun[h] = mj[h] * c2;
           }
+          lrun_l = ls;
         } else {
+          float al = 0.f, bl = 0.f;
 #pragma unroll
           for (int h = 0; h < 8; ++h) {
             const float ov = wg ? o[8 + h] : o[h];
@@ -634,23 +655,26 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
             const float M = fmaxf(mrun[h], ms);
             const float a = ex2(mrun[h] - M), bb = ex2(ms - M);
             acc[h] = acc[h] * a + ov * bb;
-            lrun[h] = lrun[h] * a + lsj[h] * bb;
             mrun[h] = M;
+            if ((lane & 7) == h) { al = a; bl = bb; }
           }
+          lrun_l = lrun_l * al + ls * bl;
         }
       } else if (flags & kFirst) {
 #pragma unroll
-        for (int h = 0; h < 8; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; lrun[h] = 0.f; }
+        for (int h = 0; h < 8; ++h) { acc[h] = 0.f; mrun[h] = -INFINITY; }
+        lrun_l = 0.f;
       }
       tc_fence_before();
       warp_arrive(&sm.o_empty[sb]);
       if (flags & kLast) {
         // the head's running max / sum are the same in every thread: each lane
         // finishes one head and the scale goes out by shuffle
-        float mh = mrun[0], lh = lrun[0];
+        float mh = mrun[0];
+        const float lh = lrun_l;
 #pragma unroll
         for (int h = 1; h < 8; ++h)
-          if ((lane & 7) == h) { mh = mrun[h]; lh = lrun[h]; }
+          if ((lane & 7) == h) mh = mrun[h];
         const float M = fmaxf(mh, s2);
         float inv = 0.f, lv = -INFINITY;
         if (M != -INFINITY) {
@@ -694,9 +718,10 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
     // the last job's row sums still need their reduction round
     if (ok && job > 0) {
       float unused[16], mlast[8], llast[8];
-      if (reduce_round<false>(unused, lw_prev, job, sm.red, sm.reds, w8, lane, tid, &sm.sm_bar, bar_use, st)) {
-        load8(&sm.red[8 + ((job - 1) & 1)][wg * 8], mlast);
-        load8(&sm.reds[8][wg * 8], llast);
+      if (reduce_round<false>(unused, lw_prev, job, sm.bmax, sm.bsum, w8, lane, tid, &sm.sm_bar, bar_use, st)) {
+        load_max4(&sm.bmax[(job + 3) % 4][wg * 8], &mlast[0]);
+        load_max4(&sm.bmax[(job + 3) % 4][wg * 8 + 4], &mlast[4]);
+        load8(&sm.bsum[job & 1][hl][0], llast);
         epilogue(job - 1, prev, mlast, llast);
       }
     }
