@@ -743,57 +743,54 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
     }
   } else if (warp == 10 || warp == 12) {
     // ============================================================ TMA loads
-    // Two loader threads: warp 10 gathers K_e / V_e and the batches' Q rows,
+    // Two loader warps: warp 10 gathers K_e / V_e and the batches' Q rows,
     // warp 12 their dO rows.  Each 16-head row is a 2 KB box and one thread
-    // issues about one box per 100 cycles, so one loader alone would set the
-    // pace.  The batch's coordinates are read into registers up front (no
-    // shared-memory load between two TMA issues).
-    if (lane == 0) {
+    // issues about one box per 100 cycles, so lane j issues query j's boxes:
+    // the batch's copies leave together instead of one after another.
+    {
       const bool is_q = warp == 10;
       const CUtensorMap* map = is_q ? &tmq : &tmdo;
       int job = 0, gb = 0;
       bool ok = true;
       while (ok) {
         const int js = job % kJD;
-        if (!(ok = wt(&sm.jd_full[js], (job / kJD) & 1, st, is_q ? 5 : 8))) break;
+        if (!(ok = wtw(&sm.jd_full[js], (job / kJD) & 1, st, is_q ? 5 : 8))) break;
         const JobDesc& d = sm.jd[js];
         const int flags = d.flags;
         if (flags & kSentinel) break;
         const int hk = d.hk, n = d.n, krow = d.kv0 + d.e * 64, kb = d.b;
-        mbar_arrive(&sm.jd_empty[js]);
+        warp_arrive(&sm.jd_empty[js]);
         if (is_q) {
-          if (!(ok = wt(&sm.kv_empty, (job & 1) ^ 1, st, 6))) break;
-          mbar_arrive_expect_tx(&sm.kv_full, 2u * 64u * D * 2u);
+          if (lane == 0) {
+            ok = wt(&sm.kv_empty, (job & 1) ^ 1, st, 6);
+            if (ok) {
+              mbar_arrive_expect_tx(&sm.kv_full, 2u * 64u * D * 2u);
 #pragma unroll
-          for (int cd = 0; cd < D / 64; ++cd) {
-            tma_load_4d(&sm.ke[cd * 64 * 128], &tmk, &sm.kv_full, cd * 64, hk, krow, kb);
-            tma_load_4d(&sm.ve[cd * 64 * 128], &tmv, &sm.kv_full, cd * 64, hk, krow, kb);
+              for (int cd = 0; cd < D / 64; ++cd) {
+                tma_load_4d(&sm.ke[cd * 64 * 128], &tmk, &sm.kv_full, cd * 64, hk, krow, kb);
+                tma_load_4d(&sm.ve[cd * 64 * 128], &tmv, &sm.kv_full, cd * 64, hk, krow, kb);
+              }
+            }
           }
+          if (!(ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0)) break;
         }
         const int nb = (n + kQB - 1) / kQB;
         for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
           const int slot = gb % kMeta, s = gb & 1;
-          if (!(ok = wt(&sm.meta_full[slot], (gb / kMeta) & 1, st, is_q ? 7 : 9))) break;
+          if (!(ok = wtw(&sm.meta_full[slot], (gb / kMeta) & 1, st, is_q ? 7 : 9))) break;
           const BatchMeta& mt = sm.meta[slot];
           const int m = mt.m;
-          int tq[kQB], bq[kQB];
-#pragma unroll
-          for (int j = 0; j < kQB; ++j) {
-            tq[j] = mt.tq[j];
-            bq[j] = mt.b[j];
-          }
-          mbar_arrive(&sm.meta_empty[slot]);
-          if (!(ok = wt(&sm.b_empty[s], ((gb >> 1) & 1) ^ 1, st, is_q ? 3 : 19))) break;
+          const int tq = lane < kQB ? mt.tq[lane] : 0, bq = lane < kQB ? mt.b[lane] : 0;
+          warp_arrive(&sm.meta_empty[slot]);
+          if (!(ok = wtw(&sm.b_empty[s], ((gb >> 1) & 1) ^ 1, st, is_q ? 3 : 19))) break;
           uint64_t* full = is_q ? &sm.bq_full[s] : &sm.bdo_full[s];
           uint8_t* buf = is_q ? sm.qb[s] : sm.dob[s];
-          mbar_arrive_expect_tx(full, (uint32_t)(m * G * D * 2));
+          if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(m * G * D * 2));
+          __syncwarp();
+          if (lane < m) {
 #pragma unroll
-          for (int j = 0; j < kQB; ++j) {
-            if (j < m) {
-#pragma unroll
-              for (int cd = 0; cd < D / 64; ++cd)
-                tma_load_4d(buf + cd * 128 * 128 + j * 16 * 128, map, full, cd * 64, hk * G, tq[j], bq[j]);
-            }
+            for (int cd = 0; cd < D / 64; ++cd)
+              tma_load_4d(buf + cd * 128 * 128 + lane * 16 * 128, map, full, cd * 64, hk * G, tq, bq);
           }
         }
         ++job;
@@ -992,16 +989,19 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         if (!(ok = wtw(&sm.meta_full[slot], (gb / kMeta) & 1, st, 24))) break;
         const BatchMeta& mt = sm.meta[slot];
         // this thread's (query, head) row: lse and delta straight from global
-        // memory (their latency overlaps the wait for S/dP below)
-        const int pos = mt.pos[jq];
+        // memory, issued after the slot is released (the arrive's release
+        // would otherwise wait for them), so their latency overlaps the wait
+        // for S/dP below
+        const int pos = mt.pos[jq], qb_ = mt.b[jq], qtq = mt.tq[jq], qrow = mt.rowid[jq];
+        const bool live = jq < mt.m && h < G;
+        warp_arrive(&sm.meta_empty[slot]);
         float lse2 = -INFINITY, dl = 0.f;
-        if (jq < mt.m && h < G) {
+        if (live) {
           const int hh = d.hk * G + h;
-          lse2 = __ldg(p.lse + mt.b[jq] * p.l_sb + (int64_t)mt.tq[jq] * p.l_st + (int64_t)hh * p.l_sh) * kLog2e;
-          dl = __ldg(args.delta + (int64_t)mt.rowid[jq] * p.h_q + hh);
+          lse2 = __ldg(p.lse + qb_ * p.l_sb + (int64_t)qtq * p.l_st + (int64_t)hh * p.l_sh) * kLog2e;
+          dl = __ldg(args.delta + (int64_t)qrow * p.h_q + hh);
         }
         const bool rvalid = lse2 != -INFINITY;
-        warp_arrive(&sm.meta_empty[slot]);
         // keys of this warpgroup valid for this row: key_base + i < lim
         int lim = rvalid ? min(kv_len, p.causal ? pos + 1 : kv_len) - key_base : 0;
         if (!(ok = wtw(&sm.sdp_full[s], (gb >> 1) & 1, st, 21))) break;
