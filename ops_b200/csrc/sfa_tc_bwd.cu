@@ -513,9 +513,10 @@ cudaError_t launch(const SfaParams& p, const float* delta, cudaStream_t stream) 
 // =========================================================================
 namespace dkdv {
 
-constexpr int kThreads = 416;       // warp 0 metadata, 1 S/dP issuer, 2-9 P/dS + epilogue, 10 K/V/Q loads,
-                                    // 11 dV/dK issuer, 12 dO loads
-constexpr int kThreadsDQ = 672;     // + warps 13-20: fused-dQ reducers (two per TMEM lane quadrant)
+constexpr int kThreads = 384;       // warp 0 metadata, 1 S/dP issuer, 2-9 P/dS + epilogue, 10 loads,
+                                    // 11 dV/dK issuer
+constexpr int kThreadsDQ = 640;     // + warps 12-19: fused-dQ reducers (two per TMEM lane quadrant);
+                                    // 20 warps leave 96 registers a thread (21 would leave 80)
 constexpr int kWG = 256;            // P/dS threads: 2 warpgroups, each takes 32 of the 64 keys
 constexpr int kQB = 8;              // queries per batch (x 16 heads = 128 MMA rows)
 constexpr int kMeta = 6;            // batch metadata ring depth
@@ -614,7 +615,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
     // counts in warps for the P/dS warps (one arrival per warp)
     for (int i = 0; i < kMeta; ++i) {
       mbar_init(&sm.meta_full[i], 1);
-      mbar_init(&sm.meta_empty[i], 2 + kWG / 32 + (kDQ ? 8 : 0));   // loader threads, P/dS warps, reducers
+      mbar_init(&sm.meta_empty[i], 1 + kWG / 32 + (kDQ ? 8 : 0));   // loader warp, P/dS warps, reducers
     }
     mbar_init(&sm.kv_full, 1);
     mbar_init(&sm.kv_empty, 1);
@@ -622,11 +623,11 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
     mbar_init(&sm.pds_empty, 1);
     mbar_init(&sm.dq_full, 1);
     mbar_init(&sm.dq_empty, 8);   // the 8 reducer warps
-    // consumers of a job descriptor: the two issuers, the two loader threads,
+    // consumers of a job descriptor: the two issuers, the loader warp, the
     // P/dS warps and (fused dQ) the reducer warps
     for (int i = 0; i < kJD; ++i) {
       mbar_init(&sm.jd_full[i], 1);
-      mbar_init(&sm.jd_empty[i], 4 + kWG / 32 + (kDQ ? 8 : 0));
+      mbar_init(&sm.jd_empty[i], 3 + kWG / 32 + (kDQ ? 8 : 0));
     }
     fence_barrier_init();
   }
@@ -741,60 +742,60 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         mbar_arrive(&sm.jd_full[js]);
       }
     }
-  } else if (warp == 10 || warp == 12) {
+  } else if (warp == 10) {
     // ============================================================ TMA loads
-    // Two loader warps: warp 10 gathers K_e / V_e and the batches' Q rows,
-    // warp 12 their dO rows.  Each 16-head row is a 2 KB box and one thread
-    // issues about one box per 100 cycles, so lane j issues query j's boxes:
-    // the batch's copies leave together instead of one after another.
-    {
-      const bool is_q = warp == 10;
-      const CUtensorMap* map = is_q ? &tmq : &tmdo;
-      int job = 0, gb = 0;
-      bool ok = true;
-      while (ok) {
-        const int js = job % kJD;
-        if (!(ok = wtw(&sm.jd_full[js], (job / kJD) & 1, st, is_q ? 5 : 8))) break;
-        const JobDesc& d = sm.jd[js];
-        const int flags = d.flags;
-        if (flags & kSentinel) break;
-        const int hk = d.hk, n = d.n, krow = d.kv0 + d.e * 64, kb = d.b;
-        warp_arrive(&sm.jd_empty[js]);
-        if (is_q) {
-          if (lane == 0) {
-            ok = wt(&sm.kv_empty, (job & 1) ^ 1, st, 6);
-            if (ok) {
-              mbar_arrive_expect_tx(&sm.kv_full, 2u * 64u * D * 2u);
+    // One loader warp: lane 0 gathers K_e / V_e, lanes 0-7 the batch's Q rows
+    // (query = lane) and lanes 8-15 its dO rows (query = lane - 8).  Each
+    // 16-head row is a 2 KB box and one thread issues about one box per 100
+    // cycles, so the batch's 32 boxes leave from 16 lanes at once.
+    const bool is_q = lane < kQB;
+    const int qj = lane & (kQB - 1);
+    const CUtensorMap* map = is_q ? &tmq : &tmdo;
+    int job = 0, gb = 0;
+    bool ok = true;
+    while (ok) {
+      const int js = job % kJD;
+      if (!(ok = wtw(&sm.jd_full[js], (job / kJD) & 1, st, 5))) break;
+      const JobDesc& d = sm.jd[js];
+      const int flags = d.flags;
+      if (flags & kSentinel) break;
+      const int hk = d.hk, n = d.n, krow = d.kv0 + d.e * 64, kb = d.b;
+      warp_arrive(&sm.jd_empty[js]);
+      if (lane == 0) {
+        ok = wt(&sm.kv_empty, (job & 1) ^ 1, st, 6);
+        if (ok) {
+          mbar_arrive_expect_tx(&sm.kv_full, 2u * 64u * D * 2u);
 #pragma unroll
-              for (int cd = 0; cd < D / 64; ++cd) {
-                tma_load_4d(&sm.ke[cd * 64 * 128], &tmk, &sm.kv_full, cd * 64, hk, krow, kb);
-                tma_load_4d(&sm.ve[cd * 64 * 128], &tmv, &sm.kv_full, cd * 64, hk, krow, kb);
-              }
-            }
+          for (int cd = 0; cd < D / 64; ++cd) {
+            tma_load_4d(&sm.ke[cd * 64 * 128], &tmk, &sm.kv_full, cd * 64, hk, krow, kb);
+            tma_load_4d(&sm.ve[cd * 64 * 128], &tmv, &sm.kv_full, cd * 64, hk, krow, kb);
           }
-          if (!(ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0)) break;
         }
-        const int nb = (n + kQB - 1) / kQB;
-        for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
-          const int slot = gb % kMeta, s = gb & 1;
-          if (!(ok = wtw(&sm.meta_full[slot], (gb / kMeta) & 1, st, is_q ? 7 : 9))) break;
-          const BatchMeta& mt = sm.meta[slot];
-          const int m = mt.m;
-          const int tq = lane < kQB ? mt.tq[lane] : 0, bq = lane < kQB ? mt.b[lane] : 0;
-          warp_arrive(&sm.meta_empty[slot]);
-          if (!(ok = wtw(&sm.b_empty[s], ((gb >> 1) & 1) ^ 1, st, is_q ? 3 : 19))) break;
+      }
+      if (!(ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0)) break;
+      const int nb = (n + kQB - 1) / kQB;
+      for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
+        const int slot = gb % kMeta, s = gb & 1;
+        if (!(ok = wtw(&sm.meta_full[slot], (gb / kMeta) & 1, st, 7))) break;
+        const BatchMeta& mt = sm.meta[slot];
+        const int m = mt.m;
+        const int tq = mt.tq[qj], bq = mt.b[qj];
+        warp_arrive(&sm.meta_empty[slot]);
+        if (!(ok = wtw(&sm.b_empty[s], ((gb >> 1) & 1) ^ 1, st, 3))) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&sm.bq_full[s], (uint32_t)(m * G * D * 2));
+          mbar_arrive_expect_tx(&sm.bdo_full[s], (uint32_t)(m * G * D * 2));
+        }
+        __syncwarp();
+        if (lane < 2 * kQB && qj < m) {
           uint64_t* full = is_q ? &sm.bq_full[s] : &sm.bdo_full[s];
           uint8_t* buf = is_q ? sm.qb[s] : sm.dob[s];
-          if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(m * G * D * 2));
-          __syncwarp();
-          if (lane < m) {
 #pragma unroll
-            for (int cd = 0; cd < D / 64; ++cd)
-              tma_load_4d(buf + cd * 128 * 128 + lane * 16 * 128, map, full, cd * 64, hk * G, tq, bq);
-          }
+          for (int cd = 0; cd < D / 64; ++cd)
+            tma_load_4d(buf + cd * 128 * 128 + qj * 16 * 128, map, full, cd * 64, hk * G, tq, bq);
         }
-        ++job;
       }
+      ++job;
     }
   } else if (warp == 1) {
     // ============================================================ S/dP issuer
@@ -888,6 +889,10 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
             mma_bf16_ss(acc, od + (uint64_t)(kk * 128), pdsc + (uint64_t)(kk * 128), id_acc, accum);
             mma_bf16_ss(acc + 64, qd + (uint64_t)(kk * 128), dd + (uint64_t)(kk * 128), id_acc, accum);
           }
+          // the last readers of the batch's Q / dO rows (the S/dP MMAs retired
+          // before its P/dS were written): the slot goes back to the loader
+          // now, not after the dQ MMAs below
+          mma_commit(&sm.b_empty[s]);
           if (kDQ) {
             // the reducer warps have read the previous batch's partial out of TMEM
             if (!(ok = wt(&sm.dq_empty, (gb & 1) ^ 1, st, 19))) break;
@@ -897,9 +902,6 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
               mma_bf16_ss(tmem + kColDQ, kdq + (uint64_t)(kk * 128), ddq + (uint64_t)(kk * 2), id_dq, kk != 0);
             mma_commit(&sm.dq_full);
           }
-          // the S/dP MMAs of this batch retired before its P/dS were written, so
-          // this commit frees the batch buffers for both issuers
-          mma_commit(&sm.b_empty[s]);
           mma_commit(&sm.pds_empty);
         }
         if (!ok) break;
@@ -908,16 +910,16 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         ++job;
       }
     }
-  } else if (kDQ && warp >= 13) {
-    // ============================================================ fused-dQ reducers (warps 13-20)
+  } else if (kDQ && warp >= 12) {
+    // ============================================================ fused-dQ reducers (warps 12-19)
     // thread = dim (TMEM lane); per batch the dQ^T partial's 128 columns are
     // the batch's 8 queries x 16 heads, and each quadrant has two reducer
-    // warps: warps 13-16 take queries 0-3, warps 17-20 queries 4-7.  A warp
+    // warps: warps 12-15 take queries 0-3, warps 16-19 queries 4-7.  A warp
     // reads its 64 columns at once and releases the partial before issuing
     // its reductions, so the next batch's dQ MMAs need not wait for them; each
     // reduction adds 32 dims of one (query, head) row: coalesced 128 bytes.
     const int wq = warp & 3;
-    const int q0 = ((warp - 13) >> 2) * 4;   // first query of this warp's half
+    const int q0 = ((warp - 12) >> 2) * 4;   // first query of this warp's half
     const int dim = wq * 32 + lane;
     const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
     int job = 0, gb = 0;
