@@ -552,7 +552,10 @@ struct Smem {
   alignas(16) BatchMeta meta[kMeta];
   uint64_t bq_full[2], bdo_full[2], b_empty[2], kv_full, kv_empty;
   uint64_t meta_full[kMeta], meta_empty[kMeta];
-  uint64_t sdp_full[2], sdp_empty[2], pds_full, pds_empty;
+  // S and dP of a batch land separately (s_full, dp_full), and P and dS go
+  // back separately (p_full, ds_full): P's exponentials overlap the dP MMAs
+  // and the dV MMAs overlap the dS math
+  uint64_t s_full[2], dp_full[2], sdp_empty[2], p_full, p_empty, ds_full, ds_empty;
   uint64_t acc_full[2], acc_empty[2];
   uint64_t dq_full, dq_empty;         // fused dQ partial (TMEM) hand-off
   uint64_t jd_full[kJD], jd_empty[kJD];
@@ -607,7 +610,8 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
       mbar_init(&sm.bq_full[i], 1);
       mbar_init(&sm.bdo_full[i], 1);
       mbar_init(&sm.b_empty[i], 1);
-      mbar_init(&sm.sdp_full[i], 1);
+      mbar_init(&sm.s_full[i], 1);
+      mbar_init(&sm.dp_full[i], 1);
       mbar_init(&sm.sdp_empty[i], kWG / 32);
       mbar_init(&sm.acc_full[i], 1);
       mbar_init(&sm.acc_empty[i], kWG / 32);
@@ -619,8 +623,10 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
     }
     mbar_init(&sm.kv_full, 1);
     mbar_init(&sm.kv_empty, 1);
-    mbar_init(&sm.pds_full, kWG / 32);
-    mbar_init(&sm.pds_empty, 1);
+    mbar_init(&sm.p_full, kWG / 32);
+    mbar_init(&sm.p_empty, 1);
+    mbar_init(&sm.ds_full, kWG / 32);
+    mbar_init(&sm.ds_empty, 1);
     mbar_init(&sm.dq_full, 1);
     mbar_init(&sm.dq_empty, 8);   // the 8 reducer warps
     // consumers of a job descriptor: the two issuers, the loader warp, the
@@ -830,6 +836,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
             const uint64_t ko = (uint64_t)(((k >> 2) * (64 * 128) + (k & 3) * 32) >> 4);
             mma_bf16_ss(scol, qd + ro, kd + ko, id_sdp, k != 0);
           }
+          mma_commit(&sm.s_full[s]);
           if (!(ok = wt(&sm.bdo_full[s], (gb >> 1) & 1, st, 18))) break;
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
@@ -837,7 +844,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
             const uint64_t ko = (uint64_t)(((k >> 2) * (64 * 128) + (k & 3) * 32) >> 4);
             mma_bf16_ss(scol + 64, od + ro, vd + ko, id_sdp, k != 0);
           }
-          mma_commit(&sm.sdp_full[s]);
+          mma_commit(&sm.dp_full[s]);
         }
         if (!ok) break;
         // K_e / V_e are free once their last reader retires: these S/dP MMAs,
@@ -878,17 +885,26 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
         const uint32_t acc = tmem + kColAcc + ab * 128;
         for (int jb = 0; jb < nb && ok; ++jb, ++gb) {
           const int s = gb & 1;
-          if (!(ok = wt(&sm.pds_full, gb & 1, st, 10))) break;
-          tc_fence_after();
           const uint64_t od = smem_desc(smem_u32(&sm.dob[s][0]), lbo_rows, 1024, kSw128);
           const uint64_t qd = smem_desc(smem_u32(&sm.qb[s][0]), lbo_rows, 1024, kSw128);
-          // 16 rows per K-step: +2048 bytes = +128 in the start-address field
+          // dV^T += dOb^T . P as soon as P is in (16 rows per K-step: +2048
+          // bytes = +128 in the start-address field).  P is made from S
+          // alone, so p_full says nothing about the batch's dO rows: wait for
+          // their copy here (the slot cannot refill before this batch's dK
+          // MMAs retire, so the parity is unambiguous).
+          if (!(ok = wt(&sm.p_full, gb & 1, st, 10))) break;
+          if (!(ok = wt(&sm.bdo_full[s], (gb >> 1) & 1, st, 30))) break;
+          tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t accum = (jb == 0 && kk == 0) ? 0u : 1u;
-            mma_bf16_ss(acc, od + (uint64_t)(kk * 128), pdsc + (uint64_t)(kk * 128), id_acc, accum);
-            mma_bf16_ss(acc + 64, qd + (uint64_t)(kk * 128), dd + (uint64_t)(kk * 128), id_acc, accum);
-          }
+          for (int kk = 0; kk < 8; ++kk)
+            mma_bf16_ss(acc, od + (uint64_t)(kk * 128), pdsc + (uint64_t)(kk * 128), id_acc, (jb | kk) != 0);
+          mma_commit(&sm.p_empty);
+          // dK^T += Qb^T . dS
+          if (!(ok = wt(&sm.ds_full, gb & 1, st, 9))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_bf16_ss(acc + 64, qd + (uint64_t)(kk * 128), dd + (uint64_t)(kk * 128), id_acc, (jb | kk) != 0);
           // the last readers of the batch's Q / dO rows (the S/dP MMAs retired
           // before its P/dS were written): the slot goes back to the loader
           // now, not after the dQ MMAs below
@@ -902,7 +918,7 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
               mma_bf16_ss(tmem + kColDQ, kdq + (uint64_t)(kk * 128), ddq + (uint64_t)(kk * 2), id_dq, kk != 0);
             mma_commit(&sm.dq_full);
           }
-          mma_commit(&sm.pds_empty);
+          mma_commit(&sm.ds_empty);   // dS read by the dK (and dQ) MMAs
         }
         if (!ok) break;
         if (kDQ && nb > 0) mma_commit(&sm.kv_empty);   // the dQ MMAs read K_e
@@ -1003,41 +1019,56 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
           lse2 = __ldg(p.lse + qb_ * p.l_sb + (int64_t)qtq * p.l_st + (int64_t)hh * p.l_sh) * kLog2e;
           dl = __ldg(args.delta + (int64_t)qrow * p.h_q + hh);
         }
-        const bool rvalid = lse2 != -INFINITY;
-        // keys of this warpgroup valid for this row: key_base + i < lim
-        int lim = rvalid ? min(kv_len, p.causal ? pos + 1 : kv_len) - key_base : 0;
-        if (!(ok = wtw(&sm.sdp_full[s], (gb >> 1) & 1, st, 21))) break;
+        // S first: P = exp2(S*scale*log2e - lse2) goes out while dP is computed
+        if (!(ok = wtw(&sm.s_full[s], (gb >> 1) & 1, st, 21))) break;
         tc_fence_after();
-        float sv[32], dp[32];
         const uint32_t col = tl + kColSdP + s * 128 + wg * 32;
-        tmem_ld16(col, *reinterpret_cast<float(*)[16]>(&sv[0]));
-        tmem_ld16(col + 16, *reinterpret_cast<float(*)[16]>(&sv[16]));
+        float pv[32];
+        tmem_ld16(col, *reinterpret_cast<float(*)[16]>(&pv[0]));
+        tmem_ld16(col + 16, *reinterpret_cast<float(*)[16]>(&pv[16]));
+        tmem_ld_wait();
+        // keys of this warpgroup valid for this row: key_base + i < lim
+        const int lim = lse2 != -INFINITY ? min(kv_len, p.causal ? pos + 1 : kv_len) - key_base : 0;
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          pv[i] = i < lim ? ex2(pv[i] * c2 - lse2) : 0.f;
+          pv[i + 1] = i + 1 < lim ? ex2(pv[i + 1] * c2 - lse2) : 0.f;
+          pk[i / 2] = pack_bf16x2(pv[i], pv[i + 1]);
+        }
+        // row lrow: 64 keys = 8 chunks of 16 bytes, 128B swizzle (chunk ^= row & 7);
+        // this warpgroup writes chunks 4*wg .. 4*wg+3
+        const uint32_t prow = smem_u32(&sm.pbuf[0]) + lrow * 128;
+        const uint32_t drow = smem_u32(&sm.dsbuf[0]) + lrow * 128;
+        if (!(ok = wtw(&sm.p_empty, (gb & 1) ^ 1, st, 22))) break;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t off = (uint32_t)(((wg * 4 + c) ^ (lrow & 7)) * 16);
+          st_shared_v4(prow + off, pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
+        }
+        fence_proxy_async_smem();
+        warp_arrive(&sm.p_full);
+        // then dP: dS = P o (dP - delta)
+        if (!(ok = wtw(&sm.dp_full[s], (gb >> 1) & 1, st, 28))) break;
+        tc_fence_after();
+        float dp[32];
         tmem_ld16(col + 64, *reinterpret_cast<float(*)[16]>(&dp[0]));
         tmem_ld16(col + 80, *reinterpret_cast<float(*)[16]>(&dp[16]));
         tmem_ld_wait();
         tc_fence_before();
         warp_arrive(&sm.sdp_empty[s]);
-        uint32_t pk[16], dk[16];
+        uint32_t dk[16];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = i < lim ? ex2(sv[i] * c2 - lse2) : 0.f;
-          const float p1 = i + 1 < lim ? ex2(sv[i + 1] * c2 - lse2) : 0.f;
-          pk[i / 2] = pack_bf16x2(p0, p1);
-          dk[i / 2] = pack_bf16x2(p0 * (dp[i] - dl), p1 * (dp[i + 1] - dl));
-        }
-        if (!(ok = wtw(&sm.pds_empty, (gb & 1) ^ 1, st, 22))) break;
-        // row lrow: 64 keys = 8 chunks of 16 bytes, 128B swizzle (chunk ^= row & 7);
-        // this warpgroup writes chunks 4*wg .. 4*wg+3
-        const uint32_t prow = smem_u32(&sm.pbuf[0]) + lrow * 128;
-        const uint32_t drow = smem_u32(&sm.dsbuf[0]) + lrow * 128;
+        for (int i = 0; i < 32; i += 2)
+          dk[i / 2] = pack_bf16x2(pv[i] * (dp[i] - dl), pv[i + 1] * (dp[i + 1] - dl));
+        if (!(ok = wtw(&sm.ds_empty, (gb & 1) ^ 1, st, 29))) break;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const uint32_t off = (uint32_t)(((wg * 4 + c) ^ (lrow & 7)) * 16);
-          st_shared_v4(prow + off, pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
           st_shared_v4(drow + off, dk[c * 4], dk[c * 4 + 1], dk[c * 4 + 2], dk[c * 4 + 3]);
         }
         fence_proxy_async_smem();
-        warp_arrive(&sm.pds_full);
+        warp_arrive(&sm.ds_full);
       }
       if (!ok) break;
       // epilogue: thread = dim; this warpgroup's 32 keys of dV^T and dK^T

@@ -101,3 +101,34 @@ def test_atomic_and_inverted_dkdv_agree():
                dkv_mode="atomic")
     for n in ("dk", "dv"):
         assert (a[n].float() - b[n].float()).abs().max() < 2e-2 * max(1.0, float(b[n].float().abs().max()))
+
+
+def test_key_centric_dkdv_at_full_shape_is_reproducible_and_exact():
+    # The c2 geometry at B = 1: long query lists per block (the first blocks
+    # are selected by ~3000 queries) and enough batches in flight for the
+    # pass's hand-offs to race if one is missing.  dk/dv must be bitwise
+    # reproducible, and dv of the most-selected keys must match an fp32
+    # recomputation from the op's own lse.
+    cfg = W.scaled(W.CONFIGS["c2"], B=1)
+    dev = torch.device("cuda")
+    d = W.make_inputs(cfg, "cpu", 11)   # run_op copies to the device: separate leaves per run
+    a = run_op(d["q"], d["k"], d["v"], d["idx"], 64, None, None, True, d["do"], kernel="tcgen05",
+               dkv_mode="inverted", dq_mode="fused")
+    b = run_op(d["q"], d["k"], d["v"], d["idx"], 64, None, None, True, d["do"], kernel="tcgen05",
+               dkv_mode="inverted", dq_mode="fused")
+    assert torch.equal(a["dk"], b["dk"]) and torch.equal(a["dv"], b["dv"])
+    G = cfg.Hq // cfg.Hk
+    q, k, do, idx = (d[n][0].to(dev) for n in ("q", "k", "do", "idx"))
+    q, k, do = q.float(), k.float(), do.float()
+    lse = a["lse"][0].to(dev)
+    tq = torch.arange(cfg.T, device=dev)
+    for hk in (0, cfg.Hk - 1):
+        for key in (1, 2, 37, 63, 100):
+            sel = (idx[:, hk, :] == key // 64).any(-1) & (tq >= key)
+            qs = sel.nonzero().flatten()
+            heads = torch.arange(hk * G, (hk + 1) * G, device=dev)
+            s = (q[qs][:, heads] @ k[key, hk]) * cfg.scale
+            p = torch.exp(s - lse[qs][:, heads])
+            ref = (p[..., None] * do[qs][:, heads]).sum((0, 1)).cpu()
+            err = float((a["dv"][0, key, hk].float() - ref).abs().max())
+            assert err < 1e-2 * max(1.0, float(ref.abs().max())), (hk, key, qs.numel(), err)
