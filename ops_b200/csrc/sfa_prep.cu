@@ -70,42 +70,68 @@ preprocess_kernel(SfaParams p, float* __restrict__ delta, float* __restrict__ ds
 
 // The same delta with 16-byte loads: 16 lanes per (row, head), each lane 8
 // consecutive elements per step (d_v % 8 == 0, 16-byte aligned rows and
-// strides), two (row, head) pairs per warp.  The dsink partials follow as above.
+// strides), two (row, head) pairs per warp, and each half-warp loads four
+// pairs before reducing any (one pair's two loads per lane leave too little
+// in flight to cover the memory latency).  kDv = 64 / 128: one 16-byte chunk
+// per lane; kDv = 0: any multiple of 8.  The dsink partials follow as above.
+template <int kDv>
 __global__ void __launch_bounds__(kPreThreads)
 preprocess_vec_kernel(SfaParams p, float* __restrict__ delta, float* __restrict__ dsink_part) {
   extern __shared__ float sdelta[];  // [kPreRows][h_q]
+  constexpr int kU = 4;
   const int rows = num_rows(p);
   const int row0 = blockIdx.x * kPreRows;
   const int hw = threadIdx.x >> 4, l16 = threadIdx.x & 15;   // half-warp = one (row, head)
   const int nhw = kPreThreads / 16;
-  const int Dv = p.d_v;
-  for (int pr = hw; pr < kPreRows * p.h_q; pr += nhw) {
-    const int rl = pr / p.h_q, h = pr - rl * p.h_q;
-    const int row = row0 + rl;
-    float acc = 0.f;
-    if (row < rows) {
-      const Row r = row_info(p, row);
-      const uint4* o = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.o) + r.b * p.o_sb +
-                                                      r.tq * p.o_st + (int64_t)h * p.o_sh);
-      const uint4* dO = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.dout) +
-                                                       r.b * p.do_sb + r.tq * p.do_st + (int64_t)h * p.do_sh);
-      for (int c = l16; c < Dv / 8; c += 16) {
-        const uint4 a = __ldg(o + c), b = __ldg(dO + c);
-        const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+  const int Dv = kDv ? kDv : p.d_v;
+  const int total = kPreRows * p.h_q;   // a multiple of nhw: both half-warps of a warp loop alike
+  auto dot8 = [](const uint4& a, const uint4& b, float acc) {
+    const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&av[k]));
-          const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bv[k]));
-          acc = fmaf(x.x, y.x, acc);
-          acc = fmaf(x.y, y.y, acc);
+    for (int k = 0; k < 4; ++k) {
+      const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&av[k]));
+      const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bv[k]));
+      acc = fmaf(x.x, y.x, acc);
+      acc = fmaf(x.y, y.y, acc);
+    }
+    return acc;
+  };
+  for (int pr0 = hw; pr0 < total; pr0 += nhw * kU) {
+    float acc[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int pr = pr0 + u * nhw;
+      const int rl = pr / p.h_q, h = pr - rl * p.h_q;
+      const int row = row0 + rl;
+      acc[u] = 0.f;
+      if (pr < total && row < rows) {
+        const Row r = row_info(p, row);
+        const uint4* o = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.o) + r.b * p.o_sb +
+                                                        r.tq * p.o_st + (int64_t)h * p.o_sh);
+        const uint4* dO = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.dout) +
+                                                         r.b * p.do_sb + r.tq * p.do_st + (int64_t)h * p.do_sh);
+        if (kDv) {
+          if (l16 < kDv / 8) acc[u] = dot8(__ldg(o + l16), __ldg(dO + l16), 0.f);
+        } else {
+          for (int c = l16; c < Dv / 8; c += 16) acc[u] = dot8(__ldg(o + c), __ldg(dO + c), acc[u]);
         }
       }
     }
 #pragma unroll
-    for (int off = 8; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    for (int u = 0; u < kU; ++u) {
+#pragma unroll
+      for (int off = 8; off; off >>= 1) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], off);
+    }
     if (l16 == 0) {
-      if (row < rows) delta[(int64_t)row * p.h_q + h] = acc;
-      sdelta[pr] = acc;
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int pr = pr0 + u * nhw;
+        if (pr < total) {
+          const int rl = pr / p.h_q, h = pr - rl * p.h_q;
+          if (row0 + rl < rows) delta[(int64_t)(row0 + rl) * p.h_q + h] = acc[u];
+          sdelta[pr] = acc[u];
+        }
+      }
     }
   }
   __syncthreads();
@@ -150,9 +176,11 @@ cudaError_t launch_preprocess(const SfaParams& p, float* delta, float* dsink_par
                    reinterpret_cast<uintptr_t>(p.dout) % 16 == 0 && p.o_sb % 8 == 0 && p.o_st % 8 == 0 &&
                    p.o_sh % 8 == 0 && p.do_sb % 8 == 0 && p.do_st % 8 == 0 && p.do_sh % 8 == 0;
   if (vec) {
-    e = cudaFuncSetAttribute(preprocess_vec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    auto kern = p.d_v == 128 ? preprocess_vec_kernel<128> : p.d_v == 64 ? preprocess_vec_kernel<64>
+                                                                       : preprocess_vec_kernel<0>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    preprocess_vec_kernel<<<pre_ctas, kPreThreads, smem, st>>>(p, delta, part);
+    kern<<<pre_ctas, kPreThreads, smem, st>>>(p, delta, part);
   } else {
     preprocess_kernel<<<pre_ctas, kPreThreads, smem, st>>>(p, delta, part);
   }
