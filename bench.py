@@ -7,7 +7,11 @@ A step is one forward + backward of the sparse attention op over one batch of
 the configuration's synthetic inputs (default c2: B=4, T=8192, Hq=64, Hk=4,
 D=128, block_size=64, 16 selected blocks per (query, kv head)).  Under torchrun
 every rank processes its own batch of that shape (weak scaling: the global
-batch is 4*N; no collective on the data path — ranks share nothing).
+batch is 4*N; no collective on the data path — ranks share nothing).  With
+--split query (for configurations with fewer (batch, kv head) units than
+ranks, e.g. c3) the ranks instead split one batch's query rows, balanced by
+selected pairs (ops_b200/shard.py), and the step includes the one
+reduce-scatter that sums the dK/dV partials (strong scaling).
 
 value      selected-token TFLOP/s of the whole job (all ranks), inputs resident
            in HBM, timed with CUDA events per step (L2 flushed between steps),
@@ -203,11 +207,14 @@ def rank_seed(rank: int) -> int:
     return 1000 + rank
 
 
-def config_dict(cfg, n):
-    return {"workload": f"{cfg.name}: block-sparse GQA attention fwd+bwd, B={cfg.B}/rank, T={cfg.T}, "
+def config_dict(cfg, n, split=False):
+    per = "" if split else "/rank"
+    return {"workload": f"{cfg.name}: block-sparse GQA attention fwd+bwd, B={cfg.B}{per}, T={cfg.T}, "
                         f"Hq={cfg.Hq}, Hk={cfg.Hk}, Dqk={cfg.Dqk}, Dv={cfg.Dv}, block_size={cfg.bs}, "
                         f"S={cfg.S}, {cfg.mode} causal selection, q/k/v/dO ~ N(0,1)",
-            "global_batch": cfg.B * n, "seq_len": cfg.T, "parallelism": f"dp{n} (independent batch shards)",
+            "global_batch": cfg.B if split else cfg.B * n, "seq_len": cfg.T,
+            "parallelism": (f"{n} query-row ranges balanced by selected pairs, dK/dV summed by one "
+                            f"reduce-scatter" if split else f"dp{n} (independent batch shards)"),
             "l2": "flushed between timed steps (256 MiB memset)"}
 
 
@@ -234,15 +241,27 @@ def run_ours(args, cfg):
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     lib = _lib.load()
 
-    d = W.make_inputs(cfg, dev, seed=rank_seed(rank))
+    # --split query (strong scaling of one batch): every rank builds the same
+    # inputs and takes its range of query rows against the keys they can see;
+    # the dK/dV partials are summed by one reduce-scatter inside the step
+    split = args.split == "query" and world > 1
+    d = W.make_inputs(cfg, dev, seed=rank_seed(0 if split else rank))
     q, k, v, idx, do = d["q"], d["k"], d["v"], d["idx"], d["do"]
+    r0, r1, ke = 0, cfg.T, cfg.T
+    if split:
+        from ops_b200 import shard
+        ranges = shard.query_ranges(shard.row_work(idx, cfg.bs, cfg.T), world)
+        r0, r1 = ranges[rank]
+        ke = r1
+        q, idx, do = q[:, r0:r1], idx[:, r0:r1], do[:, r0:r1]
+        k, v = k[:, :ke], v[:, :ke]
     G = cfg.Hq // cfg.Hk
-    pairs = W.count_pairs(idx, cfg.bs, cfg.T, cfg.T) * G
+    pairs = W.count_pairs(idx, cfg.bs, r1 - r0, ke) * G
     fl = O.sfa_flops(pairs, cfg.Dqk, cfg.Dv)
     o = torch.empty(*q.shape[:-1], cfg.Dv, dtype=q.dtype, device=dev)
     lse = torch.empty(q.shape[:-1], dtype=torch.float32, device=dev)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    scfg = S._Cfg(cfg.bs, cfg.scale, True, False, cfg.T, cfg.T, _lib.SFA_DKV_AUTO, _lib.SFA_KERNEL_AUTO, False)
+    scfg = S._Cfg(cfg.bs, cfg.scale, True, False, r1 - r0, ke, _lib.SFA_DKV_AUTO, _lib.SFA_KERNEL_AUTO, False)
     P = S.build_params(q, k, v, idx, o, lse, scfg, None, None, None, do, dq, dk, dv, None)
     fam_f = lib.sfa_select_kernel(ctypes.byref(P), 0)
     fam_b = lib.sfa_select_kernel(ctypes.byref(P), 1)
@@ -255,7 +274,11 @@ def run_ours(args, cfg):
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
     Pp = ctypes.byref(P)
-    stages = ["fwd", "bwd_preprocess", "bwd_dq", "bwd_dkdv"]
+    stages = ["fwd", "bwd_preprocess", "bwd_dq", "bwd_dkdv"] + (["dkdv_reduce_scatter"] if split else [])
+    if split:
+        tc = (cfg.T + world - 1) // world
+        rs_in = torch.zeros(world * tc, cfg.B, cfg.Hk, cfg.Dqk + cfg.Dv, dtype=torch.float32, device=dev)
+        rs_out = torch.empty(tc, cfg.B, cfg.Hk, cfg.Dqk + cfg.Dv, dtype=torch.float32, device=dev)
 
     def step(ev=None):
         if ev:
@@ -272,6 +295,12 @@ def run_ours(args, cfg):
         _lib.check(lib.sfa_bwd_dkdv(Pp, ws.data_ptr(), nbytes, sptr), "dkdv")
         if ev:
             ev[4].record(stream)
+        if split:
+            rs_in[:ke, ..., :cfg.Dqk].copy_(dk.transpose(0, 1))
+            rs_in[:ke, ..., cfg.Dqk:].copy_(dv.transpose(0, 1))
+            dist.reduce_scatter_tensor(rs_out, rs_in)
+            if ev:
+                ev[5].record(stream)
 
     for _ in range(args.warmup):
         step()
@@ -284,7 +313,8 @@ def run_ours(args, cfg):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    nev = len(stages) + 1
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nev)] for _ in range(args.steps)]
     n0 = lib.sfa_kernel_launches()
     t_wall0 = time.time()
     for i in range(args.steps):
@@ -297,16 +327,34 @@ def run_ours(args, cfg):
         dist.barrier()
     stage_ms = {s: sum(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps)) / args.steps
                 for j, s in enumerate(stages)}
-    step_ms = sum(evs[i][0].elapsed_time(evs[i][4]) for i in range(args.steps)) / args.steps
+    step_ms = sum(evs[i][0].elapsed_time(evs[i][nev - 1]) for i in range(args.steps)) / args.steps
 
     # e2e through the public API, host buffers
     host = {n: t.cpu().pin_memory() for n, t in (("q", q), ("k", k), ("v", v), ("idx", idx), ("do", do))}
     outs = {n: torch.empty(tuple(t.shape), dtype=t.dtype, pin_memory=True) for n, t in
             (("o", o), ("dq", q), ("dk", k), ("dv", v))}
+    if split:   # a rank gets back its rows and its key share of dk / dv
+        k0, k1 = shard.key_share(cfg.T, world, rank)
+        outs["dk"] = torch.empty((cfg.B, k1 - k0, cfg.Hk, cfg.Dqk), dtype=k.dtype, pin_memory=True)
+        outs["dv"] = torch.empty((cfg.B, k1 - k0, cfg.Hk, cfg.Dv), dtype=v.dtype, pin_memory=True)
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = sum(t.numel() * t.element_size() for t in outs.values())
 
+    def e2e_split_step():
+        qd = host["q"].to(dev, non_blocking=True)
+        kd = host["k"].to(dev, non_blocking=True)
+        vd = host["v"].to(dev, non_blocking=True)
+        ixd = host["idx"].to(dev, non_blocking=True)
+        dod = host["do"].to(dev, non_blocking=True)
+        r = shard.local_step(qd, kd, vd, ixd, dod, (r0, r1), cfg.T, rank, world, cfg.bs, cfg.scale)
+        outs["o"].copy_(r["o"], non_blocking=True)
+        outs["dq"].copy_(r["dq"], non_blocking=True)
+        outs["dk"].copy_(r["dk"], non_blocking=True)
+        outs["dv"].copy_(r["dv"], non_blocking=True)
+
     def e2e_step():
+        if split:
+            return e2e_split_step()
         qd = host["q"].to(dev, non_blocking=True).requires_grad_()
         kd = host["k"].to(dev, non_blocking=True).requires_grad_()
         vd = host["v"].to(dev, non_blocking=True).requires_grad_()
@@ -354,7 +402,8 @@ def run_ours(args, cfg):
                    "bwd_preprocess": 0.0,
                    "bwd_dq": 0.0 if fused_dq else (two_p * (2 * cfg.Dqk + cfg.Dv) if tc_bwd else fl.bwd),
                    "bwd_dkdv": (two_p * (2 * cfg.Dqk + cfg.Dv) if fused_dq else two_p * (cfg.Dqk + cfg.Dv))
-                   if tc_bwd else 0.0}
+                   if tc_bwd else 0.0,
+                   "dkdv_reduce_scatter": 0.0}
     dom = max(stages, key=lambda s: stage_ms[s])
     # K and V rows gathered per (row, kv head): selected keys x (Dqk + Dv) bf16
     kv_gather = pairs / G * (cfg.Dqk + cfg.Dv) * 2.0
@@ -369,10 +418,11 @@ def run_ours(args, cfg):
     fams = {1: "tcgen05", 2: "general"}
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": step_ms_max, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config_dict(cfg, world),
+        "warmup": args.warmup, "ms_per_step": step_ms_max, "higher_is_better": True,
+        "scaling": "strong" if split else "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config_dict(cfg, world, split),
         "pct_bf16_peak": 100.0 * value / world / peak,
-        "tokens_per_s": cfg.B * cfg.T * world / (step_ms_max * 1e-3),
+        "tokens_per_s": cfg.B * cfg.T * (1 if split else world) / (step_ms_max * 1e-3),
         "selected_pairs_per_rank": pairs,
         "stages_ms": stage_ms,
         "kernel_family": {"fwd": fams.get(fam_f, str(fam_f)), "bwd": fams.get(fam_b, str(fam_b)),
@@ -523,6 +573,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--batch", type=int, default=0, help="override the per-rank batch (profiling runs)")
     ap.add_argument("--seq", type=int, default=0, help="override the sequence length (scaled secondary configs)")
+    ap.add_argument("--split", choices=["none", "query"], default="none",
+                    help="with N > 1: 'query' splits one batch's query rows over the ranks (strong scaling, "
+                         "for configurations with fewer (batch, kv head) units than ranks)")
     args = ap.parse_args()
     from ops_b200 import workloads as W
     cfg = W.CONFIGS[args.config]

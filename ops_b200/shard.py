@@ -1,0 +1,136 @@
+"""Query-range sharding of one long sequence across ranks (strong scaling).
+
+Independent (sequence, kv head) units need no coordination at all: a rank
+takes whole units or whole batches.  A configuration with fewer units than
+ranks (one 65536-token sequence with 4 kv heads, or a single-unit MLA shape)
+splits its query rows instead.  Rank r takes rows ``[r0, r1)`` of every
+sequence in the batch and attends to keys ``[0, r1 + (Tk - T))``: with the
+bottom-right causal alignment the op uses (``pos(t) = t + kv_len - q_len``),
+``q_len = r1 - r0`` and ``kv_len = r1 + Tk - T`` give every row the position it
+has in the full problem, and no key past that range is visible to those rows.
+The forward outputs and dq of those rows stay on the rank.  dK / dV receive
+contributions from every rank's rows: each rank's fp32 partial (zero past its
+key range) is summed with one reduce-scatter over the key axis, after which
+rank r holds dk / dv of its own equal key share — the one exchange step of the
+path, so the one collective.
+
+The row ranges balance the exact work: valid (query, kv head, key) triples per
+query row, counted from the indices with the op's own validity rules.
+"""
+from __future__ import annotations
+
+import math
+from typing import Callable, List, Optional, Tuple
+
+import torch
+
+
+def row_work(block_indices: torch.Tensor, block_size: int, kv_len: int, causal: bool = True) -> torch.Tensor:
+    """Valid (kv head, key) pairs of each query row, summed over the batch.
+
+    ``block_indices [B, T, Hk, S]``; an entry ``e`` is valid iff
+    ``0 <= e < ceil(kv_len / block_size)``; block ``e`` holds keys
+    ``e*block_size + j < kv_len`` and, when causal, ``<= pos(t)``."""
+    B, T, Hk, S = block_indices.shape
+    e = block_indices.to(torch.int64)
+    nblk = (kv_len + block_size - 1) // block_size
+    pos = torch.arange(T, device=e.device) + (kv_len - T)
+    first = e * block_size
+    end = torch.clamp(first + block_size, max=kv_len)
+    if causal:
+        end = torch.minimum(end, pos[None, :, None, None] + 1)
+    n = torch.clamp(end - first, min=0)
+    n = torch.where((e >= 0) & (e < nblk), n, torch.zeros_like(n))
+    return n.sum(dim=(0, 2, 3))
+
+
+def query_ranges(work: torch.Tensor, world: int) -> List[Tuple[int, int]]:
+    """Contiguous row ranges of (nearly) equal total work, one per rank.
+
+    Cut r (r = 1 .. world-1) is the first row whose work prefix reaches
+    r / world of the total; rows of zero work go with their neighbours."""
+    T = int(work.numel())
+    csum = torch.cumsum(work.to(torch.float64).cpu(), 0)
+    total = float(csum[-1]) if T else 0.0
+    cuts = [0]
+    for r in range(1, world):
+        target = total * r / world
+        c = int(torch.searchsorted(csum, torch.tensor([target], dtype=torch.float64)).item()) + 1 if total else 0
+        cuts.append(min(max(c, cuts[-1]), T))
+    cuts.append(T)
+    return [(cuts[r], cuts[r + 1]) for r in range(world)]
+
+
+def key_share(kv_len: int, world: int, rank: int) -> Tuple[int, int]:
+    """Keys [k0, k1) whose dk / dv rank ``rank`` holds after the reduce-scatter."""
+    tc = (kv_len + world - 1) // world
+    return min(rank * tc, kv_len), min((rank + 1) * tc, kv_len)
+
+
+def op_fwd_bwd(q, k, v, idx, do, block_size, scale, causal):
+    """The single-device step on the CUDA op: (o, lse, dq, dk, dv)."""
+    from .sfa import sparse_flash_attention
+    qg = q.detach().requires_grad_(True)
+    kg = k.detach().requires_grad_(True)
+    vg = v.detach().requires_grad_(True)
+    o, lse = sparse_flash_attention(qg, kg, vg, idx, block_size, scale, causal=causal)
+    o.backward(do)
+    return o.detach(), lse, qg.grad, kg.grad, vg.grad
+
+
+def shard_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_indices: torch.Tensor, do: torch.Tensor,
+               rank: int, world: int, ranges: List[Tuple[int, int]], block_size: int = 64,
+               scale: Optional[float] = None, causal: bool = True, group=None,
+               fwd_bwd: Callable = op_fwd_bwd) -> dict:
+    """Forward + backward of this rank's query rows of a dense batch.
+
+    ``q [B,T,Hq,Dqk]``, ``k [B,Tk,Hk,Dqk]``, ``v [B,Tk,Hk,Dv]`` (every rank holds
+    the inputs), ``ranges`` from :func:`query_ranges`.  Slices this rank's rows
+    and visible keys and runs :func:`local_step` on them."""
+    T, Tk = q.shape[1], k.shape[1]
+    r0, r1 = ranges[rank]
+    ke = r1 + (Tk - T) if r1 > r0 else 0            # keys visible to rows < r1
+    return local_step(q[:, r0:r1], k[:, :ke], v[:, :ke], block_indices[:, r0:r1], do[:, r0:r1], (r0, r1), Tk,
+                      rank, world, block_size, scale, causal, group, fwd_bwd)
+
+
+def local_step(q_rows: torch.Tensor, k_pre: torch.Tensor, v_pre: torch.Tensor, idx_rows: torch.Tensor,
+               do_rows: torch.Tensor, rows: Tuple[int, int], kv_len: int, rank: int, world: int,
+               block_size: int = 64, scale: Optional[float] = None, causal: bool = True, group=None,
+               fwd_bwd: Callable = op_fwd_bwd) -> dict:
+    """The same step from this rank's own slices: rows ``[r0, r1)`` of q /
+    indices / dO and the first ``r1 + kv_len - T`` keys of k / v.  Returns the
+    rows with their ``o``, ``lse`` and ``dq``, and this rank's key share
+    ``(k0, k1)`` of ``[0, kv_len)`` with the summed ``dk``, ``dv`` (fp32 sums, in
+    k's dtype).  ``fwd_bwd(q, k, v, idx, do, block_size, scale, causal)`` is the
+    single-device step (the CUDA op by default)."""
+    import torch.distributed as dist
+    B, _, _, Dqk = q_rows.shape
+    Hk, Dv = k_pre.shape[2], v_pre.shape[3]
+    dev = q_rows.device
+    if scale is None:
+        scale = 1.0 / math.sqrt(Dqk)
+    r0, r1 = rows
+    ke = k_pre.shape[1]
+    o = lse = dq = None
+    if r1 > r0:
+        o, lse, dq, dk, dv = fwd_bwd(q_rows, k_pre, v_pre, idx_rows, do_rows, block_size, scale, causal)
+    else:                                            # no rows here: nothing to add
+        ke = 0
+    # fp32 partials on the key axis (keys major), padded to world equal shares;
+    # dk and dv travel in one buffer
+    tc = (kv_len + world - 1) // world
+    buf = torch.zeros(world * tc, B, Hk, Dqk + Dv, dtype=torch.float32, device=dev)
+    if ke > 0:
+        buf[:ke, ..., :Dqk] = dk.float().transpose(0, 1)
+        buf[:ke, ..., Dqk:] = dv.float().transpose(0, 1)
+    mine = torch.empty(tc, B, Hk, Dqk + Dv, dtype=torch.float32, device=dev)
+    if world > 1:
+        dist.reduce_scatter_tensor(mine, buf, group=group)
+    else:
+        mine.copy_(buf)
+    k0, k1 = key_share(kv_len, world, rank)
+    n = k1 - k0
+    dk_own = mine[:n, ..., :Dqk].transpose(0, 1).to(k_pre.dtype).contiguous()
+    dv_own = mine[:n, ..., Dqk:].transpose(0, 1).to(v_pre.dtype).contiguous()
+    return dict(rows=(r0, r1), o=o, lse=lse, dq=dq, keys=(k0, k1), dk=dk_own, dv=dv_own)

@@ -1,0 +1,89 @@
+"""Query-range sharding (ops_b200.shard) on CPU ranks: gloo, world size 2 and 3.
+
+Each rank runs the CPU restatement on its rows (the CUDA op needs a GPU), and
+the reduce-scatter of the dK/dV partials is the same call the GPU ranks make.
+The assembled rows and key shares must equal the single-process result."""
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import sfa_oracle as O
+from ops_b200 import shard
+from ops_b200 import workloads as W
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _oracle_fwd_bwd(q, k, v, idx, do, bs, scale, causal):
+    o, lse = O.sfa_forward(q.float(), k.float(), v.float(), idx, bs, scale, None, causal)
+    dq, dk, dv, _ = O.sfa_backward(q.float(), k.float(), v.float(), idx, o, lse, do.float(), bs, scale, None, causal)
+    return o, lse, dq, dk, dv
+
+
+def _case():
+    cfg = W.scaled(W.CONFIGS["c3"], B=1, T=384, Hq=8, Hk=2, Dqk=32, Dv=32, bs=16, S=6)
+    d = W.make_inputs(cfg, "cpu", 5, dtype=torch.float32)
+    return cfg, d
+
+
+def _worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    cfg, d = _case()
+    work = shard.row_work(d["idx"], cfg.bs, cfg.T)
+    ranges = shard.query_ranges(work, world)
+    r = shard.shard_step(d["q"], d["k"], d["v"], d["idx"], d["do"], rank, world, ranges, block_size=cfg.bs,
+                         fwd_bwd=_oracle_fwd_bwd)
+    rec = {key: (val.clone() if torch.is_tensor(val) else val) for key, val in r.items()}
+    rec["work"] = [int(work[a:b].sum()) for a, b in ranges]
+    out[rank] = rec
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_query_range_shards_assemble_to_the_full_result(world):
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_worker, args=(world, _free_port(), out), nprocs=world, join=True)
+    cfg, d = _case()
+    o, lse, dq, dk, dv = _oracle_fwd_bwd(d["q"], d["k"], d["v"], d["idx"], d["do"], cfg.bs, None, True)
+    rows, keys = [], []
+    for r in range(world):
+        res = out[r]
+        r0, r1 = res["rows"]
+        rows.append((r0, r1))
+        if r1 > r0:
+            assert torch.allclose(res["o"], o[:, r0:r1], atol=1e-5, rtol=1e-5)
+            assert torch.allclose(res["lse"], lse[:, r0:r1], atol=1e-5, rtol=1e-5)
+            assert torch.allclose(res["dq"], dq[:, r0:r1], atol=1e-5, rtol=1e-5)
+        k0, k1 = res["keys"]
+        keys.append((k0, k1))
+        assert torch.allclose(res["dk"], dk[:, k0:k1], atol=1e-4, rtol=1e-4)
+        assert torch.allclose(res["dv"], dv[:, k0:k1], atol=1e-4, rtol=1e-4)
+    # the ranges tile the rows and the key shares tile the keys
+    assert rows[0][0] == 0 and rows[-1][1] == cfg.T and all(rows[i][1] == rows[i + 1][0] for i in range(world - 1))
+    assert keys[0][0] == 0 and keys[-1][1] == cfg.T and all(keys[i][1] == keys[i + 1][0] for i in range(world - 1))
+    # balanced: no rank carries more than its share plus one row's work
+    work = out[0]["work"]
+    assert max(work) - sum(work) / world <= int(shard.row_work(d["idx"], cfg.bs, cfg.T).max())
+
+
+def test_query_ranges_balance_and_edge_cases():
+    w = torch.tensor([0, 0, 5, 5, 5, 5, 0, 0, 10, 0], dtype=torch.int64)
+    rg = shard.query_ranges(w, 2)
+    assert rg[0][0] == 0 and rg[-1][1] == 10 and rg[0][1] == rg[1][0]
+    assert abs(int(w[rg[0][0]:rg[0][1]].sum()) - 15) <= 10
+    assert shard.query_ranges(torch.zeros(4, dtype=torch.int64), 3)[-1] == (0, 4)
+    assert shard.query_ranges(w, 1) == [(0, 10)]
+    assert [shard.key_share(10, 3, r) for r in range(3)] == [(0, 4), (4, 8), (8, 10)]
