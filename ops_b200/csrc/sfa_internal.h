@@ -43,7 +43,8 @@ struct BwdLayout {
   bool fused_dq;
 };
 
-constexpr int kPreRows = 16;  // query rows per preprocess CTA
+constexpr int kPreRows = 16;  // query rows per preprocess CTA (x h_q must stay a multiple of 16: the
+                              // delta kernel's half-warps loop in step)
 
 BwdLayout bwd_layout(const SfaParams& p, int kernel_family, int dkv_mode, int dq_mode);
 

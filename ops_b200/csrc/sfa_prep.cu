@@ -74,6 +74,8 @@ preprocess_kernel(SfaParams p, float* __restrict__ delta, float* __restrict__ ds
 // pairs before reducing any (one pair's two loads per lane leave too little
 // in flight to cover the memory latency).  kDv = 64 / 128: one 16-byte chunk
 // per lane; kDv = 0: any multiple of 8.  The dsink partials follow as above.
+static_assert(kPreRows % (kPreThreads / 16) == 0, "a CTA's (row, head) pairs must split evenly over its half-warps");
+
 template <int kDv>
 __global__ void __launch_bounds__(kPreThreads)
 preprocess_vec_kernel(SfaParams p, float* __restrict__ delta, float* __restrict__ dsink_part) {
