@@ -49,9 +49,9 @@ METRIC = "SFA fwd+bwd TFLOP/s (selected tokens) & % bf16 tensor peak, 1/2/4/8 B2
 # (the kernel summaries kept with the profiles), scaled x4 to the bench's B=4
 # launch: each unit's q/dO/o/dq rows are read or written once and its K/V stay
 # in L2.
-NCU_TRAFFIC = {"c2": {"fwd": 4 * (0.153959e9 + 0.101943e9),
+NCU_TRAFFIC = {"c2": {"fwd": 4 * (0.153979e9 + 0.102984e9),
                       "bwd_dq": 4 * (0.296924e9 + 0.112170e9),        # SFA_DQ_SEPARATE
-                      "bwd_dkdv": 4 * (1.259915e9 + 0.725504e9)}}     # with the fused dQ
+                      "bwd_dkdv": 4 * (1.294898e9 + 0.735617e9)}}     # with the fused dQ
 FALLBACK_BF16_TFLOPS = 1590.0
 
 
