@@ -202,6 +202,14 @@ int sfa_inverted_index_layout(const SfaParams* p, size_t* offsets_off, size_t* e
 int sfa_device_status(void* stream, int32_t* status);
 int sfa_reset_device_status(void* stream);
 
+/* Self-test of that failure path: one warp waits, with a limit of limit_us
+ * (1 .. 1e6), on an mbarrier nothing ever arrives on, through the same bounded
+ * wait the kernels use.  The wait runs out and the status word receives
+ * SFA_SELFTEST_STATUS (unless an earlier code is still there); the kernel
+ * returns and the context stays usable.  Stream-ordered. */
+#define SFA_SELFTEST_STATUS ((15 << 16) | 1)
+int sfa_selftest_wait_timeout(void* stream, uint32_t limit_us);
+
 #ifdef __cplusplus
 }
 #endif

@@ -22,6 +22,7 @@ SFA_ERR_DEVICE_TIMEOUT = -5
 SFA_DKV_AUTO, SFA_DKV_INVERTED, SFA_DKV_ATOMIC = 0, 1, 2
 SFA_KERNEL_AUTO, SFA_KERNEL_TCGEN05, SFA_KERNEL_GENERAL = 0, 1, 2
 SFA_DQ_AUTO, SFA_DQ_SEPARATE, SFA_DQ_FUSED = 0, 1, 2
+SFA_SELFTEST_STATUS = (15 << 16) | 1   # status code of sfa_selftest_wait_timeout
 
 _c_void_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -65,6 +66,7 @@ EXPORTS = {
                                    ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(_i32),
                                    ctypes.POINTER(_i32)], _i32),
     "sfa_device_status": ([_c_void_p, ctypes.POINTER(_i32)], _i32),
+    "sfa_selftest_wait_timeout": ([_c_void_p, ctypes.c_uint32], _i32),
     "sfa_reset_device_status": ([_c_void_p], _i32),
 }
 

@@ -412,6 +412,15 @@ int sfa_device_status(void* stream, int32_t* status) {
   return SFA_OK;
 }
 
+int sfa_selftest_wait_timeout(void* stream, uint32_t limit_us) {
+  int32_t* ptr = device_status_ptr();
+  if (!ptr) return fail(SFA_ERR_CUDA, "device status word unavailable");
+  if (limit_us == 0 || limit_us > 1000000u) return fail(SFA_ERR_INVALID_ARGUMENT, "limit_us must be in [1, 1000000]");
+  cudaError_t e = launch_wait_probe(limit_us, ptr, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sfa_selftest_wait_timeout");
+  return SFA_OK;
+}
+
 int sfa_reset_device_status(void* stream) {
   int32_t* ptr = device_status_ptr();
   if (!ptr) return fail(SFA_ERR_CUDA, "device status word unavailable");

@@ -62,6 +62,8 @@ cudaError_t launch_convert_dkdv(const SfaParams& p, const float* dk_acc, const f
 // dk/dv from the row-range partials of the key-centric pass, summed in range order
 cudaError_t launch_reduce_dkdv_ranges(const SfaParams& p, const BwdLayout& L, const char* ws, cudaStream_t st);
 // dq = bf16(scale * dq_acc), dq_acc fp32 [rows][h_q][d_qk]
+// one warp waits, with a limit of limit_us, on an mbarrier nothing arrives on (sfa_selftest.cu)
+cudaError_t launch_wait_probe(uint32_t limit_us, int32_t* status, cudaStream_t st);
 cudaError_t launch_convert_dq(const SfaParams& p, const float* dq_acc, cudaStream_t st);
 
 // inverted block->query index

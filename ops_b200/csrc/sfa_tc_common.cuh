@@ -84,12 +84,13 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 // Wait for the phase with the given parity; gives up after ~2 s (returns false).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
+  const uint32_t hint = limit_ns < 1000000ull ? (uint32_t)limit_ns : 1000000u;
   while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
-    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+    if (mbar_try_wait_sleep(bar, parity, hint)) return true;
+    if (global_timer_ns() - t0 > limit_ns) return false;
   }
 }
 
