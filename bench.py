@@ -261,7 +261,8 @@ def run_ours(args, cfg):
     o = torch.empty(*q.shape[:-1], cfg.Dv, dtype=q.dtype, device=dev)
     lse = torch.empty(q.shape[:-1], dtype=torch.float32, device=dev)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    scfg = S._Cfg(cfg.bs, cfg.scale, True, False, r1 - r0, ke, _lib.SFA_DKV_AUTO, _lib.SFA_KERNEL_AUTO, False)
+    scfg = S._Cfg(cfg.bs, cfg.scale, True, False, r1 - r0, ke, _lib.SFA_DKV_AUTO, _lib.SFA_KERNEL_AUTO, False,
+                  S._DQ[args.dq_mode])
     P = S.build_params(q, k, v, idx, o, lse, scfg, None, None, None, do, dq, dk, dv, None)
     fam_f = lib.sfa_select_kernel(ctypes.byref(P), 0)
     fam_b = lib.sfa_select_kernel(ctypes.byref(P), 1)
@@ -360,7 +361,7 @@ def run_ours(args, cfg):
         vd = host["v"].to(dev, non_blocking=True).requires_grad_()
         ixd = host["idx"].to(dev, non_blocking=True)
         dod = host["do"].to(dev, non_blocking=True)
-        oo, _ = ops_b200.sparse_flash_attention(qd, kd, vd, ixd, cfg.bs)
+        oo, _ = ops_b200.sparse_flash_attention(qd, kd, vd, ixd, cfg.bs, dq_mode=args.dq_mode)
         oo.backward(dod)
         outs["o"].copy_(oo.detach(), non_blocking=True)
         outs["dq"].copy_(qd.grad, non_blocking=True)
@@ -573,6 +574,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--batch", type=int, default=0, help="override the per-rank batch (profiling runs)")
     ap.add_argument("--seq", type=int, default=0, help="override the sequence length (scaled secondary configs)")
+    ap.add_argument("--dq-mode", choices=["auto", "separate", "fused"], default="auto",
+                    help="backward dQ plan (profiling runs): its own query-centric pass or fused into dK/dV")
     ap.add_argument("--split", choices=["none", "query"], default="none",
                     help="with N > 1: 'query' splits one batch's query rows over the ranks (strong scaling, "
                          "for configurations with fewer (batch, kv head) units than ranks)")
