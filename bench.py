@@ -387,6 +387,10 @@ def run_ours(args, cfg):
     sampler.stop()
     clocks = sampler.summary(t_wall0, t_wall1)
 
+    per_rank = [stage_ms]
+    if world > 1:   # every rank's stage times (load balance of a split)
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, {k: round(v, 4) for k, v in stage_ms.items()})
     step_ms_max, e_ms_max, flops_all = reduce_over_ranks(step_ms, e_ms, fl.total, dev)
     if world > 1:
         dist.destroy_process_group()
@@ -426,6 +430,7 @@ def run_ours(args, cfg):
         "tokens_per_s": cfg.B * cfg.T * (1 if split else world) / (step_ms_max * 1e-3),
         "selected_pairs_per_rank": pairs,
         "stages_ms": stage_ms,
+        **({"stages_ms_per_rank": per_rank} if world > 1 else {}),
         "kernel_family": {"fwd": fams.get(fam_f, str(fam_f)), "bwd": fams.get(fam_b, str(fam_b)),
                           "dkv": {1: "inverted", 2: "atomic"}.get(dkv_mode.value),
                           "dq": {1: "separate", 2: "fused"}.get(dq_mode.value)},
