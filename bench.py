@@ -250,7 +250,9 @@ def run_ours(args, cfg):
     r0, r1, ke = 0, cfg.T, cfg.T
     if split:
         from ops_b200 import shard
-        ranges = shard.query_ranges(shard.row_work(idx, cfg.bs, cfg.T), world)
+        work = (shard.row_cost(idx, cfg.bs, cfg.T) if args.balance == "cost"
+                else shard.row_work(idx, cfg.bs, cfg.T))
+        ranges = shard.query_ranges(work, world)
         r0, r1 = ranges[rank]
         ke = r1
         q, idx, do = q[:, r0:r1], idx[:, r0:r1], do[:, r0:r1]
@@ -581,6 +583,9 @@ def main():
     ap.add_argument("--seq", type=int, default=0, help="override the sequence length (scaled secondary configs)")
     ap.add_argument("--dq-mode", choices=["auto", "separate", "fused"], default="auto",
                     help="backward dQ plan (profiling runs): its own query-centric pass or fused into dK/dV")
+    ap.add_argument("--balance", choices=["pairs", "cost"], default="pairs",
+                    help="--split query: balance rows by selected pairs, or by a cost that also counts the "
+                         "dK/dV pass's jobs and batches (ops_b200/shard.py row_cost)")
     ap.add_argument("--split", choices=["none", "query"], default="none",
                     help="with N > 1: 'query' splits one batch's query rows over the ranks (strong scaling, "
                          "for configurations with fewer (batch, kv head) units than ranks)")

@@ -44,6 +44,44 @@ def row_work(block_indices: torch.Tensor, block_size: int, kv_len: int, causal: 
     return n.sum(dim=(0, 2, 3))
 
 
+def row_cost(block_indices: torch.Tensor, block_size: int, kv_len: int, causal: bool = True,
+             range_rows: int = 2048, batch_rows: int = 8, per_pair: float = 3.59e-8,
+             per_batch: float = 1.62e-5, per_job: float = 3.67e-5) -> torch.Tensor:
+    """A per-row cost (ms) that also counts the key-centric dK/dV pass's units.
+
+    Pairs alone balance the forward, but the dK/dV pass works in jobs (one per
+    row range of ``range_rows``, kv head and block with at least one query) of
+    batches of ``batch_rows`` queries, and a job costs its change-over on top
+    of its batches.  Rows whose selections spread over more blocks make more,
+    thinner jobs.  Each valid (row, kv head, block) entry carries 1/n of its
+    job and ceil(n / batch_rows)/n of its batches (n = the job's queries).  The
+    default weights are B200 times at D = 128 (ms per pair of the forward, per
+    batch and per job of the pass), fitted to the two ranks of a measured
+    two-GPU split.  Returns float64 per row."""
+    B, T, Hk, S = block_indices.shape
+    e = block_indices.to(torch.int64)
+    nblk = (kv_len + block_size - 1) // block_size
+    pos = torch.arange(T, device=e.device) + (kv_len - T)
+    first = e * block_size
+    end = torch.clamp(first + block_size, max=kv_len)
+    if causal:
+        end = torch.minimum(end, pos[None, :, None, None] + 1)
+    n = torch.clamp(end - first, min=0)
+    valid = (e >= 0) & (e < nblk) & (n > 0)
+    pairs = torch.where(valid, n, torch.zeros_like(n)).sum(dim=(0, 2, 3)).to(torch.float64)
+    # job id of every entry: (batch, kv head, row range, block)
+    rr = (torch.arange(T, device=e.device) // range_rows)[None, :, None, None]
+    nr = (T + range_rows - 1) // range_rows
+    bb = torch.arange(B, device=e.device)[:, None, None, None]
+    hh = torch.arange(Hk, device=e.device)[None, None, :, None]
+    jid = ((bb * Hk + hh) * nr + rr) * max(nblk, 1) + torch.clamp(e, 0, max(nblk - 1, 0))
+    counts = torch.bincount(jid[valid], minlength=B * Hk * nr * max(nblk, 1)).to(torch.float64)
+    per_entry = torch.where(counts > 0, (per_job + per_batch * torch.ceil(counts / batch_rows)) / counts.clamp(min=1),
+                            torch.zeros_like(counts))
+    ent = torch.where(valid, per_entry[jid.clamp(min=0)], torch.zeros(jid.shape, dtype=torch.float64, device=e.device))
+    return per_pair * pairs + ent.sum(dim=(0, 2, 3))
+
+
 def query_ranges(work: torch.Tensor, world: int) -> List[Tuple[int, int]]:
     """Contiguous row ranges of (nearly) equal total work, one per rank.
 

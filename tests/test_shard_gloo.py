@@ -87,3 +87,26 @@ def test_query_ranges_balance_and_edge_cases():
     assert shard.query_ranges(torch.zeros(4, dtype=torch.int64), 3)[-1] == (0, 4)
     assert shard.query_ranges(w, 1) == [(0, 10)]
     assert [shard.key_share(10, 3, r) for r in range(3)] == [(0, 4), (4, 8), (8, 10)]
+
+
+def test_row_cost_conserves_pairs_batches_and_jobs():
+    # every (batch, kv head, 2048-row range, block) list with n queries is one
+    # job of ceil(n / 8) batches; the per-row costs must add up to exactly
+    # per_pair * pairs + per_batch * batches + per_job * jobs
+    cfg = W.scaled(W.CONFIGS["c3"], B=2, T=5000, Hq=8, Hk=2, S=8)
+    idx = W.make_indices(cfg, "cpu", 4)
+    pairs = int(shard.row_work(idx, cfg.bs, cfg.T).sum())
+    lists = {}
+    for b in range(cfg.B):
+        for t in range(cfg.T):
+            for h in range(cfg.Hk):
+                for e in idx[b, t, h].tolist():
+                    if 0 <= e and e * cfg.bs <= t:     # causal, self-attention: the block has a key <= t
+                        key = (b, h, t // 2048, e)
+                        lists[key] = lists.get(key, 0) + 1
+    jobs = len(lists)
+    batches = sum((n + 7) // 8 for n in lists.values())
+    c = shard.row_cost(idx, cfg.bs, cfg.T, per_pair=1.0, per_batch=1000.0, per_job=1e6)
+    assert abs(float(c.sum()) - (pairs + 1000.0 * batches + 1e6 * jobs)) < 1e-3 * float(c.sum())
+    only_pairs = shard.row_cost(idx, cfg.bs, cfg.T, per_pair=1.0, per_batch=0.0, per_job=0.0)
+    assert torch.equal(only_pairs, shard.row_work(idx, cfg.bs, cfg.T).to(torch.float64))
