@@ -583,7 +583,7 @@ def main():
     ap.add_argument("--seq", type=int, default=0, help="override the sequence length (scaled secondary configs)")
     ap.add_argument("--dq-mode", choices=["auto", "separate", "fused"], default="auto",
                     help="backward dQ plan (profiling runs): its own query-centric pass or fused into dK/dV")
-    ap.add_argument("--balance", choices=["pairs", "cost"], default="pairs",
+    ap.add_argument("--balance", choices=["pairs", "cost"], default="cost",
                     help="--split query: balance rows by selected pairs, or by a cost that also counts the "
                          "dK/dV pass's jobs and batches (ops_b200/shard.py row_cost)")
     ap.add_argument("--split", choices=["none", "query"], default="none",
