@@ -1,6 +1,8 @@
 """Host-side logic on the CPU: index generation for the benchmark configs,
 FLOP/pair accounting, the tiling layer, and input validation of the Python
 surface (which must refuse CPU tensors — there is no CPU implementation)."""
+import os
+
 import pytest
 import torch
 
@@ -92,3 +94,26 @@ def test_oracle_index_semantics():
     assert not ok[0, 4:8].any()              # -1
     assert not ok[0, 8:12].any()             # block 9 is past kv_len 10 (blocks 0..2)
     assert ok[0, 12:].tolist() == [True, True, False, False]   # duplicate counts again
+
+
+def test_reference_arm_prints_one_contract_line():
+    # the reference arm (the CPU restatement) runs without a GPU: its one JSON
+    # line must carry the contract's keys, with e2e equal to the value and no
+    # host/device copies
+    import json
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, os.path.join(root, "bench.py"), "--impl", "reference", "--config", "c1",
+                          "--steps", "1", "--warmup", "1"], capture_output=True, text=True, timeout=600, cwd=root)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["value"] > 0 and d["steps"] == 1 and d["warmup"] == 1
+    assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert d["config"]["workload"].startswith("c1")
