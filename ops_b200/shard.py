@@ -56,8 +56,9 @@ def row_cost(block_indices: torch.Tensor, block_size: int, kv_len: int, causal: 
     thinner jobs.  Each valid (row, kv head, block) entry carries 1/n of its
     job and ceil(n / batch_rows)/n of its batches (n = the job's queries).  The
     default weights are B200 times at D = 128 (ms per pair of the forward, per
-    batch and per job of the pass), fitted to the two ranks of a measured
-    two-GPU split.  Returns float64 per row."""
+    batch and per job of the pass), fitted with :func:`fit_cost` to the two
+    ranks of a measured two-GPU split of one 65536-token sequence (4 kv heads,
+    32 selected 64-key blocks a row).  Returns float64 per row."""
     B, T, Hk, S = block_indices.shape
     e = block_indices.to(torch.int64)
     nblk = (kv_len + block_size - 1) // block_size
@@ -80,6 +81,50 @@ def row_cost(block_indices: torch.Tensor, block_size: int, kv_len: int, causal: 
                             torch.zeros_like(counts))
     ent = torch.where(valid, per_entry[jid.clamp(min=0)], torch.zeros(jid.shape, dtype=torch.float64, device=e.device))
     return per_pair * pairs + ent.sum(dim=(0, 2, 3))
+
+
+def range_units(block_indices: torch.Tensor, block_size: int, ranges: List[Tuple[int, int]], kv_len_of=None,
+                causal: bool = True, range_rows: int = 2048, batch_rows: int = 8) -> List[Tuple[int, int, int]]:
+    """(pairs, batches, jobs) of each rank's rows as the rank runs them: rows
+    [r0, r1) against keys [0, r1) (``kv_len_of(r0, r1)`` overrides), the
+    dK/dV pass's row ranges counted from r0."""
+    out = []
+    for r0, r1 in ranges:
+        if r1 <= r0:
+            out.append((0, 0, 0))
+            continue
+        kv = kv_len_of(r0, r1) if kv_len_of else r1
+        e = block_indices[:, r0:r1].to(torch.int64)
+        B, Tq, Hk, S = e.shape
+        nblk = (kv + block_size - 1) // block_size
+        pos = torch.arange(Tq, device=e.device) + (kv - Tq)
+        first = e * block_size
+        end = torch.clamp(first + block_size, max=kv)
+        if causal:
+            end = torch.minimum(end, pos[None, :, None, None] + 1)
+        n = torch.clamp(end - first, min=0)
+        valid = (e >= 0) & (e < nblk) & (n > 0)
+        nr = (Tq + range_rows - 1) // range_rows
+        rr = (torch.arange(Tq, device=e.device) // range_rows)[None, :, None, None]
+        jid = ((torch.arange(B, device=e.device)[:, None, None, None] * Hk +
+                torch.arange(Hk, device=e.device)[None, None, :, None]) * nr + rr) * nblk + torch.clamp(e, 0, nblk - 1)
+        cnt = torch.bincount(jid[valid], minlength=B * Hk * nr * nblk)
+        out.append((int(n[valid].sum()), int(((cnt + batch_rows - 1) // batch_rows).sum()), int((cnt > 0).sum())))
+    return out
+
+
+def fit_cost(units: List[Tuple[int, int, int]], fwd_ms: List[float], dkdv_ms: List[float]) -> dict:
+    """Weights for :func:`row_cost` from a measured split: per-rank (pairs,
+    batches, jobs) from :func:`range_units` and the ranks' forward and dK/dV
+    stage times (the bench line's ``stages_ms_per_rank``).  The forward is
+    taken as proportional to pairs; the dK/dV pass as a per-batch plus a
+    per-job time, solved by least squares (two or more ranks)."""
+    pairs = torch.tensor([u[0] for u in units], dtype=torch.float64)
+    A = torch.tensor([[u[1], u[2]] for u in units], dtype=torch.float64)
+    y = torch.tensor(dkdv_ms, dtype=torch.float64)
+    per_pair = float(sum(fwd_ms)) / float(pairs.sum())
+    sol = torch.linalg.lstsq(A, y[:, None]).solution.flatten()
+    return {"per_pair": per_pair, "per_batch": float(sol[0]), "per_job": float(sol[1])}
 
 
 def query_ranges(work: torch.Tensor, world: int) -> List[Tuple[int, int]]:

@@ -110,3 +110,20 @@ def test_row_cost_conserves_pairs_batches_and_jobs():
     assert abs(float(c.sum()) - (pairs + 1000.0 * batches + 1e6 * jobs)) < 1e-3 * float(c.sum())
     only_pairs = shard.row_cost(idx, cfg.bs, cfg.T, per_pair=1.0, per_batch=0.0, per_job=0.0)
     assert torch.equal(only_pairs, shard.row_work(idx, cfg.bs, cfg.T).to(torch.float64))
+
+
+def test_default_cost_weights_come_from_the_recorded_split():
+    # per-rank stage times of a two-GPU split of the c3 shape balanced by pairs
+    # (bench --config c3 --split query --balance pairs, stages_ms_per_rank):
+    # forward 9.3779 / 9.2859 ms, dK/dV 9.2304 / 10.5881 ms; refitting them
+    # from the rows' counted pairs, batches and jobs gives row_cost's defaults
+    import inspect
+    cfg = W.CONFIGS["c3"]
+    idx = W.make_indices(cfg, "cpu", 1000)
+    ranges = shard.query_ranges(shard.row_work(idx, cfg.bs, cfg.T), 2)
+    units = shard.range_units(idx, cfg.bs, ranges)
+    fit = shard.fit_cost(units, [9.3779, 9.2859], [9.2304, 10.5881])
+    defaults = {k: v.default for k, v in inspect.signature(shard.row_cost).parameters.items()
+                if k in ("per_pair", "per_batch", "per_job")}
+    for k, v in defaults.items():
+        assert abs(fit[k] - v) <= 0.02 * v, (k, fit[k], v)
