@@ -5,35 +5,43 @@
 
 A step is one forward + backward of the sparse attention op over one batch of
 the configuration's synthetic inputs (default c2: B=4, T=8192, Hq=64, Hk=4,
-D=128, block_size=64, 16 selected blocks per (query, kv head)).  Under torchrun
-every rank processes its own batch of that shape (weak scaling: the global
-batch is 4*N; no collective on the data path — ranks share nothing).  With
---split query (for configurations with fewer (batch, kv head) units than
-ranks, e.g. c3) the ranks instead split one batch's query rows, balanced by
-selected pairs (ops_b200/shard.py), and the step includes the one
-reduce-scatter that sums the dK/dV partials (strong scaling).
+D=128, block_size=64, 16 selected blocks per (query, kv head)).
+
+Several GPUs (torchrun, one process per GPU).  The default split is by
+(batch, kv head) units, the partition the op's independence gives: c2's 16
+units are dealt out 16/N per rank (whole batches, or kv heads of one batch),
+every rank runs the unchanged op on views of its units, and nothing is
+exchanged (strong scaling: the global problem is the configuration's).
+``--split query`` splits one batch's query rows instead (for configurations
+with fewer units than ranks, e.g. c3 at 8 GPUs; ops_b200/shard.py) and adds the
+one reduce-scatter that sums the dK/dV partials; ``--split batch`` gives every
+rank its own batch of the configuration (weak scaling).
 
 value      selected-token TFLOP/s of the whole job (all ranks), inputs resident
            in HBM, timed with CUDA events per step (L2 flushed between steps),
            max over ranks.  FLOPs: fwd 2P(Dqk+Dv) + bwd 2P(3Dqk+2Dv) over the
            P valid (query-head, key) pairs counted from the indices.
+kernels    every kernel of the step, timed with CUDA events recorded between
+           launches (the library's launch trace, sfa_launch_trace).
+roofline   the kernel with the largest share of the step: its algorithmic
+           FLOPs per launch / its CUDA-event duration, against the measured
+           bf16 peak; traffic from an ncu capture of that kernel.
 e2e        the same metric through the public API (ops_b200.sparse_flash_attention
            + autograd) with the step's inputs copied from pinned host memory and
-           its outputs (o, dq, dk, dv) copied back inside the timed region.
-roofline   the dominant kernel: its algorithmic FLOPs per launch / its CUDA-event
-           duration, against the measured bf16 peak.
+           its outputs (o, dq, dk, dv) copied back inside the timed region; the
+           rank's units go through in chunks on three streams, so one chunk's
+           copies overlap another's kernels.
 cpu_baseline  the CPU restatement (oracle/sfa_oracle.py, fp32 PyTorch, all host
-           threads) on a bounded sample of the same workload (rank 0, N=1).
---impl reference  times that CPU restatement alone on the same config/metric
-           (the reference's own kernels are Triton-Ascend and have no CPU or CUDA
-           implementation to run here).
+           threads) on a fixed sample of the same workload (rank 0, N=1); the
+           reference arm (--impl reference) runs that same sample per step.
+configs    (N = 1, default config) the other BASELINE configurations, each
+           with its value, roofline, e2e and CPU baseline.
 """
 from __future__ import annotations
 
 import argparse
 import ctypes
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -45,24 +53,26 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "SFA fwd+bwd TFLOP/s (selected tokens) & % bf16 tensor peak, 1/2/4/8 B200"
-# DRAM bytes (read + write) per launch from ncu captures of the c2 shape at B=1
-# (the kernel summaries kept with the profiles), scaled x4 to the bench's B=4
-# launch: each unit's q/dO/o/dq rows are read or written once and its K/V stay
-# in L2.
-NCU_TRAFFIC = {"c2": {"fwd": 4 * (0.153979e9 + 0.102984e9),
-                      "bwd_dq": 4 * (0.296924e9 + 0.112170e9),        # SFA_DQ_SEPARATE
-                      "bwd_dkdv": 4 * (1.294898e9 + 0.735617e9)}}     # with the fused dQ
+DECODE_METRIC = "SFA decode forward GB/s (gathered K/V rows), B200"
+# DRAM bytes (read + write) per launch of each tensor-core kernel from ncu
+# captures of the c2 shape at B = 1 (4 (batch, kv head) units; the summaries
+# are kept with the profiles).  A launch over u units moves u/4 of that: each
+# unit's q/dO/o/dq rows are read or written once and its K/V stay in L2.
+NCU_TRAFFIC_C2_B1 = {"fwd_tc": 0.153979e9 + 0.102984e9,
+                     "bwd_dq_tc": 0.296924e9 + 0.112170e9,
+                     "bwd_dkdv_tc": 1.294898e9 + 0.735617e9}
 FALLBACK_BF16_TFLOPS = 1590.0
+FALLBACK_HBM_GBS = 6650.0
 
 
 def peaks():
-    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    """(bf16 burst TFLOP/s, HBM GB/s, kind) from MEASURED_PEAKS.json."""
     try:
-        with open(path) as f:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             d = json.load(f)
-        return float(d["bf16_tflops"]), "measured"
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
     except Exception:
-        return FALLBACK_BF16_TFLOPS, "fallback"
+        return FALLBACK_BF16_TFLOPS, FALLBACK_HBM_GBS, "fallback"
 
 
 class ClockSampler:
@@ -106,6 +116,7 @@ class ClockSampler:
         sel = [p for (t, p) in self.samples if t0 <= t <= t1] or [p for (_, p) in self.samples]
         if not sel:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+
         def num(x):
             try:
                 return float(x)
@@ -120,345 +131,503 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# CPU restatement (reference arm and cpu_baseline)
+# CPU restatement: one sampling rule for cpu_baseline and the reference arm
 # ---------------------------------------------------------------------------
-def cpu_sample_run(cfg, n_tok, seed=0):
-    """fwd+bwd of the CPU restatement over the last n_tok queries of one (batch,
-    kv head) unit of the configuration; returns (seconds, flops)."""
+# Fixed sample per configuration: fwd+bwd of the last `last` queries of the
+# (batch 0, kv head 0) unit (decode: the forward of the first `seqs`
+# sequences).  A few seconds of fp32 work on 16 host threads each.
+CPU_SAMPLE = {"c1": {"last": 1024}, "c2": {"last": 8192}, "c3": {"last": 1024}, "c4": {"last": 64},
+              "c5": {"seqs": 16}}
+
+
+def cpu_sample_desc(cfg) -> str:
+    s = CPU_SAMPLE.get(cfg.name, {"last": min(cfg.T, 1024)})
+    if cfg.fwd_only:
+        return (f"forward of the first {s.get('seqs', cfg.n_seqs)} sequences of {cfg.name} (all kv heads), "
+                "fp32 PyTorch restatement of SFA.py")
+    G = cfg.Hq // cfg.Hk
+    return (f"fwd+bwd of the last {min(cfg.T, s['last'])} queries x {G} heads of the (batch 0, kv head 0) unit "
+            f"of {cfg.name}, fp32 PyTorch restatement of SFA.py")
+
+
+def cpu_sample_run(cfg, seed=0):
+    """One CPU sample; returns (seconds, work) with work in FLOPs (fwd+bwd
+    configurations) or gathered K/V bytes (decode)."""
     import torch
     from oracle import sfa_oracle as O
     from ops_b200 import workloads as W
+    s = CPU_SAMPLE.get(cfg.name, {"last": min(cfg.T, 1024)})
+    if cfg.fwd_only:
+        n = s.get("seqs", cfg.n_seqs)
+        d = W.make_decode(W.scaled(cfg, n_seqs=n), "cpu", seed)
+        keys = W.count_pairs(d["idx"], cfg.bs, 1, 0, kv_lens=d["kv_lens"])
+        q, k, v = d["q"].float(), d["k"].float(), d["v"].float()
+        t0 = time.perf_counter()
+        O.sfa_forward(q, k, v, d["idx"], cfg.bs, cfg.scale, None, True, d["cu_q"], d["cu_k"])
+        return time.perf_counter() - t0, keys * (cfg.Dqk + cfg.Dv) * 2.0
     G = cfg.Hq // cfg.Hk
     one = W.scaled(cfg, B=1, Hq=G, Hk=1)
     d = W.make_inputs(one, "cpu", seed, dtype=torch.bfloat16)
+    n_tok = min(cfg.T, s["last"])
     t0 = cfg.T - n_tok
     q = d["q"][:, t0:].float()
     k, v = d["k"].float(), d["v"].float()
     idx = d["idx"][:, t0:]
     do = d["do"][:, t0:].float()
     pairs = W.count_pairs(idx, cfg.bs, n_tok, cfg.T) * G
-    flops = O.sfa_flops(pairs, cfg.Dqk, cfg.Dv).total
-    s = time.perf_counter()
+    flops = W.sfa_flops(pairs, cfg.Dqk, cfg.Dv).total
+    t1 = time.perf_counter()
     o, lse = O.sfa_forward(q, k, v, idx, cfg.bs, cfg.scale, None, cfg.causal)
     O.sfa_backward(q, k, v, idx, o, lse, do, cfg.bs, cfg.scale, None, cfg.causal)
-    return time.perf_counter() - s, flops
+    return time.perf_counter() - t1, flops
 
 
-def calibrate_cpu_tokens(cfg, target_s):
-    n = 32
-    dt, _ = cpu_sample_run(cfg, n)
-    n2 = int(max(32, min(cfg.T, n * target_s / max(dt, 1e-3))))
-    return n2
+def cpu_unit(cfg):
+    return ("GB/s", 1e9) if cfg.fwd_only else ("TFLOP/s", 1e12)
 
 
-def cpu_baseline(cfg, target_s=12.0):
+def cpu_baseline(cfg, reps=2):
+    """The fixed sample, `reps` times (seeds 0..reps-1): total work / total time."""
     import torch
-    n = calibrate_cpu_tokens(cfg, target_s)
-    dt, fl = cpu_sample_run(cfg, n)
-    G = cfg.Hq // cfg.Hk
-    return {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"last {n} queries x {G} heads of one (batch, kv head) unit of {cfg.name}, "
-                      f"fwd+bwd, fp32 PyTorch ({dt:.1f} s)"}
+    torch.set_num_threads(os.cpu_count() or 1)
+    tt, ww = 0.0, 0.0
+    for r in range(reps):
+        dt, w = cpu_sample_run(cfg, seed=r)
+        tt += dt
+        ww += w
+    unit, div = cpu_unit(cfg)
+    return {"value": ww / tt / div, "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{cpu_sample_desc(cfg)}; {reps} seeds, {tt:.1f} s"}
 
 
 def run_reference(args, cfg):
+    """The reference arm: the CPU restatement on the same sample rule as
+    cpu_baseline, one sample per step (seed = step index)."""
     import torch
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     torch.set_num_threads(os.cpu_count() or 1)
-    n = calibrate_cpu_tokens(cfg, 4.0)
-    for _ in range(args.warmup):
-        cpu_sample_run(cfg, n)
-    tot_t, tot_f = 0.0, 0.0
+    for i in range(args.warmup):
+        cpu_sample_run(cfg, seed=i)
+    tot_t, tot_w = 0.0, 0.0
     for i in range(args.steps):
-        dt, fl = cpu_sample_run(cfg, n, seed=i)
+        dt, w = cpu_sample_run(cfg, seed=i)
         tot_t += dt
-        tot_f += fl
-    v = tot_f / tot_t / 1e12
-    G = cfg.Hq // cfg.Hk
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot_t / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": config_dict(cfg, args.gpus),
-            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": f"per step: last {n} queries x {G} heads of one (batch, kv head) unit, "
-                                       "fwd+bwd of the fp32 PyTorch restatement of SFA.py"},
-            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        tot_w += w
+    unit, div = cpu_unit(cfg)
+    v = tot_w / tot_t / div
+    split = resolve_split(args, cfg, args.gpus)
+    line = {"impl": "reference", "metric": DECODE_METRIC if cfg.fwd_only else METRIC, "value": v, "unit": unit,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * tot_t / args.steps, "higher_is_better": True,
+            "scaling": scaling_kind(split), "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": config_dict(cfg, args.gpus, split, args.balance),
+            "cpu_baseline": {"value": v, "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"per step: {cpu_sample_desc(cfg)}"},
+            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def reduce_over_ranks(step_ms, e2e_ms, flops, device):
-    """Whole-job figures: the slowest rank's step times and the work of all
-    ranks (each rank processes its own batch; nothing else is exchanged)."""
+# ---------------------------------------------------------------------------
+# splits
+# ---------------------------------------------------------------------------
+def unit_range(cfg, world, rank):
+    """(b0, b1, h0, h1) of rank's (batch, kv head) units, or None when the
+    units do not deal out evenly as whole batches or kv-head groups."""
+    units = cfg.B * cfg.Hk
+    if units % world:
+        return None
+    per = units // world
+    u0 = rank * per
+    if per % cfg.Hk == 0:
+        b0 = u0 // cfg.Hk
+        return b0, b0 + per // cfg.Hk, 0, cfg.Hk
+    if cfg.Hk % per == 0:
+        b0, h0 = divmod(u0, cfg.Hk)
+        return b0, b0 + 1, h0, h0 + per
+    return None
+
+
+def resolve_split(args, cfg, world):
+    if world == 1:
+        return "none"
+    if args.split != "auto":
+        return args.split
+    if cfg.fwd_only:
+        return "units"
+    return "units" if unit_range(cfg, world, 0) is not None else "query"
+
+
+def rank_seed(rank: int) -> int:
+    """Seed of a rank's inputs under --split batch (each rank its own batch);
+    the other splits give every rank the inputs of rank 0."""
+    return 1000 + rank
+
+
+def reduce_over_ranks(step_ms, e2e_ms, work, device):
+    """Whole-job figures: the slowest rank's step and e2e times, the work of
+    all ranks.  One MAX and one SUM all-reduce, the same on every rank."""
     import torch
     import torch.distributed as dist
     if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
-        return float(step_ms), float(e2e_ms), float(flops)
+        return float(step_ms), float(e2e_ms), float(work)
     t = torch.tensor([step_ms, e2e_ms], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    f = torch.tensor([flops], dtype=torch.float64, device=device)
+    f = torch.tensor([work], dtype=torch.float64, device=device)
     dist.all_reduce(f, op=dist.ReduceOp.SUM)
     return float(t[0]), float(t[1]), float(f[0])
 
 
-def rank_seed(rank: int) -> int:
-    """Each rank draws its own batch of the configuration."""
-    return 1000 + rank
+def scaling_kind(split):
+    return "weak" if split == "batch" else "strong"
 
 
-def config_dict(cfg, n, split=False):
-    per = "" if split else "/rank"
-    return {"workload": f"{cfg.name}: block-sparse GQA attention fwd+bwd, B={cfg.B}{per}, T={cfg.T}, "
-                        f"Hq={cfg.Hq}, Hk={cfg.Hk}, Dqk={cfg.Dqk}, Dv={cfg.Dv}, block_size={cfg.bs}, "
-                        f"S={cfg.S}, {cfg.mode} causal selection, q/k/v/dO ~ N(0,1)",
-            "global_batch": cfg.B if split else cfg.B * n, "seq_len": cfg.T,
-            "parallelism": (f"{n} query-row ranges balanced by selected pairs, dK/dV summed by one "
-                            f"reduce-scatter" if split else f"dp{n} (independent batch shards)"),
-            "l2": "flushed between timed steps (256 MiB memset)"}
+def config_dict(cfg, n, split, balance="cost"):
+    if cfg.fwd_only:
+        return {"workload": f"{cfg.name}: varlen decode forward, {cfg.n_seqs} sequences x 1 query, kv "
+                            f"lengths U[{cfg.kv_min}, {cfg.kv_max}], Hq={cfg.Hq}, Hk={cfg.Hk}, Dqk={cfg.Dqk}, "
+                            f"Dv={cfg.Dv}, block_size={cfg.bs}, S={cfg.S} uniform blocks, q/k/v ~ N(0,1)",
+                "global_batch": cfg.n_seqs,
+                "parallelism": "single GPU" if n == 1 else f"{n} ranks x {cfg.n_seqs // n} sequences",
+                "l2": "flushed between timed steps (256 MiB memset)"}
+    per = "/rank" if split == "batch" else ""
+    par = {"none": "single GPU",
+           "units": f"{n} ranks x {cfg.B * cfg.Hk // max(n, 1)} (batch, kv head) units each, no collective",
+           "batch": f"dp{n} (every rank its own batch)",
+           "query": (f"{n} query-row ranges balanced by "
+                     + ("the job-aware cost (shard.row_cost)" if balance == "cost" else "selected pairs")
+                     + ", dK/dV summed by one reduce-scatter")}[split]
+    sel = {"uniform": "uniform causal", "recent": "recent-biased causal", "token": "token-level causal top-k",
+           "decode": "uniform"}[cfg.mode]
+    return {"workload": f"{cfg.name}: sparse attention fwd+bwd, B={cfg.B}{per}, T={cfg.T}, Hq={cfg.Hq}, "
+                        f"Hk={cfg.Hk}, Dqk={cfg.Dqk}, Dv={cfg.Dv}, block_size={cfg.bs}, S={cfg.S}, {sel} "
+                        "selection, q/k/v/dO ~ N(0,1)",
+            "global_batch": cfg.B * n if split == "batch" else cfg.B, "seq_len": cfg.T,
+            "parallelism": par, "l2": "flushed between timed steps (256 MiB memset)"}
 
 
 # ---------------------------------------------------------------------------
-# GPU arm
+# GPU arm: one fwd+bwd configuration
 # ---------------------------------------------------------------------------
-def run_ours(args, cfg):
+def kernel_flops(name, P, cfg, fl, fused_dq):
+    """Algorithmic FLOPs a kernel owns (recomputation not counted).  With the
+    fused dQ the key-centric pass performs every backward product (S, dP, dQ,
+    dK, dV); the separate dQ pass owns S, dP and dQ, leaving dK and dV."""
+    two_p = 2.0 * P
+    if name.startswith("fwd_"):
+        return fl.fwd
+    if name == "bwd_dq_tc":
+        return two_p * (2 * cfg.Dqk + cfg.Dv)
+    if name == "bwd_dkdv_tc":
+        return fl.bwd if fused_dq else two_p * (cfg.Dqk + cfg.Dv)
+    if name in ("bwd_general", "bwd_tok"):
+        return fl.bwd
+    return 0.0
+
+
+def measure_config(args, cfg, world, rank, dev, split, steps, warmup, primary):
     import torch
     import torch.distributed as dist
 
-    import ops_b200
     from ops_b200 import _lib
     from ops_b200 import sfa as S
     from ops_b200 import workloads as W
-    from oracle import sfa_oracle as O  # noqa: F401  (FLOP formula only)
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     lib = _lib.load()
-
-    # --split query (strong scaling of one batch): every rank builds the same
-    # inputs and takes its range of query rows against the keys they can see;
-    # the dK/dV partials are summed by one reduce-scatter inside the step
-    split = args.split == "query" and world > 1
-    d = W.make_inputs(cfg, dev, seed=rank_seed(0 if split else rank))
+    d = W.make_inputs(cfg, dev, seed=rank_seed(rank if split == "batch" else 0))
     q, k, v, idx, do = d["q"], d["k"], d["v"], d["idx"], d["do"]
-    r0, r1, ke = 0, cfg.T, cfg.T
-    if split:
+    v_view = v.data_ptr() == k.data_ptr()            # v = kv[..., :Dv] (MLA latent)
+    T = cfg.T
+    r0, r1, ke = 0, T, T
+    b0, b1, h0, h1 = 0, cfg.B, 0, cfg.Hk
+    G = cfg.Hq // cfg.Hk
+    if split == "units":
+        b0, b1, h0, h1 = unit_range(cfg, world, rank)
+        q, do = q[b0:b1, :, h0 * G:h1 * G], do[b0:b1, :, h0 * G:h1 * G]
+        k, v, idx = k[b0:b1, :, h0:h1], v[b0:b1, :, h0:h1], idx[b0:b1, :, h0:h1]
+    elif split == "query":
         from ops_b200 import shard
-        work = (shard.row_cost(idx, cfg.bs, cfg.T) if args.balance == "cost"
-                else shard.row_work(idx, cfg.bs, cfg.T))
-        ranges = shard.query_ranges(work, world)
-        r0, r1 = ranges[rank]
+        work = (shard.row_cost(idx, cfg.bs, T) if args.balance == "cost" else shard.row_work(idx, cfg.bs, T))
+        r0, r1 = shard.query_ranges(work, world)[rank]
         ke = r1
         q, idx, do = q[:, r0:r1], idx[:, r0:r1], do[:, r0:r1]
         k, v = k[:, :ke], v[:, :ke]
-    G = cfg.Hq // cfg.Hk
+    units = (b1 - b0) * (h1 - h0)
     pairs = W.count_pairs(idx, cfg.bs, r1 - r0, ke) * G
-    fl = O.sfa_flops(pairs, cfg.Dqk, cfg.Dv)
+    fl = W.sfa_flops(pairs, cfg.Dqk, cfg.Dv)
     o = torch.empty(*q.shape[:-1], cfg.Dv, dtype=q.dtype, device=dev)
     lse = torch.empty(q.shape[:-1], dtype=torch.float32, device=dev)
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    scfg = S._Cfg(cfg.bs, cfg.scale, True, False, r1 - r0, ke, _lib.SFA_DKV_AUTO, _lib.SFA_KERNEL_AUTO, False,
-                  S._DQ[args.dq_mode])
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)   # v = kv[..., :Dv] (c4): the caller adds dv into kv's gradient
+    scfg = S._Cfg(cfg.bs, cfg.scale, cfg.causal, False, r1 - r0, ke, _lib.SFA_DKV_AUTO, _lib.SFA_KERNEL_AUTO,
+                  False, S._DQ[args.dq_mode])
     P = S.build_params(q, k, v, idx, o, lse, scfg, None, None, None, do, dq, dk, dv, None)
-    fam_f = lib.sfa_select_kernel(ctypes.byref(P), 0)
-    fam_b = lib.sfa_select_kernel(ctypes.byref(P), 1)
+    Pp = ctypes.byref(P)
+    fam_f = lib.sfa_select_kernel(Pp, 0)
+    fam_b = lib.sfa_select_kernel(Pp, 1)
+    _lib.check(min(0, fam_f), "select fwd")
+    _lib.check(min(0, fam_b), "select bwd")
     dkv_mode, dq_mode = ctypes.c_int32(), ctypes.c_int32()
-    _lib.check(min(0, lib.sfa_bwd_plan(ctypes.byref(P), ctypes.byref(dkv_mode), ctypes.byref(dq_mode))), "plan")
+    _lib.check(min(0, lib.sfa_bwd_plan(Pp, ctypes.byref(dkv_mode), ctypes.byref(dq_mode))), "plan")
     fused_dq = dq_mode.value == _lib.SFA_DQ_FUSED
-    nbytes = lib.sfa_bwd_workspace_bytes(ctypes.byref(P))
+    nbytes = lib.sfa_bwd_workspace_bytes(Pp)
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
-    Pp = ctypes.byref(P)
-    stages = ["fwd", "bwd_preprocess", "bwd_dq", "bwd_dkdv"] + (["dkdv_reduce_scatter"] if split else [])
-    if split:
-        tc = (cfg.T + world - 1) // world
+    if split == "query":
+        tc = (T + world - 1) // world
         rs_in = torch.zeros(world * tc, cfg.B, cfg.Hk, cfg.Dqk + cfg.Dv, dtype=torch.float32, device=dev)
         rs_out = torch.empty(tc, cfg.B, cfg.Hk, cfg.Dqk + cfg.Dv, dtype=torch.float32, device=dev)
 
-    def step(ev=None):
-        if ev:
-            ev[0].record(stream)
+    def step():
         _lib.check(lib.sfa_fwd(Pp, None, 0, sptr), "sfa_fwd")
-        if ev:
-            ev[1].record(stream)
         _lib.check(lib.sfa_bwd_preprocess(Pp, ws.data_ptr(), nbytes, sptr), "preprocess")
-        if ev:
-            ev[2].record(stream)
         _lib.check(lib.sfa_bwd_dq(Pp, ws.data_ptr(), nbytes, sptr), "dq")
-        if ev:
-            ev[3].record(stream)
         _lib.check(lib.sfa_bwd_dkdv(Pp, ws.data_ptr(), nbytes, sptr), "dkdv")
-        if ev:
-            ev[4].record(stream)
-        if split:
+        if split == "query":
             rs_in[:ke, ..., :cfg.Dqk].copy_(dk.transpose(0, 1))
             rs_in[:ke, ..., cfg.Dqk:].copy_(dv.transpose(0, 1))
             dist.reduce_scatter_tensor(rs_out, rs_in)
-            if ev:
-                ev[5].record(stream)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
+    # events: one before the step, then one after each library operation (trace)
+    NEV = 48
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    tr = [[torch.cuda.Event(enable_timing=True) for _ in range(NEV)] for _ in range(steps)]
+    for e in starts + ends + [x for row in tr for x in row]:
+        e.record(stream)                      # creates the handles
+    torch.cuda.synchronize()
+    handles = [(ctypes.c_void_p * NEV)(*[e.cuda_event for e in row]) for row in tr]
+    sampler = None
+    if primary:
+        sampler = ClockSampler(torch.cuda.current_device())
+        sampler.start()
+        time.sleep(0.3)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    nev = len(stages) + 1
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nev)] for _ in range(args.steps)]
+    counts, names = [], []
     n0 = lib.sfa_kernel_launches()
     t_wall0 = time.time()
-    for i in range(args.steps):
+    for i in range(steps):
         flush.zero_()
-        step(evs[i])
+        starts[i].record(stream)
+        lib.sfa_launch_trace(handles[i], NEV)
+        step()
+        counts.append(lib.sfa_launch_trace_count())
+        names.append([lib.sfa_launch_trace_name(j).decode() for j in range(counts[-1])])
+        lib.sfa_launch_trace(None, 0)
+        ends[i].record(stream)
     torch.cuda.synchronize()
     t_wall1 = time.time()
     n1 = lib.sfa_kernel_launches()
     if world > 1:
         dist.barrier()
-    stage_ms = {s: sum(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps)) / args.steps
-                for j, s in enumerate(stages)}
-    step_ms = sum(evs[i][0].elapsed_time(evs[i][nev - 1]) for i in range(args.steps)) / args.steps
+    step_ms = sum(starts[i].elapsed_time(ends[i]) for i in range(steps)) / steps
+    kern_ms = {}
+    for i in range(steps):
+        prev = starts[i]
+        for j in range(counts[i]):
+            kern_ms[names[i][j]] = kern_ms.get(names[i][j], 0.0) + prev.elapsed_time(tr[i][j]) / steps
+            prev = tr[i][j]
+        if split == "query":
+            kern_ms["dkdv_reduce_scatter"] = kern_ms.get("dkdv_reduce_scatter", 0.0) + \
+                prev.elapsed_time(ends[i]) / steps
 
-    # e2e through the public API, host buffers
-    host = {n: t.cpu().pin_memory() for n, t in (("q", q), ("k", k), ("v", v), ("idx", idx), ("do", do))}
-    outs = {n: torch.empty(tuple(t.shape), dtype=t.dtype, pin_memory=True) for n, t in
-            (("o", o), ("dq", q), ("dk", k), ("dv", v))}
-    if split:   # a rank gets back its rows and its key share of dk / dv
-        k0, k1 = shard.key_share(cfg.T, world, rank)
-        outs["dk"] = torch.empty((cfg.B, k1 - k0, cfg.Hk, cfg.Dqk), dtype=k.dtype, pin_memory=True)
-        outs["dv"] = torch.empty((cfg.B, k1 - k0, cfg.Hk, cfg.Dv), dtype=v.dtype, pin_memory=True)
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
-    d2h = sum(t.numel() * t.element_size() for t in outs.values())
+    e2e_ms, h2d, d2h = e2e_pipeline(args, cfg, d, split, (b0, b1, h0, h1), (r0, r1, ke), world, rank, dev,
+                                    stream, flush, v_view, steps=max(1, min(steps, 5)))
+    clocks = None
+    if sampler is not None:
+        sampler.stop()
+        clocks = sampler.summary(t_wall0, t_wall1)
 
-    def e2e_split_step():
-        qd = host["q"].to(dev, non_blocking=True)
-        kd = host["k"].to(dev, non_blocking=True)
-        vd = host["v"].to(dev, non_blocking=True)
-        ixd = host["idx"].to(dev, non_blocking=True)
-        dod = host["do"].to(dev, non_blocking=True)
-        r = shard.local_step(qd, kd, vd, ixd, dod, (r0, r1), cfg.T, rank, world, cfg.bs, cfg.scale)
-        outs["o"].copy_(r["o"], non_blocking=True)
-        outs["dq"].copy_(r["dq"], non_blocking=True)
-        outs["dk"].copy_(r["dk"], non_blocking=True)
-        outs["dv"].copy_(r["dv"], non_blocking=True)
-
-    def e2e_step():
-        if split:
-            return e2e_split_step()
-        qd = host["q"].to(dev, non_blocking=True).requires_grad_()
-        kd = host["k"].to(dev, non_blocking=True).requires_grad_()
-        vd = host["v"].to(dev, non_blocking=True).requires_grad_()
-        ixd = host["idx"].to(dev, non_blocking=True)
-        dod = host["do"].to(dev, non_blocking=True)
-        oo, _ = ops_b200.sparse_flash_attention(qd, kd, vd, ixd, cfg.bs, dq_mode=args.dq_mode)
-        oo.backward(dod)
-        outs["o"].copy_(oo.detach(), non_blocking=True)
-        outs["dq"].copy_(qd.grad, non_blocking=True)
-        outs["dk"].copy_(kd.grad, non_blocking=True)
-        outs["dv"].copy_(vd.grad, non_blocking=True)
-
-    e2e_steps = max(1, min(args.steps, 5))
-    for _ in range(max(1, min(args.warmup, 2))):
-        e2e_step()
-    torch.cuda.synchronize()
+    per_rank = None
     if world > 1:
-        dist.barrier()
-    e_ms = 0.0
-    for _ in range(e2e_steps):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        flush.zero_()
-        a.record(stream)
-        e2e_step()
-        b.record(stream)
-        torch.cuda.synchronize()
-        e_ms += a.elapsed_time(b)
-    e_ms /= e2e_steps
-    sampler.stop()
-    clocks = sampler.summary(t_wall0, t_wall1)
-
-    per_rank = [stage_ms]
-    if world > 1:   # every rank's stage times (load balance of a split)
         per_rank = [None] * world
-        dist.all_gather_object(per_rank, {k: round(v, 4) for k, v in stage_ms.items()})
-    step_ms_max, e_ms_max, flops_all = reduce_over_ranks(step_ms, e_ms, fl.total, dev)
-    if world > 1:
-        dist.destroy_process_group()
+        dist.all_gather_object(per_rank, {kk: round(vv, 4) for kk, vv in kern_ms.items()})
+    step_max, e2e_max, flops_all = reduce_over_ranks(step_ms, e2e_ms, fl.total, dev)
     if rank != 0:
-        return
+        return None
 
-    peak, peak_kind = peaks()
-    # algorithmic FLOPs owned by each stage (recomputation not counted)
-    two_p = 2.0 * pairs
-    tc_bwd = fam_b == _lib.SFA_KERNEL_TCGEN05
-    # with the fused dQ the dK/dV stage also owns dQ = dS.K (2P.Dqk) and the dQ
-    # stage only clears the accumulator
-    stage_flops = {"fwd": fl.fwd,
-                   "bwd_preprocess": 0.0,
-                   "bwd_dq": 0.0 if fused_dq else (two_p * (2 * cfg.Dqk + cfg.Dv) if tc_bwd else fl.bwd),
-                   "bwd_dkdv": (two_p * (2 * cfg.Dqk + cfg.Dv) if fused_dq else two_p * (cfg.Dqk + cfg.Dv))
-                   if tc_bwd else 0.0,
-                   "dkdv_reduce_scatter": 0.0}
-    dom = max(stages, key=lambda s: stage_ms[s])
-    # K and V rows gathered per (row, kv head): selected keys x (Dqk + Dv) bf16
-    kv_gather = pairs / G * (cfg.Dqk + cfg.Dv) * 2.0
-    # dK/dV: each selected (block, query) gathers the query's G heads of q and dO
-    qdo_gather = pairs / cfg.bs * (cfg.Dqk + cfg.Dv) * 2.0
-    gather_bytes = {"fwd": kv_gather, "bwd_dkdv": qdo_gather} if tc_bwd else {}
-    if tc_bwd and not fused_dq:
-        gather_bytes["bwd_dq"] = kv_gather
-    ach = stage_flops[dom] / (stage_ms[dom] * 1e-3) / 1e12
-    value = flops_all / (step_ms_max * 1e-3) / 1e12
-    e2e_v = flops_all / (e_ms_max * 1e-3) / 1e12
+    peak, _, peak_kind = peaks()
     fams = {1: "tcgen05", 2: "general"}
+    kernels = {}
+    for name, ms in sorted(kern_ms.items(), key=lambda x: -x[1]):
+        f = kernel_flops(name, pairs, cfg, fl, fused_dq)
+        ent = {"ms": round(ms, 4), "share": round(ms / step_ms, 4)}
+        if f:
+            ach_k = f / (ms * 1e-3) / 1e12
+            ent.update(tflops=round(ach_k, 2), frac=round(ach_k / peak, 4))
+        kernels[name] = ent
+    dom = max((n for n in kern_ms if not n.startswith("memset") and n != "dkdv_reduce_scatter"),
+              key=lambda n: kern_ms[n])
+    dom_f = kernel_flops(dom, pairs, cfg, fl, fused_dq)
+    ach = dom_f / (kern_ms[dom] * 1e-3) / 1e12 if dom_f else 0.0
+    traffic = tsrc = None
+    if cfg.name == "c2" and dom in NCU_TRAFFIC_C2_B1 and cfg.T == 8192 and split in ("none", "units", "batch"):
+        traffic = NCU_TRAFFIC_C2_B1[dom] * units / 4.0
+        tsrc = (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one {dom} launch at c2 B=1 (4 units), "
+                f"x{units}/4 for this launch's {units} units (profiles/)")
+    fwd_name = next((n for n in kern_ms if n.startswith("fwd_")), None)
+    # K/V rows the query-centric forward gathers: selected keys x (Dqk + Dv) bf16 per (row, kv head)
+    gather = pairs / G * (cfg.Dqk + cfg.Dv) * 2.0
+    value = flops_all / (step_max * 1e-3) / 1e12
     line = {
-        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": step_ms_max, "higher_is_better": True,
-        "scaling": "strong" if split else "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config_dict(cfg, world, split),
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": step_max, "higher_is_better": True,
+        "scaling": scaling_kind(split), "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": config_dict(cfg, world, split, args.balance),
         "pct_bf16_peak": 100.0 * value / world / peak,
-        "tokens_per_s": cfg.B * cfg.T * (1 if split else world) / (step_ms_max * 1e-3),
-        "selected_pairs_per_rank": pairs,
-        "stages_ms": stage_ms,
-        **({"stages_ms_per_rank": per_rank} if world > 1 else {}),
+        "tokens_per_s": cfg.B * cfg.T * (world if split == "batch" else 1) / (step_max * 1e-3),
+        "selected_pairs_rank0": pairs,
+        "kernels": kernels,
+        **({"kernels_ms_per_rank": per_rank} if per_rank else {}),
         "kernel_family": {"fwd": fams.get(fam_f, str(fam_f)), "bwd": fams.get(fam_b, str(fam_b)),
                           "dkv": {1: "inverted", 2: "atomic"}.get(dkv_mode.value),
                           "dq": {1: "separate", 2: "fused"}.get(dq_mode.value)},
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
-                     "frac": ach / peak, "peak_kind": f"{peak_kind} bf16 burst",
-                     "traffic": NCU_TRAFFIC.get(cfg.name, {}).get(dom) if cfg.B == 4 else None,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at B=1, "
-                                       "x4 for the B=4 launch (profiles/)"},
-        # gathered K/V rows per launch (L2 -> shared memory) of the dominant stage
-        "gather": {"kernel": dom, "bytes_per_launch": gather_bytes.get(dom),
-                   "achieved": (gather_bytes[dom] / (stage_ms[dom] * 1e-3) / 1e12) if gather_bytes.get(dom) else None,
-                   "unit": "TB/s"},
-        "e2e": {"value": e2e_v, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": e_ms_max},
-        "clocks": clocks,
+                     "frac": ach / peak, "peak_kind": f"{peak_kind} bf16 burst (kernels timed alone, a few ms)",
+                     "traffic": traffic, "traffic_source": tsrc,
+                     "algorithmic": f"{dom_f:.4g} FLOP per launch"},
+        "gather": {"kernel": fwd_name, "bytes_per_launch": gather,
+                   "achieved_tbs": gather / (kern_ms[fwd_name] * 1e-3) / 1e12 if fwd_name else None},
+        "e2e": {"value": flops_all / (e2e_max * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_max},
         "gpu_launches": int(n1 - n0),
     }
-    if world == 1 and not args.no_cpu:
-        line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
-    print(json.dumps(line), flush=True)
+    if clocks is not None:
+        line["clocks"] = clocks
+    return line
 
 
-def run_decode(args, cfg):
-    """Forward-only configurations (c5: varlen decode, one query per sequence):
-    a step is one sfa_fwd over the batch; HBM-bound, so the line reports the
-    gathered K/V bytes per second against the measured copy bandwidth."""
+def e2e_pipeline(args, cfg, d, split, units, rows, world, rank, dev, stream, flush, v_view, steps):
+    """Public-API step with host-resident inputs/outputs; returns (ms, h2d, d2h).
+
+    The rank's share is cut into chunks along the batch (or the kv heads of one
+    batch); chunk i's H2D copies run on one stream, its forward + backward on a
+    second, its D2H copies on a third, so the PCIe traffic of neighbouring
+    chunks overlaps the kernels (and H2D overlaps D2H)."""
+    import torch
+
+    import ops_b200
+    from ops_b200 import shard
+    b0, b1, h0, h1 = units
+    r0, r1, ke = rows
+    G = cfg.Hq // cfg.Hk
+    q, k, v, idx, do = d["q"], d["k"], d["v"], d["idx"], d["do"]
+    if split == "query":
+        chunks = [None]
+    elif b1 - b0 > 1:
+        chunks = [(b, b + 1, h0, h1) for b in range(b0, b1)]
+    elif h1 - h0 > 1:
+        chunks = [(b0, b1, h, h + 1) for h in range(h0, h1)]
+    else:
+        chunks = [(b0, b1, h0, h1)]
+
+    def pin(t):
+        return t.contiguous().cpu().pin_memory()
+
+    host, dbuf, outs = [], [], []
+    for c in chunks:
+        if c is None:   # query split: this rank's rows and visible keys
+            hs = dict(q=pin(q[:, r0:r1]), k=pin(k[:, :ke]), idx=pin(idx[:, r0:r1]), do=pin(do[:, r0:r1]))
+            if not v_view:
+                hs["v"] = pin(v[:, :ke])
+        else:
+            cb0, cb1, ch0, ch1 = c
+            hs = dict(q=pin(q[cb0:cb1, :, ch0 * G:ch1 * G]), k=pin(k[cb0:cb1, :, ch0:ch1]),
+                      idx=pin(idx[cb0:cb1, :, ch0:ch1]), do=pin(do[cb0:cb1, :, ch0 * G:ch1 * G]))
+            if not v_view:
+                hs["v"] = pin(v[cb0:cb1, :, ch0:ch1])
+        host.append(hs)
+        dbuf.append({n: torch.empty(t.shape, dtype=t.dtype, device=dev) for n, t in hs.items()})
+        o_sh = tuple(hs["q"].shape[:-1]) + (cfg.Dv,)
+        if c is None:
+            k0, k1 = shard.key_share(cfg.T, world, rank)
+            kv_sh = (cfg.B, k1 - k0, cfg.Hk)
+        else:
+            kv_sh = tuple(hs["k"].shape[:-1])
+        od = dict(o=torch.empty(o_sh, dtype=q.dtype, pin_memory=True),
+                  dq=torch.empty(tuple(hs["q"].shape), dtype=q.dtype, pin_memory=True),
+                  dk=torch.empty(kv_sh + (cfg.Dqk,), dtype=k.dtype, pin_memory=True))
+        if not v_view:
+            od["dv"] = torch.empty(kv_sh + (cfg.Dv,), dtype=v.dtype, pin_memory=True)
+        outs.append(od)
+    h2d = sum(t.numel() * t.element_size() for hs in host for t in hs.values())
+    d2h = sum(t.numel() * t.element_size() for od in outs for t in od.values())
+    s_in, s_c, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def one_step():
+        keep = []
+        start = torch.cuda.Event()
+        start.record(stream)
+        for s in (s_in, s_c, s_out):
+            s.wait_event(start)
+        in_ev = []
+        for hs, db in zip(host, dbuf):
+            with torch.cuda.stream(s_in):
+                for n in hs:
+                    db[n].copy_(hs[n], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(s_in)
+                in_ev.append(e)
+        for i, (c, db, od) in enumerate(zip(chunks, dbuf, outs)):
+            with torch.cuda.stream(s_c):
+                s_c.wait_event(in_ev[i])
+                if c is None:
+                    r = shard.local_step(db["q"], db["k"], db["k"][..., :cfg.Dv] if v_view else db["v"], db["idx"],
+                                         db["do"], (r0, r1), cfg.T, rank, world, cfg.bs, cfg.scale)
+                    res = [("o", r["o"]), ("dq", r["dq"]), ("dk", r["dk"])] + \
+                        ([] if v_view else [("dv", r["dv"])])
+                else:
+                    qg = db["q"].detach().requires_grad_()
+                    kg = db["k"].detach().requires_grad_()
+                    vg = kg[..., :cfg.Dv] if v_view else db["v"].detach().requires_grad_()
+                    oo, _ = ops_b200.sparse_flash_attention(qg, kg, vg, db["idx"], cfg.bs, cfg.scale,
+                                                            causal=cfg.causal, dq_mode=args.dq_mode)
+                    oo.backward(db["do"])
+                    res = [("o", oo.detach()), ("dq", qg.grad), ("dk", kg.grad)] + \
+                        ([] if v_view else [("dv", vg.grad)])
+                e = torch.cuda.Event()
+                e.record(s_c)
+            keep.append(res)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(e)
+                for n, t in res:
+                    od[n].copy_(t, non_blocking=True)
+        end = torch.cuda.Event()
+        end.record(s_out)
+        stream.wait_event(end)
+        return keep
+
+    one_step()
+    torch.cuda.synchronize()
+    ms = 0.0
+    for _ in range(steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        keep = one_step()
+        b.record(stream)
+        torch.cuda.synchronize()
+        del keep
+        ms += a.elapsed_time(b)
+    return ms / steps, h2d, d2h
+
+
+# ---------------------------------------------------------------------------
+# GPU arm: decode (forward-only, HBM-bound)
+# ---------------------------------------------------------------------------
+def measure_decode(args, cfg, world, rank, dev, steps, warmup, primary):
     import torch
     import torch.distributed as dist
 
@@ -467,21 +636,15 @@ def run_decode(args, cfg):
     from ops_b200 import sfa as S
     from ops_b200 import workloads as W
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     lib = _lib.load()
-    d = W.make_decode(cfg, dev, seed=rank_seed(rank))
+    # the sequences are dealt out evenly: every rank draws its own share
+    n_local = cfg.n_seqs // world if cfg.n_seqs % world == 0 else cfg.n_seqs
+    local_cfg = W.scaled(cfg, n_seqs=n_local)
+    d = W.make_decode(local_cfg, dev, seed=rank_seed(rank))
     q, k, v, idx, cu_q, cu_k = d["q"], d["k"], d["v"], d["idx"], d["cu_q"], d["cu_k"]
-    keys = W.count_pairs(idx, cfg.bs, 1, 0, kv_lens=d["kv_lens"])        # valid (query, kv head, key)
+    keys = W.count_pairs(idx, cfg.bs, 1, 0, kv_lens=d["kv_lens"])
     G = cfg.Hq // cfg.Hk
-    gathered = keys * (cfg.Dqk + cfg.Dv) * 2.0                             # K and V rows read
-    flops = 2.0 * keys * G * (cfg.Dqk + cfg.Dv)
+    gathered = keys * (cfg.Dqk + cfg.Dv) * 2.0
     o = torch.empty(q.shape[0], cfg.Hq, cfg.Dv, dtype=q.dtype, device=dev)
     lse = torch.empty(q.shape[0], cfg.Hq, dtype=torch.float32, device=dev)
     scfg = S._Cfg(cfg.bs, cfg.scale, True, True, 1, d["max_k"], _lib.SFA_DKV_AUTO, _lib.SFA_KERNEL_AUTO, False)
@@ -490,15 +653,17 @@ def run_decode(args, cfg):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         _lib.check(lib.sfa_fwd(ctypes.byref(P), None, 0, sptr), "sfa_fwd")
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sampler = None
+    if primary:
+        sampler = ClockSampler(torch.cuda.current_device())
+        sampler.start()
+        time.sleep(0.3)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     n0 = lib.sfa_kernel_launches()
     t_wall0 = time.time()
     for a, b in evs:
@@ -509,64 +674,134 @@ def run_decode(args, cfg):
     torch.cuda.synchronize()
     t_wall1 = time.time()
     n1 = lib.sfa_kernel_launches()
-    step_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
-    # e2e through the public API with host buffers
-    host = {n: t.cpu().pin_memory() for n, t in (("q", q), ("k", k), ("v", v), ("idx", idx))}
+    step_ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+    # decode e2e: the KV cache is state that stays resident in HBM (as in
+    # serving); a step's inputs from the host are the new queries and their
+    # selected block ids, its output the attention rows
+    host = {n: t.cpu().pin_memory() for n, t in (("q", q), ("idx", idx))}
     o_h = torch.empty(tuple(o.shape), dtype=o.dtype, pin_memory=True)
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = o_h.numel() * o_h.element_size()
     cu_qd, cu_kd = cu_q.to(dev), cu_k.to(dev)
 
     def e2e_step():
-        qd, kd, vd, ixd = (host[n].to(dev, non_blocking=True) for n in ("q", "k", "v", "idx"))
-        oo, _ = ops_b200.sparse_flash_attention(qd, kd, vd, ixd, cfg.bs, cu_seqlens=cu_qd, cu_seqlens_k=cu_kd,
+        qd, ixd = (host[n].to(dev, non_blocking=True) for n in ("q", "idx"))
+        oo, _ = ops_b200.sparse_flash_attention(qd, k, v, ixd, cfg.bs, cu_seqlens=cu_qd, cu_seqlens_k=cu_kd,
                                                 max_seqlen_q=1, max_seqlen_k=d["max_k"])
         o_h.copy_(oo, non_blocking=True)
 
     e2e_step()
     torch.cuda.synchronize()
     e_ms = 0.0
-    for _ in range(max(1, min(args.steps, 3))):
+    ne = max(1, min(steps, 3))
+    for _ in range(ne):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         e2e_step()
         b.record(stream)
         torch.cuda.synchronize()
         e_ms += a.elapsed_time(b)
-    e_ms /= max(1, min(args.steps, 3))
-    sampler.stop()
-    clocks = sampler.summary(t_wall0, t_wall1)
-    step_ms_max, e_ms_max, bytes_all = reduce_over_ranks(step_ms, e_ms, gathered, dev)
+    e_ms /= ne
+    clocks = None
+    if sampler is not None:
+        sampler.stop()
+        clocks = sampler.summary(t_wall0, t_wall1)
+    step_max, e_max, bytes_all = reduce_over_ranks(step_ms, e_ms, gathered, dev)
+    if rank != 0:
+        return None
+    _, hbm, kind = peaks()
+    gbs = gathered / (step_ms * 1e-3) / 1e9
+    line = {
+        "metric": DECODE_METRIC, "value": bytes_all / (step_max * 1e-3) / 1e9,
+        "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": step_max,
+        "higher_is_better": True, "scaling": "strong" if n_local != cfg.n_seqs else "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic", "config": config_dict(cfg, world, "units"),
+        "tflops": 2.0 * keys * G * (cfg.Dqk + cfg.Dv) / (step_ms * 1e-3) / 1e12,
+        "kernel_family": {1: "tcgen05", 2: "general"}.get(fam, str(fam)),
+        "roofline": {"bound": "hbm", "kernel": "fwd", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": gbs / hbm, "peak_kind": f"{kind} copy", "traffic": None,
+                     "algorithmic": "gathered K/V rows (selected keys x (Dqk + Dv) x 2 B) per launch"},
+        "e2e": {"value": bytes_all / (e_max * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e_max, "kv_cache": "resident in HBM"},
+        "gpu_launches": int(n1 - n0),
+    }
+    if clocks is not None:
+        line["clocks"] = clocks
+    return line
+
+
+def families(cfg, dev):
+    """Kernel families (fwd, bwd) the library picks for cfg's shape (asked on
+    a short copy of it: the choice depends on head dims, group size,
+    block_size and alignment, not on the length)."""
+    import torch
+    from ops_b200 import _lib
+    from ops_b200 import sfa as S
+    from ops_b200 import workloads as W
+    small = W.scaled(cfg, B=1, T=256)
+    d = W.make_inputs(small, dev, seed=0)
+    o = torch.empty(*d["q"].shape[:-1], cfg.Dv, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(d["q"].shape[:-1], dtype=torch.float32, device=dev)
+    c = S._Cfg(cfg.bs, cfg.scale, cfg.causal, False, small.T, small.T, _lib.SFA_DKV_AUTO, _lib.SFA_KERNEL_AUTO,
+               False)
+    P = S.build_params(d["q"], d["k"], d["v"], d["idx"], o, lse, c, None, None, None, d["do"],
+                       torch.empty_like(d["q"]), torch.empty_like(d["k"]), torch.empty_like(d["v"]), None)
+    lib = _lib.load()
+    names = {_lib.SFA_KERNEL_TCGEN05: "tcgen05", _lib.SFA_KERNEL_GENERAL: "general"}
+    return tuple(names.get(lib.sfa_select_kernel(ctypes.byref(P), b), "unsupported") for b in (0, 1))
+
+
+def compact(line, cpu):
+    """A secondary configuration's entry in the primary line."""
+    keys = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "config", "kernel_family", "roofline",
+            "e2e", "kernels", "pct_bf16_peak", "tflops", "gpu_launches")
+    out = {k: line[k] for k in keys if k in line}
+    out["cpu_baseline"] = cpu
+    return out
+
+
+def run_ours(args, cfg):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from ops_b200 import workloads as W
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    split = resolve_split(args, cfg, world)
+    if cfg.fwd_only:
+        line = measure_decode(args, cfg, world, rank, dev, args.steps, args.warmup, True)
+    else:
+        line = measure_config(args, cfg, world, rank, dev, split, args.steps, args.warmup, True)
+    others = []
+    if world == 1 and args.configs != "none":
+        others = [c for c in args.configs.split(",") if c and c != cfg.name]
+    extra = {}
+    for name in others:
+        sub_cfg = W.CONFIGS[name]
+        torch.cuda.empty_cache()
+        if not sub_cfg.fwd_only and sub_cfg.T > 4096 and "general" in families(sub_cfg, dev):
+            # the CUDA-core family would take minutes per step at full size
+            sub_cfg = W.scaled(sub_cfg, T=2048)
+        if sub_cfg.fwd_only:
+            sub = measure_decode(args, sub_cfg, 1, 0, dev, 5, 3, False)
+        else:
+            sub = measure_config(args, sub_cfg, 1, 0, dev, "none", 3, 3, False)
+        extra[name] = (sub, None if args.no_cpu else cpu_baseline(sub_cfg, reps=1))
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
         return
-    hbm = None
-    try:
-        hbm = float(json.load(open(os.path.join(os.path.dirname(os.path.abspath(__file__)),
-                                                "MEASURED_PEAKS.json")))["hbm_gbs"])
-        hbm_kind = "measured copy"
-    except Exception:
-        hbm, hbm_kind = 6650.0, "fallback"
-    gbs = gathered / (step_ms * 1e-3) / 1e9
-    line = {
-        "metric": "SFA decode forward GB/s (gathered K/V rows), B200", "value": bytes_all / (step_ms_max * 1e-3) / 1e9,
-        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms_max,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{cfg.name}: varlen decode forward, {cfg.n_seqs} sequences/rank x 1 query, kv "
-                               f"lengths U[{cfg.kv_min}, {cfg.kv_max}], Hq={cfg.Hq}, Hk={cfg.Hk}, Dqk={cfg.Dqk}, "
-                               f"Dv={cfg.Dv}, block_size={cfg.bs}, S={cfg.S} uniform blocks, q/k/v ~ N(0,1)",
-                   "global_batch": cfg.n_seqs * world, "parallelism": f"dp{world} (independent sequence shards)",
-                   "l2": "flushed between timed steps (256 MiB memset)"},
-        "tflops": flops / (step_ms * 1e-3) / 1e12,
-        "kernel_family": {1: "tcgen05", 2: "general"}.get(fam, str(fam)),
-        "roofline": {"bound": "hbm", "kernel": "fwd", "achieved": gbs, "peak": hbm, "unit": "GB/s",
-                     "frac": gbs / hbm, "peak_kind": hbm_kind, "traffic": None},
-        "e2e": {"value": bytes_all / (e_ms_max * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e_ms_max},
-        "clocks": clocks,
-        "gpu_launches": int(n1 - n0),
-    }
+    if world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(cfg)
+    if extra:
+        line["configs"] = {n: compact(s, c) for n, (s, c) in extra.items()}
     print(json.dumps(line), flush=True)
 
 
@@ -577,18 +812,21 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c2")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--batch", type=int, default=0, help="override the per-rank batch (profiling runs)")
+    ap.add_argument("--configs", default="c1,c3,c4,c5",
+                    help="secondary configurations measured after the primary one at N=1 ('none' to skip)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline samples")
+    ap.add_argument("--batch", type=int, default=0, help="override the batch (profiling runs)")
     ap.add_argument("--seq", type=int, default=0, help="override the sequence length (scaled secondary configs)")
     ap.add_argument("--dq-mode", choices=["auto", "separate", "fused"], default="auto",
                     help="backward dQ plan (profiling runs): its own query-centric pass or fused into dK/dV")
     ap.add_argument("--balance", choices=["pairs", "cost"], default="cost",
                     help="--split query: balance rows by selected pairs, or by a cost that also counts the "
                          "dK/dV pass's jobs and batches (ops_b200/shard.py row_cost)")
-    ap.add_argument("--split", choices=["none", "query"], default="none",
-                    help="with N > 1: 'query' splits one batch's query rows over the ranks (strong scaling, "
-                         "for configurations with fewer (batch, kv head) units than ranks)")
+    ap.add_argument("--split", choices=["auto", "units", "batch", "query"], default="auto",
+                    help="with N > 1: 'units' deals (batch, kv head) units out to the ranks (strong scaling; "
+                         "the default when they divide evenly), 'query' splits one batch's query rows "
+                         "(strong scaling with one reduce-scatter; the default otherwise), 'batch' gives each "
+                         "rank its own batch (weak scaling)")
     args = ap.parse_args()
     from ops_b200 import workloads as W
     cfg = W.CONFIGS[args.config]
@@ -596,13 +834,8 @@ def main():
         cfg = W.scaled(cfg, B=args.batch)
     if args.seq:
         cfg = W.scaled(cfg, T=args.seq)
-    if cfg.fwd_only:
-        if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "forward-only decode config; the reference arm "
-                              "times the fwd+bwd configurations"}))
-            return
-        run_decode(args, cfg)
-        return
+    if args.batch or args.seq:
+        args.configs = "none"
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

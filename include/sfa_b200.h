@@ -133,6 +133,20 @@ const char* sfa_last_error_string(void);
  * threads); a caller brackets a region with two reads to count its launches. */
 unsigned long long sfa_kernel_launches(void);
 
+/* Launch trace, for benchmarks that time each kernel with CUDA events (no
+ * counterpart in the reference).  `events` holds n_events cudaEvent_t handles
+ * (as void*) created by the caller; while it is set, every kernel or memset the
+ * library enqueues from the calling thread is followed by a cudaEventRecord of
+ * the next unused event on the same stream, so the time between consecutive
+ * events (the first one against an event the caller records before its call)
+ * is one operation.  sfa_launch_trace_count() gives how many events were
+ * recorded and sfa_launch_trace_name(i) the operation event i closes.  Passing
+ * NULL stops tracing; a new call restarts the count.  The events must outlive
+ * the trace. */
+int sfa_launch_trace(void* const* events, int n_events);
+int sfa_launch_trace_count(void);
+const char* sfa_launch_trace_name(int i);
+
 /* Which kernel family a call with these params would launch (SFA_KERNEL_*), or
  * a negative error code if the shape is unsupported. */
 int sfa_select_kernel(const SfaParams* p, int is_backward);
@@ -183,7 +197,9 @@ int sfa_bwd_dkdv(const SfaParams* p, void* workspace, size_t workspace_bytes, vo
  * 32 MiB are refused with SFA_ERR_WORKSPACE before anything is launched.  The first call on a device
  * looks up the array's device address; make it before any stream capture.
  * Calls share the array: calls that overlap on the GPU race and must be
- * serialised by the caller. */
+ * serialised by the caller.  The looked-up address is kept for the life of the
+ * process: after a device reset (cudaDeviceReset, or a primary-context reset)
+ * the library must be reloaded before this entry point is called again. */
 int sfa_bwd_noalloc(const SfaParams* p, void* stream);
 
 /* Inverted index alone (for tests): for every (sequence, kv head, block) the

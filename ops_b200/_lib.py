@@ -68,6 +68,9 @@ EXPORTS = {
     "sfa_device_status": ([_c_void_p, ctypes.POINTER(_i32)], _i32),
     "sfa_selftest_wait_timeout": ([_c_void_p, ctypes.c_uint32], _i32),
     "sfa_reset_device_status": ([_c_void_p], _i32),
+    "sfa_launch_trace": ([ctypes.POINTER(_c_void_p), _i32], _i32),
+    "sfa_launch_trace_count": ([], _i32),
+    "sfa_launch_trace_name": ([_i32], ctypes.c_char_p),
 }
 
 _lib = None

@@ -77,7 +77,31 @@ int device_cc() {
 }
 
 static std::atomic<unsigned long long> g_launches{0};
-void note_launch(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+
+// Launch trace (sfa_launch_trace): while a caller has handed in events, each
+// kernel or memset this thread enqueues is followed by a record of the next
+// event on the same stream, so consecutive events bracket one operation.
+struct LaunchTrace {
+  void* const* events = nullptr;
+  int n = 0;
+  int count = 0;
+  const char* names[64] = {nullptr};
+};
+static thread_local LaunchTrace g_trace;
+
+static void trace_point(const char* name, cudaStream_t st) {
+  if (!g_trace.events || g_trace.count >= g_trace.n) return;
+  cudaEventRecord(reinterpret_cast<cudaEvent_t>(g_trace.events[g_trace.count]), st);
+  if (g_trace.count < 64) g_trace.names[g_trace.count] = name;
+  ++g_trace.count;
+}
+
+void note_launch(const char* name, cudaStream_t st) {
+  g_launches.fetch_add(1ull, std::memory_order_relaxed);
+  trace_point(name, st);
+}
+
+void note_memset(const char* name, cudaStream_t st) { trace_point(name, st); }
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -319,6 +343,7 @@ int sfa_bwd_dq(const SfaParams* p, void* workspace, size_t workspace_bytes, void
   if (L.fused_dq) {
     // the dK/dV pass accumulates dQ: start from zero
     e = cudaMemsetAsync(ws + L.dq_acc, 0, sizeof(float) * (size_t)num_rows_host(*p) * p->h_q * p->d_qk, st);
+    note_memset("memset_dq_acc", st);
   } else if (fam == SFA_KERNEL_TCGEN05) {
     e = launch_bwd_dq_tc(*p, delta, st);
   } else {
@@ -328,6 +353,7 @@ int sfa_bwd_dq(const SfaParams* p, void* workspace, size_t workspace_bytes, void
     const int64_t kvr = kv_rows_host(*p);
     e = cudaMemsetAsync(dk_acc, 0, sizeof(float) * kvr * p->h_kv * p->d_qk, st);
     if (e == cudaSuccess && dv_acc != dk_acc) e = cudaMemsetAsync(dv_acc, 0, sizeof(float) * kvr * p->h_kv * p->d_v, st);
+    note_memset("memset_dkdv_acc", st);
     if (e == cudaSuccess) e = launch_bwd_general(*p, delta, dk_acc, dv_acc, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "sfa_bwd_dq");
@@ -359,6 +385,7 @@ int sfa_bwd_dkdv(const SfaParams* p, void* workspace, size_t workspace_bytes, vo
       e = cudaMemsetAsync(dk_acc, 0, sizeof(float) * kvr * p->h_kv * p->d_qk, st);
       if (e == cudaSuccess && dv_acc != dk_acc)
         e = cudaMemsetAsync(dv_acc, 0, sizeof(float) * kvr * p->h_kv * p->d_v, st);
+      note_memset("memset_dkdv_acc", st);
       SfaParams q = *p;
       q.dq = nullptr;
       if (e == cudaSuccess) e = launch_bwd_general(q, delta, dk_acc, dv_acc, st);
@@ -419,6 +446,21 @@ int sfa_selftest_wait_timeout(void* stream, uint32_t limit_us) {
   cudaError_t e = launch_wait_probe(limit_us, ptr, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "sfa_selftest_wait_timeout");
   return SFA_OK;
+}
+
+int sfa_launch_trace(void* const* events, int n_events) {
+  if (events != nullptr && n_events <= 0) return fail(SFA_ERR_INVALID_ARGUMENT, "n_events must be positive");
+  g_trace.events = events;
+  g_trace.n = events ? n_events : 0;
+  g_trace.count = 0;
+  return SFA_OK;
+}
+
+int sfa_launch_trace_count(void) { return g_trace.count; }
+
+const char* sfa_launch_trace_name(int i) {
+  if (i < 0 || i >= g_trace.count || i >= 64 || !g_trace.names[i]) return "";
+  return g_trace.names[i];
 }
 
 int sfa_reset_device_status(void* stream) {

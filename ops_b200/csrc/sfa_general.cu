@@ -267,7 +267,7 @@ cudaError_t launch_fwd_general(const SfaParams& p, cudaStream_t st) {
   dim3 grid(num_rows_host(p), p.h_kv, (G + HG - 1) / HG);
   if (grid.x == 0) return cudaSuccess;
   fwd_general_kernel<<<grid, kGenThreads, smem, st>>>(p, HG);
-  note_launch();
+  note_launch("fwd_general", st);
   return cudaGetLastError();
 }
 
@@ -281,7 +281,7 @@ cudaError_t launch_bwd_general(const SfaParams& p, const float* delta, float* dk
   dim3 grid(num_rows_host(p), p.h_kv, (G + HG - 1) / HG);
   if (grid.x == 0) return cudaSuccess;
   bwd_general_kernel<<<grid, kGenThreads, smem, st>>>(p, HG, delta, dk_acc, dv_acc);
-  note_launch();
+  note_launch("bwd_general", st);
   return cudaGetLastError();
 }
 

@@ -82,8 +82,11 @@ cudaError_t launch_bwd_dkdv_tc(const SfaParams& p, const BwdLayout& L, char* ws,
 int device_sm_count();
 int device_cc();
 
-// Count of kernels this library has enqueued (reported by sfa_kernel_launches).
-void note_launch(int n = 1);
+// Count of kernels this library has enqueued (reported by sfa_kernel_launches);
+// also a point of the calling thread's launch trace (sfa_launch_trace).
+void note_launch(const char* name, cudaStream_t st);
+// A memset enqueued by the library: a trace point, not a kernel of its own.
+void note_memset(const char* name, cudaStream_t st);
 
 // Record `msg` for sfa_last_error_string() and return `code`.
 int report_error(int code, const std::string& msg);

@@ -186,13 +186,13 @@ cudaError_t launch_preprocess(const SfaParams& p, float* delta, float* dsink_par
   } else {
     preprocess_kernel<<<pre_ctas, kPreThreads, smem, st>>>(p, delta, part);
   }
-  note_launch();
+  note_launch("preprocess", st);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (p.dsink) {
     if (!p.attn_sink) return cudaMemsetAsync(p.dsink, 0, sizeof(float) * p.h_q, st);
     dsink_reduce_kernel<<<(p.h_q + 7) / 8, 256, 0, st>>>(part, pre_ctas, p.h_q, p.dsink);
-    note_launch();
+    note_launch("dsink_reduce", st);
     e = cudaGetLastError();
   }
   return e;
@@ -224,12 +224,12 @@ cudaError_t launch_convert_dkdv(const SfaParams& p, const float* dk_acc, const f
   convert_kernel<<<grid, 256, 0, st>>>(p, dk_acc, p.d_qk, p.dk_sb, p.dk_st, p.dk_sh,
                                        reinterpret_cast<__nv_bfloat16*>(p.dk),
                                        (shared_kv && dv_acc != dk_acc) ? dv_acc : nullptr);
-  note_launch();
+  note_launch("convert_dk", st);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || shared_kv) return e;
   convert_kernel<<<grid, 256, 0, st>>>(p, dv_acc, p.d_v, p.dv_sb, p.dv_st, p.dv_sh,
                                        reinterpret_cast<__nv_bfloat16*>(p.dv), nullptr);
-  note_launch();
+  note_launch("convert_dv", st);
   return cudaGetLastError();
 }
 
@@ -306,7 +306,7 @@ cudaError_t launch_reduce_dkdv_ranges(const SfaParams& p, const BwdLayout& L, co
   reduce_dkdv_ranges_kernel<<<nlists, 256, 0, st>>>(
       p, reinterpret_cast<const float*>(ws + L.dkv_part), reinterpret_cast<const int32_t*>(ws + L.inv_cursor),
       reinterpret_cast<const int32_t*>(ws + L.inv_offsets), L.nblk, L.inv_nsub, L.sub_per_range, L.nranges);
-  note_launch();
+  note_launch("reduce_dkdv_ranges", st);
   return cudaGetLastError();
 }
 
@@ -355,7 +355,7 @@ cudaError_t launch_convert_dq(const SfaParams& p, const float* dq_acc, cudaStrea
     convert_dq_kernel<true><<<grid, 256, 0, st>>>(p, dq_acc);
   else
     convert_dq_kernel<false><<<grid, 256, 0, st>>>(p, dq_acc);
-  note_launch();
+  note_launch("convert_dq", st);
   return cudaGetLastError();
 }
 
@@ -537,25 +537,25 @@ cudaError_t launch_inverted_index(const SfaParams& p, const BwdLayout& L, char* 
   if (e != cudaSuccess) return e;
   dim3 grid(ctas_x, L.units);
   inv_pass_kernel<false><<<grid, kInvWarps * 32, smem, st>>>(p, nblk, nsub_pad, counts, entries);
-  note_launch();
+  note_launch("index_count", st);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   scan_tile_sums<<<(unsigned)ntiles, kScanThreads, 0, st>>>(counts, ncount, tile_sums);
-  note_launch();
+  note_launch("index_scan_tiles", st);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   scan_sums_single<<<1, 1024, 0, st>>>(tile_sums, (int)ntiles, total);
-  note_launch();
+  note_launch("index_scan_sums", st);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   scan_tiles<<<(unsigned)ntiles, kScanThreads, 0, st>>>(counts, ncount, tile_sums);
-  note_launch();
+  note_launch("index_scan_apply", st);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   const int64_t nlists = (int64_t)L.units * nblk;
   const int64_t gblocks = (nlists + 1 + 255) / 256;
   gather_offsets<<<(unsigned)(gblocks < 4096 ? gblocks : 4096), 256, 0, st>>>(
       counts, nlists, nsub_pad, total, offsets);
-  note_launch();
+  note_launch("index_offsets", st);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   inv_pass_kernel<true><<<grid, kInvWarps * 32, smem, st>>>(p, nblk, nsub_pad, counts, entries);
-  note_launch();
+  note_launch("index_fill", st);
   return cudaGetLastError();
 }
 

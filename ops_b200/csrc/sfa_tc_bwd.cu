@@ -502,7 +502,7 @@ cudaError_t launch(const SfaParams& p, const float* delta, cudaStream_t stream) 
   if (e != cudaSuccess) return e;
   const int grid = a.nitems < device_sm_count() ? a.nitems : device_sm_count();
   sfa_bwd_dq_tc_kernel<D><<<grid, kThreads, smem, stream>>>(a, tq, tdo, tk, tv);
-  note_launch();
+  note_launch("bwd_dq_tc", stream);
   return cudaGetLastError();
 }
 
@@ -1172,7 +1172,7 @@ cudaError_t launch(const SfaParams& p, const BwdLayout& L, char* ws, const float
   if (e != cudaSuccess) return e;
   const int grid = a.nitems < device_sm_count() ? a.nitems : device_sm_count();
   sfa_bwd_dkdv_tc_kernel<D, kDQ><<<grid, kDQ ? kThreadsDQ : kThreads, smem, stream>>>(a, tq, tdo, tk, tv);
-  note_launch();
+  note_launch("bwd_dkdv_tc", stream);
   return cudaGetLastError();
 }
 

@@ -770,7 +770,7 @@ cudaError_t launch(const SfaParams& p, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   const int grid = a.nitems < device_sm_count() ? a.nitems : device_sm_count();
   sfa_fwd_tc_kernel<D><<<grid, kThreads, smem, st>>>(a, tq, tk, tv);
-  note_launch();
+  note_launch("fwd_tc", st);
   return cudaGetLastError();
 }
 

@@ -18,7 +18,9 @@ index tensor or a non-positive topk, ``SFA.py:53``, ``SFA.py:64``); everything
 else the C ABI rejects surfaces as ``ValueError`` (bad arguments) or
 ``ops_b200.SfaError``.  Unlike the reference, neither direction synchronises the
 host with the device (no ``_effective_topk``, ``SFA.py:62-66``), and indices may
-be padded with -1 in any slot.
+be padded with -1 in any slot.  The one exception: a varlen call that leaves
+``max_seqlen_q`` / ``max_seqlen_k`` unset reads them from ``cu_seqlens`` on the
+host (one device->host copy each); pass them to keep the call sync-free.
 """
 from __future__ import annotations
 
@@ -188,7 +190,8 @@ def sparse_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bl
     Dense: ``q [B,T,Hq,Dqk]``, ``k [B,Tk,Hk,Dqk]``, ``v [B,Tk,Hk,Dv]``,
     ``block_indices [B,T,Hk,S]``.  Varlen: drop the batch axis and pass
     ``cu_seqlens`` (query offsets; also the kv offsets unless ``cu_seqlens_k``
-    is given).  ``max_seqlen_q/k`` avoid a host sync for varlen.  ``lse`` is the
+    is given).  Varlen calls should pass ``max_seqlen_q/k``: left unset, they are
+    read back from ``cu_seqlens`` with a device->host sync.  ``lse`` is the
     natural-log log-sum-exp ``[.., Hq]`` (fp32); it carries no gradient.
     ``attn_sink`` (``[Hq]`` fp32) adds ``exp(sink)`` to every denominator.
     If ``k is v`` their rows are shared and one gradient ``dk + dv`` flows back.

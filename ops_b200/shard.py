@@ -58,7 +58,13 @@ def row_cost(block_indices: torch.Tensor, block_size: int, kv_len: int, causal: 
     default weights are B200 times at D = 128 (ms per pair of the forward, per
     batch and per job of the pass), fitted with :func:`fit_cost` to the two
     ranks of a measured two-GPU split of one 65536-token sequence (4 kv heads,
-    32 selected 64-key blocks a row).  Returns float64 per row."""
+    32 selected 64-key blocks a row).  Returns float64 per row.
+
+    It is an approximation of what the ranks run: jobs are counted in row
+    ranges from global row 0, while each rank's kernel counts its ranges from
+    its own first row (``range_units`` models that), and long sequences get
+    longer ranges in the kernel (at most 64 ranges a unit).  ``range_units`` on
+    the chosen ranges gives the exact per-rank counts to check a split."""
     B, T, Hk, S = block_indices.shape
     e = block_indices.to(torch.int64)
     nblk = (kv_len + block_size - 1) // block_size
@@ -116,15 +122,29 @@ def range_units(block_indices: torch.Tensor, block_size: int, ranges: List[Tuple
 def fit_cost(units: List[Tuple[int, int, int]], fwd_ms: List[float], dkdv_ms: List[float]) -> dict:
     """Weights for :func:`row_cost` from a measured split: per-rank (pairs,
     batches, jobs) from :func:`range_units` and the ranks' forward and dK/dV
-    stage times (the bench line's ``stages_ms_per_rank``).  The forward is
+    kernel times (the bench line's per-rank kernel times).  The forward is
     taken as proportional to pairs; the dK/dV pass as a per-batch plus a
-    per-job time, solved by least squares (two or more ranks)."""
+    per-job time, solved by least squares.
+
+    Two ranks give two equations for two unknowns: the fit is exact
+    (``residual`` 0) and says nothing about how well the model predicts; more
+    ranks (or several splits' ranks together) over-determine it.  Returns the
+    weights plus ``residual`` (RMS, ms) and ``rank`` of the system; raises
+    ``ValueError`` when the system is singular or a weight comes out negative
+    (the model does not describe the measurements)."""
     pairs = torch.tensor([u[0] for u in units], dtype=torch.float64)
     A = torch.tensor([[u[1], u[2]] for u in units], dtype=torch.float64)
     y = torch.tensor(dkdv_ms, dtype=torch.float64)
     per_pair = float(sum(fwd_ms)) / float(pairs.sum())
+    rank = int(torch.linalg.matrix_rank(A))
+    if rank < 2:
+        raise ValueError("fit_cost: the ranks' (batches, jobs) counts are linearly dependent")
     sol = torch.linalg.lstsq(A, y[:, None]).solution.flatten()
-    return {"per_pair": per_pair, "per_batch": float(sol[0]), "per_job": float(sol[1])}
+    if float(sol.min()) < 0.0 or per_pair < 0.0:
+        raise ValueError(f"fit_cost: negative weight (per_batch {float(sol[0]):.3g}, per_job {float(sol[1]):.3g})")
+    resid = float(((A @ sol - y) ** 2).mean().sqrt())
+    return {"per_pair": per_pair, "per_batch": float(sol[0]), "per_job": float(sol[1]), "residual": resid,
+            "rank": rank, "exact": len(units) == 2}
 
 
 def query_ranges(work: torch.Tensor, world: int) -> List[Tuple[int, int]]:

@@ -8,9 +8,10 @@ device->host sync on every call and every new value recompiles the kernels
 
 On sm_100a the launch table lives in the C library (``sfa_select_kernel``) and
 is keyed on static shape only — (D_qk, D_v, group size, block_size, alignment)
-— so it needs no sync.  The tile constants of each family are listed in
-``B200_TILES``.  The reference-compatible helpers below keep the reference's
-bucket semantics and errors for callers that use them directly.
+— so it needs no sync.  ``select_kernel`` asks it which family a call runs;
+the tile constants live with each kernel.  The reference-compatible helpers
+below keep the reference's bucket semantics and errors for callers that use
+them directly.
 """
 from __future__ import annotations
 
@@ -60,16 +61,6 @@ def effective_topk(topk_idxs: torch.Tensor) -> int:
         raise ValueError("topk_idxs tensor is empty. Cannot determine effective topk.")
     return int((topk_idxs >= 0).sum(dim=-1).max().item())
 
-
-# Tile constants of the sm_100a kernel families (mirrors the C++ launch table).
-B200_TILES = {
-    "tcgen05.fwd": dict(keys_per_mma=128, heads_n=16, kv_sub_block=64, segment_keys=1024,
-                        note="swap-AB: S^T = K.Q^T (M=128 keys, N=16 heads), O^T += V^T.P^T"),
-    "tcgen05.dq": dict(keys_per_mma=128, heads_n=16, note="swap-AB: S^T, dP^T, dQ^T += K^T.dS^T"),
-    "tcgen05.dkdv": dict(rows_per_mma=128, keys_n=64,
-                         note="key-centric over the inverted index: 8 queries x 16 heads = 128 rows"),
-    "general": dict(heads_per_cta=16, keys_per_chunk=16, note="CUDA cores, any shape"),
-}
 
 FAMILY_NAMES = {_lib.SFA_KERNEL_TCGEN05: "tcgen05", _lib.SFA_KERNEL_GENERAL: "general"}
 

@@ -9,7 +9,8 @@ Configurations (same numbering as the benchmark):
   c1  B1  T1024  Hq16 Hk1 D64       bs64 S8   causal, uniform w/o replacement
   c2  B4  T8192  Hq64 Hk4 D128      bs64 S16  causal, current block always in
   c3  B1  T65536 Hq64 Hk4 D128      bs64 S32  half the mass on the last 8 blocks
-  c4  B1  T32768 Hq128 Hk1 Dqk576 Dv512 bs1 k2048 token-level, causal
+  c4  B1  T32768 Hq128 Hk1 Dqk576 Dv512 bs1 k2048 token-level, causal; one
+      latent kv tensor (k), v = k[..., :512] (a view)
   c5  128 seqs, kv U[4096,131072], 1 query each, Hq64 Hk8 D128 bs64 S32 (forward only)
 """
 from __future__ import annotations
@@ -154,11 +155,33 @@ def make_inputs(cfg: Config, device="cpu", seed=0, dtype=torch.bfloat16, with_do
     gen = torch.Generator(device=device).manual_seed(seed)
     q = torch.randn(cfg.B, cfg.T, cfg.Hq, cfg.Dqk, generator=gen, device=device).to(dtype)
     k = torch.randn(cfg.B, cfg.T, cfg.Hk, cfg.Dqk, generator=gen, device=device).to(dtype)
-    v = torch.randn(cfg.B, cfg.T, cfg.Hk, cfg.Dv, generator=gen, device=device).to(dtype)
+    if cfg.mode == "token" and cfg.Dv <= cfg.Dqk:
+        # MLA-style: one latent kv tensor; v is its first Dv dims (a view of k)
+        v = k[..., :cfg.Dv]
+    else:
+        v = torch.randn(cfg.B, cfg.T, cfg.Hk, cfg.Dv, generator=gen, device=device).to(dtype)
     d = dict(q=q, k=k, v=v, idx=make_indices(cfg, device, seed))
     if with_do:
         d["do"] = torch.randn(cfg.B, cfg.T, cfg.Hq, cfg.Dv, generator=gen, device=device).to(dtype)
     return d
+
+
+@dataclass(frozen=True)
+class Flops:
+    """Algorithmic FLOPs of one fwd+bwd step (recomputation not counted)."""
+    fwd: float
+    bwd: float
+
+    @property
+    def total(self) -> float:
+        return self.fwd + self.bwd
+
+
+def sfa_flops(pairs_qhead: int, d_qk: int, d_v: int) -> Flops:
+    """FLOPs over P selected (query-head, key) pairs: fwd = 2P(Dqk+Dv) (QK^T and
+    PV, SFA.py:425, 456); bwd = 2P(3Dqk+2Dv) (S, dP, dQ, dK, dV: SFA.py:678-679,
+    708, 831, 841)."""
+    return Flops(2.0 * pairs_qhead * (d_qk + d_v), 2.0 * pairs_qhead * (3 * d_qk + 2 * d_v))
 
 
 def count_pairs(idx: torch.Tensor, bs: int, q_len: int, kv_len: int, causal: bool = True,

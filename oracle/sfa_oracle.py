@@ -81,18 +81,21 @@ def key_table(block_indices: torch.Tensor, block_size: int, q_pos: torch.Tensor,
 # --------------------------------------------------------------------------
 # one sequence
 # --------------------------------------------------------------------------
-def _seq_forward(q, k, v, idx, block_size, scale, sink, causal, chunk=256):
+def _seq_forward(q, k, v, idx, block_size, scale, sink, causal, chunk=256, q_pos=None):
     """q [T,Hq,Dqk] k [Tk,Hk,Dqk] v [Tk,Hk,Dv] idx [T,Hk,S] -> o [T,Hq,Dv], lse [T,Hq].
 
     Restates the forward of ``_inner_fwd`` (``SFA.py:309-480``) with an exact
-    (non-online) softmax in fp32.
+    (non-online) softmax in fp32.  ``q_pos`` gives the rows' causal positions
+    when q holds a subset of a sequence's rows (default: the whole sequence,
+    bottom-right aligned).
     """
     T, Hq, _ = q.shape
     Tk, Hk, Dv = v.shape
     G = Hq // Hk
     o = torch.zeros(T, Hq, Dv, dtype=torch.float32)
     lse = torch.full((T, Hq), NEG_INF, dtype=torch.float32)
-    q_pos = torch.arange(T) + (Tk - T)
+    if q_pos is None:
+        q_pos = torch.arange(T) + (Tk - T)
     for hk in range(Hk):
         hs = slice(hk * G, (hk + 1) * G)
         keys, ok = key_table(idx[:, hk], block_size, q_pos, Tk, causal)
@@ -117,9 +120,10 @@ def _seq_forward(q, k, v, idx, block_size, scale, sink, causal, chunk=256):
     return o, lse
 
 
-def _seq_backward(q, k, v, idx, block_size, scale, sink, causal, o, lse, do, chunk=256):
+def _seq_backward(q, k, v, idx, block_size, scale, sink, causal, o, lse, do, chunk=256, q_pos=None):
     """Gradients of one sequence; follows ``SFA.py:590-1002`` (delta, dq, dsink)
-    and ``SFA.py:719-853`` (dk/dv), with k and v kept separate."""
+    and ``SFA.py:719-853`` (dk/dv), with k and v kept separate.  With a subset
+    of rows (``q_pos`` set), dk/dv hold those rows' contributions only."""
     T, Hq, Dqk = q.shape
     Tk, Hk, Dv = v.shape
     G = Hq // Hk
@@ -127,7 +131,8 @@ def _seq_backward(q, k, v, idx, block_size, scale, sink, causal, o, lse, do, chu
     dk = torch.zeros(Tk, Hk, Dqk, dtype=torch.float32)
     dv = torch.zeros(Tk, Hk, Dv, dtype=torch.float32)
     dsink = torch.zeros(Hq, dtype=torch.float32)
-    q_pos = torch.arange(T) + (Tk - T)
+    if q_pos is None:
+        q_pos = torch.arange(T) + (Tk - T)
     delta = (o.float() * do.float()).sum(-1)                          # [T,Hq]
     lsafe_all = torch.where(torch.isfinite(lse), lse, torch.zeros_like(lse))
     for hk in range(Hk):
@@ -210,6 +215,28 @@ def sfa_backward(q, k, v, block_indices, o, lse, do, block_size=64, scale=None, 
             dq[sq], dk[sk], dv[sk] = r[0], r[1], r[2]
             dsink += r[3]
     return dq, dk, dv, (dsink if attn_sink is not None else None)
+
+
+def sfa_rows_forward(q_rows, k, v, idx_rows, q_pos, block_size=64, scale=None, attn_sink=None, causal=True):
+    """fp32 forward of selected query rows of one sequence: q_rows [n,Hq,Dqk],
+    k [Tk,Hk,Dqk], v [Tk,Hk,Dv], idx_rows [n,Hk,S], q_pos [n] causal positions.
+    Each row depends only on its own indices, so the result equals those rows
+    of the full-sequence forward.  Returns (o, lse)."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(q_rows.shape[-1])
+    return _seq_forward(q_rows, k, v, idx_rows, block_size, scale, attn_sink, causal,
+                        q_pos=torch.as_tensor(q_pos, dtype=torch.int64))
+
+
+def sfa_rows_backward(q_rows, k, v, idx_rows, q_pos, o_rows, lse_rows, do_rows, block_size=64, scale=None,
+                      attn_sink=None, causal=True):
+    """Gradients from selected query rows of one sequence: dq of those rows
+    (exact), and the rows' contributions to dk/dv (exact for every key whose
+    selecting rows are all among them).  Returns (dq, dk, dv, dsink_part)."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(q_rows.shape[-1])
+    return _seq_backward(q_rows, k, v, idx_rows, block_size, scale, attn_sink, causal, o_rows, lse_rows,
+                         do_rows, q_pos=torch.as_tensor(q_pos, dtype=torch.int64))
 
 
 def reference_compat_forward(q, kv, attn_sink, topk_idxs, sm_scale):

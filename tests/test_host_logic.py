@@ -63,8 +63,11 @@ def test_pair_count_matches_oracle(name):
     a = W.count_pairs(idx, cfg.bs, cfg.T, cfg.T)
     b = O.selected_pairs(idx, cfg.bs, cfg.T, cfg.T)
     assert a == b
-    f = O.sfa_flops(a * cfg.Hq // cfg.Hk, cfg.Dqk, cfg.Dv)
+    f = W.sfa_flops(a * cfg.Hq // cfg.Hk, cfg.Dqk, cfg.Dv)
     assert 4.5e9 < f.total < 6e9   # about 5.4 GFLOP for config 1
+    # the bench's formula and the oracle's accounting agree
+    g = O.sfa_flops(a * cfg.Hq // cfg.Hk, cfg.Dqk, cfg.Dv)
+    assert (f.fwd, f.bwd) == (g.fwd, g.bwd)
 
 
 def test_reference_tiling_buckets():

@@ -127,3 +127,17 @@ def test_default_cost_weights_come_from_the_recorded_split():
                 if k in ("per_pair", "per_batch", "per_job")}
     for k, v in defaults.items():
         assert abs(fit[k] - v) <= 0.02 * v, (k, fit[k], v)
+    # two ranks: an exact solve, flagged as such
+    assert fit["exact"] and fit["rank"] == 2 and fit["residual"] < 1e-9
+
+
+def test_fit_cost_rejects_models_that_do_not_fit():
+    # a negative per-job time (more jobs, less time) is refused
+    with pytest.raises(ValueError):
+        shard.fit_cost([(100, 10, 5), (100, 10, 50)], [1.0, 1.0], [2.0, 1.0])
+    # dependent counts (one rank a multiple of the other) are refused
+    with pytest.raises(ValueError):
+        shard.fit_cost([(100, 10, 5), (200, 20, 10)], [1.0, 2.0], [1.0, 2.0])
+    # three ranks over-determine the fit: a residual is reported
+    f = shard.fit_cost([(100, 10, 5), (100, 12, 9), (100, 20, 6)], [1.0, 1.0, 1.0], [1.0, 1.5, 1.6])
+    assert f["rank"] == 2 and not f["exact"] and f["residual"] >= 0.0

@@ -44,15 +44,23 @@ def _snapshot(grads):
     return {n: t.clone() for n, t in grads.items()}
 
 
-@pytest.mark.parametrize("kernel,cfg,bs", [
-    (_lib.SFA_KERNEL_TCGEN05, W.scaled(W.CONFIGS["c2"], B=1, T=2048, Hq=32, Hk=2, S=16), 64),
-    (_lib.SFA_KERNEL_GENERAL, W.scaled(W.CONFIGS["c1"], T=512), 64),
-], ids=["tcgen05_inverted", "general_atomic"])
-def test_noalloc_backward_matches_workspace_backward(kernel, cfg, bs):
+@pytest.mark.parametrize("kernel,cfg,bs,fused_fits", [
+    (_lib.SFA_KERNEL_TCGEN05, W.scaled(W.CONFIGS["c2"], B=1, T=2048, Hq=32, Hk=2, S=16), 64, False),
+    (_lib.SFA_KERNEL_TCGEN05, W.scaled(W.CONFIGS["c2"], B=1, T=1024, Hq=16, Hk=1, S=8), 64, True),
+    (_lib.SFA_KERNEL_GENERAL, W.scaled(W.CONFIGS["c1"], T=512), 64, False),
+], ids=["tcgen05_separate_dq", "tcgen05_fused_dq", "general_atomic"])
+def test_noalloc_backward_matches_workspace_backward(kernel, cfg, bs, fused_fits):
     lib = _lib.load()
     st = torch.cuda.current_stream().cuda_stream
     P, grads, _keep = _problem(cfg, bs, kernel, seed=21)
     nbytes = lib.sfa_bwd_workspace_bytes(ctypes.byref(P))
+    if kernel == _lib.SFA_KERNEL_TCGEN05:
+        # the first case needs the separate dQ pass to fit the static array;
+        # the second keeps the fused dQ (its accumulator fits as well)
+        dkv, dq = ctypes.c_int32(), ctypes.c_int32()
+        lib.sfa_bwd_plan(ctypes.byref(P), ctypes.byref(dkv), ctypes.byref(dq))
+        assert dq.value == _lib.SFA_DQ_FUSED
+        assert (nbytes <= (32 << 20)) == fused_fits
     ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
     _lib.check(lib.sfa_bwd(ctypes.byref(P), ws.data_ptr(), nbytes, st), "sfa_bwd")
     ref = _snapshot(grads)
