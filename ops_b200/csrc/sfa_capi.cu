@@ -122,8 +122,11 @@ static int validate(const SfaParams* p, bool bwd) {
     return fail(SFA_ERR_INVALID_ARGUMENT, "cu_seqlens_q and cu_seqlens_k must both be set or both be NULL");
   if (p->cu_seqlens_q && (p->total_q < 0 || p->total_kv < 0))
     return fail(SFA_ERR_INVALID_ARGUMENT, "total_q / total_kv must be >= 0 for varlen");
-  if (bwd && p->dk == p->dv && (p->d_qk != p->d_v || p->k != p->v))
-    return fail(SFA_ERR_INVALID_ARGUMENT, "dk may alias dv only when k and v are the same tensor");
+  if (bwd && p->dk == p->dv &&
+      (p->k != p->v || p->d_v > p->d_qk || p->v_sb != p->k_sb || p->v_st != p->k_st || p->v_sh != p->k_sh ||
+       p->dv_sb != p->dk_sb || p->dv_st != p->dk_st || p->dv_sh != p->dk_sh))
+    return fail(SFA_ERR_INVALID_ARGUMENT,
+                "dk may alias dv only when v is k or its leading d_v dims (same pointer and strides)");
   if (bwd && p->dkv_mode != SFA_DKV_AUTO && p->dkv_mode != SFA_DKV_INVERTED && p->dkv_mode != SFA_DKV_ATOMIC)
     return fail(SFA_ERR_INVALID_ARGUMENT, "unknown dkv_mode");
   if (p->kernel != SFA_KERNEL_AUTO && p->kernel != SFA_KERNEL_TCGEN05 && p->kernel != SFA_KERNEL_GENERAL)
@@ -146,7 +149,11 @@ static bool general_supported(const SfaParams& p, bool bwd, std::string* why) {
 // Launch table: family for (shape, direction).
 static int select_family(const SfaParams& p, bool bwd, std::string* why) {
   const char* tc_why = "";
-  bool tc_ok = bwd ? tc_bwd_supported(p, &tc_why) : tc_fwd_supported(p, &tc_why);
+  bool tc_ok;
+  if (bwd)
+    tc_ok = tc_bwd_supported(p, &tc_why);
+  else
+    tc_ok = p.block_size == 1 ? tok_fwd_supported(p, &tc_why) : tc_fwd_supported(p, &tc_why);
   if (p.kernel == SFA_KERNEL_TCGEN05) {
     if (!tc_ok) { *why = std::string("tcgen05 family: ") + tc_why; return SFA_ERR_UNSUPPORTED; }
     return SFA_KERNEL_TCGEN05;
@@ -186,7 +193,7 @@ BwdLayout bwd_layout(const SfaParams& p, int family, int dkv_mode, int dq_mode) 
   if (L.atomic_dkv) {
     L.dk_acc = off;
     off = align256(off + sizeof(float) * kvr * p.h_kv * p.d_qk);
-    if (p.dk != p.dv) {
+    if (p.dk != p.dv || p.d_v != p.d_qk) {
       L.dv_acc = off;
       off = align256(off + sizeof(float) * kvr * p.h_kv * p.d_v);
     } else {
@@ -297,7 +304,8 @@ int sfa_fwd(const SfaParams* p, void* workspace, size_t workspace_bytes, void* s
   if (fam < 0) return fail(fam, why);
   if (num_rows_host(*p) == 0) return SFA_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t e = (fam == SFA_KERNEL_TCGEN05) ? launch_fwd_tc(*p, st) : launch_fwd_general(*p, st);
+  cudaError_t e = (fam != SFA_KERNEL_TCGEN05) ? launch_fwd_general(*p, st)
+                  : (p->block_size == 1 ? launch_fwd_tok(*p, st) : launch_fwd_tc(*p, st));
   if (e != cudaSuccess) return cuda_fail(e, "sfa_fwd launch");
   return SFA_OK;
 }

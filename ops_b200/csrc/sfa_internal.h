@@ -69,7 +69,10 @@ cudaError_t launch_convert_dq(const SfaParams& p, const float* dq_acc, cudaStrea
 // inverted block->query index
 cudaError_t launch_inverted_index(const SfaParams& p, const BwdLayout& L, char* ws, cudaStream_t st);
 
-// tensor-core (tcgen05) family
+// tensor-core (tcgen05) family: block-sparse kernels (block_size 64) and the
+// token-level forward (block_size 1, sfa_tok_fwd.cu)
+bool tok_fwd_supported(const SfaParams& p, const char** why);
+cudaError_t launch_fwd_tok(const SfaParams& p, cudaStream_t st);
 bool tc_fwd_supported(const SfaParams& p, const char** why);
 bool tc_bwd_supported(const SfaParams& p, const char** why);
 cudaError_t launch_fwd_tc(const SfaParams& p, cudaStream_t st);

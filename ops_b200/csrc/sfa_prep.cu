@@ -202,7 +202,7 @@ cudaError_t launch_preprocess(const SfaParams& p, float* delta, float* dsink_par
 // fp32 accumulators -> bf16 dk / dv (or dk := dk + dv when they alias)
 // ---------------------------------------------------------------------------
 __global__ void convert_kernel(SfaParams p, const float* __restrict__ acc, int D, int64_t sb, int64_t st,
-                               int64_t sh, __nv_bfloat16* __restrict__ out, const float* __restrict__ acc2) {
+                               int64_t sh, __nv_bfloat16* __restrict__ out, const float* __restrict__ acc2, int D2) {
   int64_t n = (p.cu_seqlens_q == nullptr ? (int64_t)p.batch * p.kv_len : (int64_t)p.total_kv) * p.h_kv * D;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     int d = (int)(i % D);
@@ -212,7 +212,7 @@ __global__ void convert_kernel(SfaParams p, const float* __restrict__ acc, int D
     int64_t b = 0, t = kr;
     if (p.cu_seqlens_q == nullptr) { b = kr / p.kv_len; t = kr - b * p.kv_len; }
     float v = acc[i];
-    if (acc2) v += acc2[i];
+    if (acc2 && d < D2) v += acc2[rest * D2 + d];   // dv into the leading D2 dims of a shared kv
     out[b * sb + t * st + hk * sh + d] = f2bf(v);
   }
 }
@@ -223,12 +223,12 @@ cudaError_t launch_convert_dkdv(const SfaParams& p, const float* dk_acc, const f
   bool shared_kv = (p.dk == p.dv);
   convert_kernel<<<grid, 256, 0, st>>>(p, dk_acc, p.d_qk, p.dk_sb, p.dk_st, p.dk_sh,
                                        reinterpret_cast<__nv_bfloat16*>(p.dk),
-                                       (shared_kv && dv_acc != dk_acc) ? dv_acc : nullptr);
+                                       (shared_kv && dv_acc != dk_acc) ? dv_acc : nullptr, p.d_v);
   note_launch("convert_dk", st);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || shared_kv) return e;
   convert_kernel<<<grid, 256, 0, st>>>(p, dv_acc, p.d_v, p.dv_sb, p.dv_st, p.dv_sh,
-                                       reinterpret_cast<__nv_bfloat16*>(p.dv), nullptr);
+                                       reinterpret_cast<__nv_bfloat16*>(p.dv), nullptr, 0);
   note_launch("convert_dv", st);
   return cudaGetLastError();
 }

@@ -151,6 +151,13 @@ def _check_inputs(q, k, v, idx):
         raise ValueError(f"block indices must be an integer tensor, got {idx.dtype}")
 
 
+def _leading_view(v: torch.Tensor, k: torch.Tensor) -> bool:
+    """v is k's leading dims (``v = k[..., :Dv]``, the MLA latent kv): the two
+    share rows, so one gradient ``dk + dv`` (summed in fp32) flows back to k."""
+    return (v.data_ptr() == k.data_ptr() and v.stride() == k.stride() and v.shape[:-1] == k.shape[:-1]
+            and v.shape[-1] <= k.shape[-1] and k.stride(-1) == 1)
+
+
 def _idx32(idx: torch.Tensor) -> torch.Tensor:
     if idx.dtype == torch.int32:
         return _inner_contig(idx)
@@ -194,7 +201,8 @@ def sparse_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bl
     read back from ``cu_seqlens`` with a device->host sync.  ``lse`` is the
     natural-log log-sum-exp ``[.., Hq]`` (fp32); it carries no gradient.
     ``attn_sink`` (``[Hq]`` fp32) adds ``exp(sink)`` to every denominator.
-    If ``k is v`` their rows are shared and one gradient ``dk + dv`` flows back.
+    If ``k is v``, or v is k's leading dims (``v = k[..., :Dv]``, one latent kv
+    tensor), their rows are shared and one gradient ``dk + dv`` flows back to k.
     ``dkv_mode`` ("inverted" | "atomic"), ``dq_mode`` ("separate" | "fused") and
     ``kernel`` ("tcgen05" | "general") override the launch table ("auto").
     """
@@ -214,12 +222,12 @@ def sparse_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bl
         max_seqlen_q, max_seqlen_k = q.shape[1], k.shape[1]
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
-    shared = k is v
+    shared = k is v or _leading_view(v, k)
     cfg = _Cfg(int(block_size), float(scale), bool(causal), varlen, int(max_seqlen_q), int(max_seqlen_k),
                _DKV[dkv_mode], _KERNEL[kernel], shared, _DQ[dq_mode])
     sink = None if attn_sink is None else attn_sink.float()
     kk = _inner_contig(k)
-    vv = kk if shared else _inner_contig(v)
+    vv = (kk if k is v else v) if shared else _inner_contig(v)
     return _SFAFunction.apply(_inner_contig(q), kk, vv, _idx32(block_indices), sink, cu_q, cu_k, cfg)
 
 

@@ -1,0 +1,141 @@
+"""GPU parity of the token-level (block_size 1) tensor-core forward against the
+CPU oracle: the reference's own operating mode (one kv row per index,
+SFA.py:399-415) and the MLA geometry (128 query heads on one latent kv head,
+D_qk 576 / D_v 512, V = the latent's first 512 dims).
+
+Cases cover head tiles below, at and above 128 heads, D_v split into 256-dim
+parts, top-k counts that leave a partial last chunk, -1 / out-of-range /
+duplicate indices, rows with nothing selected, causal and non-causal,
+varlen, the attention sink, scores that force the running output to be
+rescaled, and the reference signature (SBHD, shared kv)."""
+import ctypes
+
+import pytest
+import torch
+
+import ops_b200
+from ops_b200 import _lib
+from ops_b200 import sfa as S
+from oracle import sfa_oracle as O
+from sfa_check import assert_close, assert_lse
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(B, T, Hq, Hk, Dqk, Dv, K, seed, shared=False, causal=True, edge=False):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, T, Hq, Dqk, generator=g).bfloat16()
+    k = torch.randn(B, T, Hk, Dqk, generator=g).bfloat16()
+    v = k[..., :Dv] if shared else torch.randn(B, T, Hk, Dv, generator=g).bfloat16()
+    if causal:
+        u = torch.rand(B, T, Hk, T, generator=g)
+        t = torch.arange(T)
+        u = torch.where(t[None, None, None, :] <= t[None, :, None, None], u, torch.full_like(u, 2.0))
+        val, idx = torch.topk(u, min(K, T), dim=-1, largest=False)
+        idx = torch.where(val < 2.0, idx, torch.full_like(idx, -1))
+    else:
+        idx = torch.stack([torch.randperm(T, generator=g)[:K] for _ in range(B * T * Hk)]).view(B, T, Hk, K)
+    idx = idx.to(torch.int32)
+    if edge:
+        idx[:, 1] = -1                                   # nothing selected
+        idx[:, 2, :, 0] = -1                             # -1 in front
+        idx[:, 3, :, 1] = T + 5                          # past the end
+        idx[:, 4, :, 2] = idx[:, 4, :, 3]                # duplicate slot
+        idx[:, T // 2, :, ::3] = -1                      # holes
+    return q, k, v, idx
+
+
+def _check_fwd(q, k, v, idx, causal, sink=None, scale=None):
+    dev = torch.device("cuda")
+    shared = v.data_ptr() == k.data_ptr()
+    kd = k.to(dev)
+    vd = kd[..., :v.shape[-1]] if shared else v.to(dev)
+    o, lse = ops_b200.sparse_flash_attention(q.to(dev), kd, vd, idx.to(dev), 1, scale,
+                                             attn_sink=None if sink is None else sink.to(dev), causal=causal,
+                                             kernel="tcgen05")
+    torch.cuda.synchronize()
+    ro, rl = O.sfa_forward(q.float(), k.float(), v.float(), idx, 1, scale, sink, causal)
+    assert_close("o", o.cpu(), ro)
+    assert_lse(lse.cpu(), rl)
+    return o.cpu(), lse.cpu()
+
+
+@pytest.mark.parametrize("Hq,Hk,Dqk,Dv,K", [
+    (16, 1, 64, 64, 128),       # small head tile (rows 16..127 padded)
+    (64, 2, 128, 128, 100),     # partial last chunk
+    (128, 1, 576, 512, 256),    # MLA: two V parts, nine 64-dim slabs of q/k
+    (256, 1, 128, 128, 64),     # two 128-head tiles
+    (32, 1, 192, 320, 130),     # odd slab counts: 3 q/k slabs, V parts of 256 + 64
+])
+def test_token_level_forward(Hq, Hk, Dqk, Dv, K):
+    q, k, v, idx = _inputs(2, 300, Hq, Hk, Dqk, Dv, K, seed=Hq + Dqk, edge=True)
+    sink = torch.randn(Hq, generator=torch.Generator().manual_seed(1))
+    _check_fwd(q, k, v, idx, True, sink)
+
+
+def test_mla_shared_latent_kv_non_causal():
+    q, k, v, idx = _inputs(1, 512, 128, 1, 576, 512, 2048, seed=7, shared=True, causal=False)
+    _check_fwd(q, k, v, idx, False, scale=576 ** -0.5)
+
+
+def test_empty_rows_give_zero_and_sink_or_neg_inf():
+    q, k, v, idx = _inputs(1, 64, 16, 1, 64, 64, 64, seed=3)
+    idx[:, ::2] = -1
+    o, lse = _check_fwd(q, k, v, idx, True)
+    assert o[:, ::2].abs().max() == 0 and torch.isneginf(lse[:, ::2]).all()
+    sink = torch.randn(16, generator=torch.Generator().manual_seed(2))
+    o, lse = _check_fwd(q, k, v, idx, True, sink)
+    assert o[:, ::2].abs().max() == 0 and torch.allclose(lse[0, ::2], sink.expand(32, 16))
+
+
+def test_large_scores_rescale_the_running_output():
+    # scores growing along the index list raise the running maximum by more
+    # than the rescale threshold several times within a row
+    q, k, v, _ = _inputs(1, 256, 32, 1, 128, 128, 64, seed=5, causal=False)
+    ramp = torch.linspace(0.2, 6.0, 256)[:, None, None]
+    k = (k[0].float() * ramp).bfloat16()[None]
+    idx = torch.arange(256, dtype=torch.int32).expand(1, 256, 1, 256).contiguous()
+    _check_fwd(q, k, v, idx, False, scale=0.5)
+
+
+def test_varlen_token_level():
+    g = torch.Generator().manual_seed(11)
+    q_lens, k_lens = [5, 130, 64], [40, 130, 300]
+    cu_q = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0)), dtype=torch.int32)
+    cu_k = torch.tensor([0] + list(torch.tensor(k_lens).cumsum(0)), dtype=torch.int32)
+    Hq, Hk, D, K = 32, 2, 128, 96
+    q = torch.randn(int(cu_q[-1]), Hq, D, generator=g).bfloat16()
+    k = torch.randn(int(cu_k[-1]), Hk, D, generator=g).bfloat16()
+    v = torch.randn(int(cu_k[-1]), Hk, D, generator=g).bfloat16()
+    idx = torch.randint(-1, 310, (int(cu_q[-1]), Hk, K), generator=g, dtype=torch.int32)
+    dev = torch.device("cuda")
+    o, lse = ops_b200.sparse_flash_attention(q.to(dev), k.to(dev), v.to(dev), idx.to(dev), 1,
+                                             cu_seqlens=cu_q.to(dev), cu_seqlens_k=cu_k.to(dev),
+                                             max_seqlen_q=max(q_lens), max_seqlen_k=max(k_lens), kernel="tcgen05")
+    ro, rl = O.sfa_forward(q.float(), k.float(), v.float(), idx, 1, None, None, True, cu_q, cu_k)
+    assert_close("o", o.cpu(), ro)
+    assert_lse(lse.cpu(), rl)
+
+
+def test_reference_signature_runs_on_tensor_cores():
+    # SparseFlashAttention.apply (SBHD, shared kv) picks the token-level
+    # tensor-core forward; its output matches the oracle
+    Sq, B, H, D, K = 256, 2, 64, 128, 200
+    g = torch.Generator().manual_seed(4)
+    q = torch.randn(Sq, B, H, D, generator=g).bfloat16()
+    kv = torch.randn(Sq, B, D, generator=g).bfloat16()
+    sink = torch.randn(H, generator=g)
+    idx = torch.stack([torch.randperm(Sq, generator=g)[:K] for _ in range(Sq * B)]).view(Sq, B, K).to(torch.int32)
+    dev = torch.device("cuda")
+    qd, kvd, idd = q.to(dev), kv.to(dev), idx.to(dev)
+    out = torch.empty_like(qd)
+    lse = torch.empty(Sq, B, H, device=dev)
+    cfg = S._Cfg(1, D ** -0.5, False, False, Sq, Sq, 0, 0, True)
+    kvb = kvd.permute(1, 0, 2).unsqueeze(2)
+    P = S.build_params(qd.permute(1, 0, 2, 3), kvb, kvb, idd.permute(1, 0, 2).unsqueeze(2),
+                       out.permute(1, 0, 2, 3), lse.permute(1, 0, 2), cfg)
+    assert _lib.load().sfa_select_kernel(ctypes.byref(P), 0) == _lib.SFA_KERNEL_TCGEN05
+    o = ops_b200.SparseFlashAttention.apply(qd, kvd, sink.to(dev), idd, D ** -0.5)
+    torch.cuda.synchronize()
+    ro, _ = O.reference_compat_forward(q.float(), kv.float(), sink, idx, D ** -0.5)
+    assert_close("out", o.cpu(), ro)
