@@ -512,8 +512,8 @@ def measure_config(args, cfg, world, rank, dev, split, steps, warmup, primary):
 def e2e_pipeline(args, cfg, d, split, units, rows, world, rank, dev, stream, flush, v_view, steps):
     """Public-API step with host-resident inputs/outputs; returns (ms, h2d, d2h).
 
-    The rank's share is cut into chunks along the batch (or the kv heads of one
-    batch); chunk i's H2D copies run on one stream, its forward + backward on a
+    The rank's share is cut into chunks of one (batch, kv head) unit each;
+    chunk i's H2D copies run on one stream, its forward + backward on a
     second, its D2H copies on a third, so the PCIe traffic of neighbouring
     chunks overlaps the kernels (and H2D overlaps D2H)."""
     import torch
@@ -526,12 +526,8 @@ def e2e_pipeline(args, cfg, d, split, units, rows, world, rank, dev, stream, flu
     q, k, v, idx, do = d["q"], d["k"], d["v"], d["idx"], d["do"]
     if split == "query":
         chunks = [None]
-    elif b1 - b0 > 1:
-        chunks = [(b, b + 1, h0, h1) for b in range(b0, b1)]
-    elif h1 - h0 > 1:
-        chunks = [(b0, b1, h, h + 1) for h in range(h0, h1)]
-    else:
-        chunks = [(b0, b1, h0, h1)]
+    else:   # one chunk per (batch, kv head) unit: the last chunk's copies are the only ones not hidden
+        chunks = [(b, b + 1, h, h + 1) for b in range(b0, b1) for h in range(h0, h1)]
 
     def pin(t):
         return t.contiguous().cpu().pin_memory()

@@ -74,7 +74,7 @@ def test_token_level_forward(Hq, Hk, Dqk, Dv, K):
 
 
 def test_mla_shared_latent_kv_non_causal():
-    q, k, v, idx = _inputs(1, 512, 128, 1, 576, 512, 2048, seed=7, shared=True, causal=False)
+    q, k, v, idx = _inputs(1, 640, 128, 1, 576, 512, 512, seed=7, shared=True, causal=False)
     _check_fwd(q, k, v, idx, False, scale=576 ** -0.5)
 
 
