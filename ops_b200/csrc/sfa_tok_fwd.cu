@@ -21,12 +21,17 @@
 // those rare chunks (before that chunk's PV is issued; the previous chunk's
 // PV has completed because P's buffer is single).
 //
-// Warp roles (256 threads, one persistent CTA per SM):
-//   warp 0      K producer: index validity masks of the item's 64-slot chunks,
-//               chunk descriptors (mask, key ids), Q loads, K gathers;
+// Row gathers are issue-bound: a warp's gather4 copies leave one after another
+// (~100 cycles each, so ~5 B/clk per issuing warp, measured on B200), while
+// warps issue in parallel.  A pool of nine gather warps therefore shares each
+// chunk's 64-dim slabs (K for S, then V for PV) round-robin.
+//
+// Warp roles (512 threads, one persistent CTA per SM):
+//   warp 0      descriptor producer: index validity masks of the item's 64-slot
+//               chunks, chunk descriptors (mask, key ids), Q loads;
 //   warp 1      S issuer (one thread);
 //   warp 2      PV issuer (one thread);
-//   warp 3      V producer: V gathers of the item's part from the descriptors;
+//   warps 3, 8-15  gather pool: K and V slabs of each chunk (tile::gather4);
 //   warps 4-7   softmax + epilogue, thread = head row (TMEM lane).
 // Every wait is bounded (~2 s); on expiry the kernel records (4 << 16) | site in
 // the status word and returns.
@@ -45,7 +50,8 @@ using namespace tc;
 
 namespace tokf {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;
+constexpr int kGatherWarps = 9;        // warps 3 and 8-15
 constexpr int kKeys = 64;            // keys per chunk
 constexpr int kMaxTopk = 32 * kKeys;  // one chunk per producer lane
 constexpr int kJD = 4;               // descriptor ring
@@ -61,7 +67,7 @@ struct Desc {
   uint32_t mlo, mhi;                 // valid keys of the chunk (bit j: key j)
   int flags;
   int row, hk, hg, vp, b, tq;
-  int64_t vbase;                     // V gather row of key 0 of this item's sequence / kv head
+  int64_t kbase, vbase;              // K / V gather rows of key 0 of this item's sequence / kv head
   int keys[kKeys];                   // key ids (an invalid slot repeats a valid key of the chunk)
 };
 
@@ -179,13 +185,14 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
     mbar_init(&B.p_empty, 1);
     mbar_init(&B.o_full, 1);
     mbar_init(&B.o_empty, 4);
-    // consumers of a descriptor: S issuer, PV issuer, V producer, 4 softmax warps
+    // consumers of a descriptor: S issuer, PV issuer, the gather warps, 4 softmax warps
     for (int i = 0; i < kJD; ++i) {
       mbar_init(&B.jd_full[i], 1);
-      mbar_init(&B.jd_empty[i], 7);
+      mbar_init(&B.jd_empty[i], 2 + kGatherWarps + 4);
     }
-    for (int i = 0; i < KS; ++i) { mbar_init(&B.k_full[i], 1); mbar_init(&B.k_empty[i], 1); }
-    for (int i = 0; i < VS; ++i) { mbar_init(&B.v_full[i], 1); mbar_init(&B.v_empty[i], 1); }
+    // a stage's two slabs come from two gather warps: each announces its own bytes
+    for (int i = 0; i < KS; ++i) { mbar_init(&B.k_full[i], 2); mbar_init(&B.k_empty[i], 1); }
+    for (int i = 0; i < VS; ++i) { mbar_init(&B.v_full[i], 2); mbar_init(&B.v_empty[i], 1); }
     fence_barrier_init();
   }
   // head rows past the tile's HG stay zero for the whole kernel (TMA writes HG rows)
@@ -206,11 +213,10 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
   tc_fence_after();
   const uint32_t tmem = B.tmem_base;
   const int quad = lane & 15;        // gather copy of this lane: keys 4*quad .. 4*quad+3
-  const int half = lane >> 4;        // which slab of a 2-slab stage this lane fills
 
   if (warp == 0) {
-    // ============================================================ K producer
-    int job = 0, kuse = 0, item_i = 0;
+    // ============================================================ descriptor producer
+    int job = 0, item_i = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < args.nitems && ok; item += gridDim.x) {
       int row, hk, hg, vp;
@@ -231,7 +237,6 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       }
       const uint32_t chunks = __ballot_sync(0xffffffffu, (my_lo | my_hi) != 0u);
       const int64_t kbase = ((int64_t)r.b * p.k_sb + r.kv0 * p.k_st + (int64_t)hk * p.k_sh) / args.k_rs;
-      const int64_t kstep = p.k_st / args.k_rs;
       const int64_t vbase = ((int64_t)r.b * p.v_sb + r.kv0 * p.v_st + (int64_t)hk * p.v_sh) / args.v_rs;
       if (chunks == 0u) {
         // nothing selected: one descriptor tells the softmax warps to write zeros
@@ -284,30 +289,11 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
           d.mlo = lo; d.mhi = hi;
           d.flags = (c == cfirst ? kFirst : 0) | (c == clast ? kLast : 0);
           d.row = row; d.hk = hk; d.hg = hg; d.vp = vp; d.b = r.b; d.tq = (int)r.tq;
+          d.kbase = kbase;
           d.vbase = vbase;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&B.jd_full[js]);
-        // the four keys of this lane's gather copy
-        int kr[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int src = (4 * quad + i) & 31;
-          const int a = __shfl_sync(0xffffffffu, e0, src), bb = __shfl_sync(0xffffffffu, e1, src);
-          kr[i] = (int)(kbase + (int64_t)(quad < 8 ? a : bb) * kstep);
-        }
-        for (int s = 0; s < NQ && ok; s += 2, ++kuse) {
-          const int ks = kuse % KS;
-          const int nsl = NQ - s < 2 ? NQ - s : 2;
-          if (lane == 0) {
-            ok = wt(&B.k_empty[ks], ((kuse / KS) & 1) ^ 1, st, 4);
-            if (ok) mbar_arrive_expect_tx(&B.k_full[ks], (uint32_t)(nsl * kSlab));
-          }
-          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-          if (ok && half < nsl)
-            gather4(sk + ks * 2 * kSlab + half * kSlab + quad * 512, &tmk, &B.k_full[ks], (s + half) * 64, kr[0],
-                    kr[1], kr[2], kr[3]);
-        }
       }
     }
     if (lane == 0 && ok) {
@@ -317,9 +303,15 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         mbar_arrive(&B.jd_full[js]);
       }
     }
-  } else if (warp == 3) {
-    // ============================================================ V producer
-    int job = 0, vuse = 0;
+  } else if (warp == 3 || warp >= 8) {
+    // ============================================================ gather pool
+    // Slab i of the j-th non-empty chunk (K slabs 0..NQ-1, then the part's V
+    // slabs) goes to warp (j * nslabs + i) % kGatherWarps.  Every owner waits
+    // for the stage to be free, then announces its slab's bytes before copying
+    // (the full barrier counts two arrivals; a stage of one slab arrives twice).
+    const int g = warp == 3 ? 0 : warp - 7;
+    const int64_t kstep = p.k_st / args.k_rs, vstep = p.v_st / args.v_rs;
+    int job = 0, kuse = 0, vuse = 0, nchunk = 0;
     bool ok = true;
     while (ok) {
       const int js = job % kJD;
@@ -335,31 +327,48 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         continue;
       }
       const int e0 = d.keys[lane], e1 = d.keys[lane + 32];
-      const int64_t vbase = d.vbase;
+      const int64_t kbase = d.kbase, vbase = d.vbase;
       const int vp = d.vp;
       __syncwarp();
       if (lane == 0) mbar_arrive(&B.jd_empty[js]);
-      int vr[4];
+      int kq[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int src = (4 * quad + i) & 31;
         const int a = __shfl_sync(0xffffffffu, e0, src), bb = __shfl_sync(0xffffffffu, e1, src);
-        vr[i] = (int)(vbase + (int64_t)(quad < 8 ? a : bb) * (p.v_st / args.v_rs));
+        kq[i] = quad < 8 ? a : bb;
       }
       const int d0 = vp * args.dvp;
       const int nv = (min(p.d_v - d0, args.dvp)) / 64;
-      for (int s = 0; s < nv && ok; s += 2, ++vuse) {
-        const int vs = vuse % VS;
-        const int nsl = nv - s < 2 ? nv - s : 2;
+      const int nslabs = NQ + nv;
+      for (int i = 0; i < nslabs && ok; ++i) {
+        if ((nchunk * nslabs + i) % kGatherWarps != g) continue;
+        const bool isk = i < NQ;
+        const int si = isk ? i : i - NQ;          // slab within K or V
+        const int use = (isk ? kuse : vuse) + si / 2;
+        const int nst = isk ? KS : VS;
+        const int s_ = use % nst;
+        const int tot = isk ? NQ : nv;
+        const int nsl = tot - (si & ~1) < 2 ? tot - (si & ~1) : 2;
+        uint64_t* full = isk ? &B.k_full[s_] : &B.v_full[s_];
         if (lane == 0) {
-          ok = wt(&B.v_empty[vs], ((vuse / VS) & 1) ^ 1, st, 7);
-          if (ok) mbar_arrive_expect_tx(&B.v_full[vs], (uint32_t)(nsl * kSlab));
+          ok = wt(isk ? &B.k_empty[s_] : &B.v_empty[s_], ((use / nst) & 1) ^ 1, st, 7);
+          if (ok) {
+            mbar_arrive_expect_tx(full, (uint32_t)kSlab);
+            if (nsl == 1) mbar_arrive(full);
+          }
         }
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (ok && half < nsl)
-          gather4(sv + vs * 2 * kSlab + half * kSlab + quad * 512, &tmv, &B.v_full[vs], d0 + (s + half) * 64, vr[0],
-                  vr[1], vr[2], vr[3]);
+        if (ok && lane < 16) {
+          uint8_t* dst = (isk ? sk : sv) + s_ * 2 * kSlab + (si & 1) * kSlab + quad * 512;
+          const int64_t base = isk ? kbase : vbase, step = isk ? kstep : vstep;
+          gather4(dst, isk ? &tmk : &tmv, full, isk ? si * 64 : d0 + si * 64, (int)(base + kq[0] * step),
+                  (int)(base + kq[1] * step), (int)(base + kq[2] * step), (int)(base + kq[3] * step));
+        }
       }
+      kuse += (NQ + 1) / 2;
+      vuse += (nv + 1) / 2;
+      ++nchunk;
       ++job;
     }
   } else if (warp == 1) {
@@ -486,22 +495,18 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       const int sb = chunk & 1;
       if (!(ok = wtw(&B.s_full[sb], (chunk >> 1) & 1, st, 17))) break;
       tc_fence_after();
-      float s[64];
-      {
-        float t0[32], t1[32];
-        tmem_ld32(tl + kColS + sb * kKeys, t0);
-        tmem_ld32(tl + kColS + sb * kKeys + 32, t1);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) { s[i] = t0[i]; s[i + 32] = t1[i]; }
-      }
-      tc_fence_before();
-      warp_arrive(&B.s_empty[sb]);
+      const uint32_t ts = tl + kColS + sb * kKeys;
+      // pass 1: the chunk's max over its valid keys (S read in 32-column halves)
       float mc = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if ((mlo >> i) & 1u) mc = fmaxf(mc, s[i]);
-        if ((mhi >> i) & 1u) mc = fmaxf(mc, s[i + 32]);
+      for (int hh = 0; hh < 2; ++hh) {
+        float sv[32];
+        tmem_ld32(ts + hh * 32, sv);
+        tmem_ld_wait();
+        const uint32_t msk = hh ? mhi : mlo;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if ((msk >> i) & 1u) mc = fmaxf(mc, sv[i]);
       }
       const float zc = mc * c2;                // finite: the chunk has a valid key
       float mnew = mref, fac = 1.f;
@@ -530,21 +535,30 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       mref = mnew;
       const float nm = -mref;
       const uint32_t prow = smem_u32(sp) + m * 128;
+      // pass 2: P = exp2(S*c - m) for the valid keys, bf16 into the swizzled P tile
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float pr[8];
+      for (int hh = 0; hh < 2; ++hh) {
+        float sv[32];
+        tc_fence_after();
+        tmem_ld32(ts + hh * 32, sv);
+        tmem_ld_wait();
+        const uint32_t msk = hh ? mhi : mlo;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int key = 8 * j + i;
-          const bool valid = key < 32 ? ((mlo >> key) & 1u) : ((mhi >> (key - 32)) & 1u);
-          pr[i] = valid ? ex2(fmaf(s[key], c2, nm)) : 0.f;
-          l += pr[i];
+        for (int j = 0; j < 4; ++j) {
+          float pr[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            pr[i] = ((msk >> (8 * j + i)) & 1u) ? ex2(fmaf(sv[8 * j + i], c2, nm)) : 0.f;
+            l += pr[i];
+          }
+          const int jj = 4 * hh + j;
+          st_shared_v4(prow + ((jj ^ (m & 7)) << 4), pack_bf16x2(pr[0], pr[1]), pack_bf16x2(pr[2], pr[3]),
+                       pack_bf16x2(pr[4], pr[5]), pack_bf16x2(pr[6], pr[7]));
         }
-        st_shared_v4(prow + ((j ^ (m & 7)) << 4), pack_bf16x2(pr[0], pr[1]), pack_bf16x2(pr[2], pr[3]),
-                     pack_bf16x2(pr[4], pr[5]), pack_bf16x2(pr[6], pr[7]));
       }
-      fence_proxy_async_smem();
       tc_fence_before();
+      warp_arrive(&B.s_empty[sb]);
+      fence_proxy_async_smem();
       warp_arrive(&B.p_full);
       ++chunk;
       if (flags & kLast) {
