@@ -23,8 +23,8 @@
 //
 // Row gathers are issue-bound: a warp's gather4 copies leave one after another
 // (~100 cycles each, so ~5 B/clk per issuing warp, measured on B200), while
-// warps issue in parallel.  A pool of nine gather warps therefore shares each
-// chunk's 64-dim slabs (K for S, then V for PV) round-robin.
+// warps issue in parallel.  A pool of nine gather warps therefore shares the
+// K and V rings: every (stage slot, slab half) position has a fixed owner.
 //
 // Warp roles (512 threads, one persistent CTA per SM):
 //   warp 0      descriptor producer: index validity masks of the item's 64-slot
@@ -190,7 +190,7 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       mbar_init(&B.jd_full[i], 1);
       mbar_init(&B.jd_empty[i], 2 + kGatherWarps + 4);
     }
-    // a stage's two slabs come from two gather warps: each announces its own bytes
+    // a stage's two slab positions have their own owners: each arrives once per use
     for (int i = 0; i < KS; ++i) { mbar_init(&B.k_full[i], 2); mbar_init(&B.k_empty[i], 1); }
     for (int i = 0; i < VS; ++i) { mbar_init(&B.v_full[i], 2); mbar_init(&B.v_empty[i], 1); }
     fence_barrier_init();
@@ -305,13 +305,17 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
     }
   } else if (warp == 3 || warp >= 8) {
     // ============================================================ gather pool
-    // Slab i of the j-th non-empty chunk (K slabs 0..NQ-1, then the part's V
-    // slabs) goes to warp (j * nslabs + i) % kGatherWarps.  Every owner waits
-    // for the stage to be free, then announces its slab's bytes before copying
-    // (the full barrier counts two arrivals; a stage of one slab arrives twice).
+    // Each (ring, stage slot, slab half) position has one owner warp
+    // (position % kGatherWarps), which takes part in every use of its slot, in
+    // order: it waits for the slot's previous use to be consumed, then either
+    // announces and copies its slab or, when the stage has a single slab,
+    // arrives without bytes (the full barriers count two arrivals).  Because
+    // an owner never skips a use, its parity wait can never be satisfied by a
+    // phase two laps old.  (Dealing slabs to warps round-robin instead let a
+    // warp run laps ahead of a slot and refill it early.)
     const int g = warp == 3 ? 0 : warp - 7;
     const int64_t kstep = p.k_st / args.k_rs, vstep = p.v_st / args.v_rs;
-    int job = 0, kuse = 0, vuse = 0, nchunk = 0;
+    int job = 0, kuse = 0, vuse = 0;
     bool ok = true;
     while (ok) {
       const int js = job % kJD;
@@ -340,35 +344,35 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       }
       const int d0 = vp * args.dvp;
       const int nv = (min(p.d_v - d0, args.dvp)) / 64;
-      const int nslabs = NQ + nv;
-      for (int i = 0; i < nslabs && ok; ++i) {
-        if ((nchunk * nslabs + i) % kGatherWarps != g) continue;
-        const bool isk = i < NQ;
-        const int si = isk ? i : i - NQ;          // slab within K or V
-        const int use = (isk ? kuse : vuse) + si / 2;
-        const int nst = isk ? KS : VS;
-        const int s_ = use % nst;
-        const int tot = isk ? NQ : nv;
-        const int nsl = tot - (si & ~1) < 2 ? tot - (si & ~1) : 2;
-        uint64_t* full = isk ? &B.k_full[s_] : &B.v_full[s_];
-        if (lane == 0) {
-          ok = wt(isk ? &B.k_empty[s_] : &B.v_empty[s_], ((use / nst) & 1) ^ 1, st, 7);
-          if (ok) {
-            mbar_arrive_expect_tx(full, (uint32_t)kSlab);
-            if (nsl == 1) mbar_arrive(full);
+      for (int r = 0; r < 2 && ok; ++r) {
+        const bool isk = r == 0;
+        const int tot = isk ? NQ : nv, nst = isk ? KS : VS, ubase = isk ? kuse : vuse;
+        const int64_t base = isk ? kbase : vbase, step = isk ? kstep : vstep;
+        for (int t = 0; t < (tot + 1) / 2 && ok; ++t) {
+          const int use = ubase + t, s_ = use % nst;
+          for (int h = 0; h < 2 && ok; ++h) {
+            const int pos = isk ? s_ * 2 + h : 2 * KS + s_ * 2 + h;
+            if (pos % kGatherWarps != g) continue;
+            const bool real = 2 * t + h < tot;
+            uint64_t* full = isk ? &B.k_full[s_] : &B.v_full[s_];
+            if (lane == 0) {
+              ok = wt(isk ? &B.k_empty[s_] : &B.v_empty[s_], ((use / nst) & 1) ^ 1, st, 7);
+              if (ok) {
+                if (real) mbar_arrive_expect_tx(full, (uint32_t)kSlab);
+                else mbar_arrive(full);
+              }
+            }
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (ok && real && lane < 16) {
+              uint8_t* dst = (isk ? sk : sv) + s_ * 2 * kSlab + h * kSlab + quad * 512;
+              gather4(dst, isk ? &tmk : &tmv, full, (isk ? 0 : d0) + (2 * t + h) * 64, (int)(base + kq[0] * step),
+                      (int)(base + kq[1] * step), (int)(base + kq[2] * step), (int)(base + kq[3] * step));
+            }
           }
-        }
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (ok && lane < 16) {
-          uint8_t* dst = (isk ? sk : sv) + s_ * 2 * kSlab + (si & 1) * kSlab + quad * 512;
-          const int64_t base = isk ? kbase : vbase, step = isk ? kstep : vstep;
-          gather4(dst, isk ? &tmk : &tmv, full, isk ? si * 64 : d0 + si * 64, (int)(base + kq[0] * step),
-                  (int)(base + kq[1] * step), (int)(base + kq[2] * step), (int)(base + kq[3] * step));
         }
       }
       kuse += (NQ + 1) / 2;
       vuse += (nv + 1) / 2;
-      ++nchunk;
       ++job;
     }
   } else if (warp == 1) {
