@@ -151,7 +151,7 @@ static int select_family(const SfaParams& p, bool bwd, std::string* why) {
   const char* tc_why = "";
   bool tc_ok;
   if (bwd)
-    tc_ok = tc_bwd_supported(p, &tc_why);
+    tc_ok = p.block_size == 1 ? tok_bwd_supported(p, &tc_why) : tc_bwd_supported(p, &tc_why);
   else
     tc_ok = p.block_size == 1 ? tok_fwd_supported(p, &tc_why) : tc_fwd_supported(p, &tc_why);
   if (p.kernel == SFA_KERNEL_TCGEN05) {
@@ -164,7 +164,9 @@ static int select_family(const SfaParams& p, bool bwd, std::string* why) {
 }
 
 static int resolve_dkv_mode(const SfaParams& p, int family) {
-  if (family == SFA_KERNEL_GENERAL) return SFA_DKV_ATOMIC;
+  // token-level selections have no shared block structure for a key-centric
+  // pass: the query-centric kernels add dk/dv with fp32 reductions
+  if (family == SFA_KERNEL_GENERAL || p.block_size == 1) return SFA_DKV_ATOMIC;
   if (p.dkv_mode == SFA_DKV_ATOMIC || !tc_dkdv_available()) return SFA_DKV_ATOMIC;
   return SFA_DKV_INVERTED;
 }
@@ -352,17 +354,20 @@ int sfa_bwd_dq(const SfaParams* p, void* workspace, size_t workspace_bytes, void
     // the dK/dV pass accumulates dQ: start from zero
     e = cudaMemsetAsync(ws + L.dq_acc, 0, sizeof(float) * (size_t)num_rows_host(*p) * p->h_q * p->d_qk, st);
     note_memset("memset_dq_acc", st);
-  } else if (fam == SFA_KERNEL_TCGEN05) {
+  } else if (fam == SFA_KERNEL_TCGEN05 && p->block_size != 1) {
     e = launch_bwd_dq_tc(*p, delta, st);
   } else {
-    // the general kernel computes dq together with the dk/dv atomics
+    // the general kernel and the token-level tensor-core kernel compute dq
+    // together with the dk/dv reductions
     float* dk_acc = reinterpret_cast<float*>(ws + L.dk_acc);
     float* dv_acc = reinterpret_cast<float*>(ws + L.dv_acc);
     const int64_t kvr = kv_rows_host(*p);
     e = cudaMemsetAsync(dk_acc, 0, sizeof(float) * kvr * p->h_kv * p->d_qk, st);
     if (e == cudaSuccess && dv_acc != dk_acc) e = cudaMemsetAsync(dv_acc, 0, sizeof(float) * kvr * p->h_kv * p->d_v, st);
     note_memset("memset_dkdv_acc", st);
-    if (e == cudaSuccess) e = launch_bwd_general(*p, delta, dk_acc, dv_acc, st);
+    if (e == cudaSuccess)
+      e = fam == SFA_KERNEL_TCGEN05 ? launch_bwd_tok(*p, delta, dk_acc, dv_acc, st)
+                                    : launch_bwd_general(*p, delta, dk_acc, dv_acc, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "sfa_bwd_dq");
   return SFA_OK;
@@ -387,7 +392,7 @@ int sfa_bwd_dkdv(const SfaParams* p, void* workspace, size_t workspace_bytes, vo
     float* dk_acc = reinterpret_cast<float*>(ws + L.dk_acc);
     float* dv_acc = reinterpret_cast<float*>(ws + L.dv_acc);
     e = cudaSuccess;
-    if (fam == SFA_KERNEL_TCGEN05) {
+    if (fam == SFA_KERNEL_TCGEN05 && p->block_size != 1) {
       // dq came from the tensor-core kernel; the atomic pass adds dk/dv only
       const int64_t kvr = kv_rows_host(*p);
       e = cudaMemsetAsync(dk_acc, 0, sizeof(float) * kvr * p->h_kv * p->d_qk, st);

@@ -73,6 +73,10 @@ cudaError_t launch_inverted_index(const SfaParams& p, const BwdLayout& L, char* 
 // token-level forward (block_size 1, sfa_tok_fwd.cu)
 bool tok_fwd_supported(const SfaParams& p, const char** why);
 cudaError_t launch_fwd_tok(const SfaParams& p, cudaStream_t st);
+// token-level backward (sfa_tok_bwd.cu): dq, and dk/dv added into the fp32
+// accumulators (zeroed by the caller) of the atomic workspace layout
+bool tok_bwd_supported(const SfaParams& p, const char** why);
+cudaError_t launch_bwd_tok(const SfaParams& p, const float* delta, float* dk_acc, float* dv_acc, cudaStream_t st);
 bool tc_fwd_supported(const SfaParams& p, const char** why);
 bool tc_bwd_supported(const SfaParams& p, const char** why);
 cudaError_t launch_fwd_tc(const SfaParams& p, cudaStream_t st);

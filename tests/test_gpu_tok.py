@@ -139,3 +139,95 @@ def test_reference_signature_runs_on_tensor_cores():
     torch.cuda.synchronize()
     ro, _ = O.reference_compat_forward(q.float(), kv.float(), sink, idx, D ** -0.5)
     assert_close("out", o.cpu(), ro)
+
+
+# ---------------------------------------------------------------------------
+# backward (head dims up to 256): dq directly, dk / dv through fp32 reductions
+# ---------------------------------------------------------------------------
+def _check_fwd_bwd(q, k, v, idx, causal, sink=None, scale=None, shared=False):
+    from sfa_check import check_all, run_op, run_oracle
+    got = run_op(q, k, v, idx, 1, scale, sink, causal, _do(q, v), kernel="tcgen05", shared_kv=shared)
+    ref = run_oracle(q, k, v, idx, 1, scale, sink, causal, _do(q, v), o_for_bwd=got["o"])
+    check_all(got, ref, shared_kv=shared)
+
+
+def _do(q, v):
+    g = torch.Generator().manual_seed(q.shape[-2] * 7 + v.shape[-1])
+    return torch.randn(*q.shape[:-1], v.shape[-1], generator=g).bfloat16()
+
+
+@pytest.mark.parametrize("Hq,Hk,Dqk,Dv,K,shared", [
+    (16, 1, 64, 64, 128, False),      # padded head tile, one-slab tiles
+    (64, 2, 128, 128, 100, False),    # separate dK / dV tiles, partial last chunk
+    (128, 1, 128, 128, 256, True),    # one kv tensor: dV adds into the dK tiles
+    (64, 1, 256, 256, 192, True),     # D = 256 merged: TMEM fully used
+    (32, 1, 192, 128, 64, False),     # odd slab counts
+])
+def test_token_level_backward(Hq, Hk, Dqk, Dv, K, shared):
+    q, k, v, idx = _inputs(2, 260, Hq, Hk, Dqk, Dv, K, seed=Hq + Dqk + 1, edge=True)
+    if shared:
+        v = k
+    sink = torch.randn(Hq, generator=torch.Generator().manual_seed(8))
+    _check_fwd_bwd(q, k, v, idx, True, sink, shared=shared)
+
+
+def test_token_level_backward_latent_view():
+    # v is k's leading dims (one latent tensor): one fp32-summed dk + dv
+    q, k, _, idx = _inputs(1, 200, 32, 1, 192, 128, 96, seed=13)
+    dev = torch.device("cuda")
+    qd = q.to(dev).requires_grad_()
+    kd = k.to(dev).requires_grad_()
+    do = _do(q, k[..., :128])
+    o, _ = ops_b200.sparse_flash_attention(qd, kd, kd[..., :128], idx.to(dev), 1, kernel="tcgen05")
+    o.backward(do.to(dev))
+    torch.cuda.synchronize()
+    ro, rl = O.sfa_forward(q.float(), k.float(), k[..., :128].float(), idx, 1)
+    rdq, rdk, rdv, _ = O.sfa_backward(q.float(), k.float(), k[..., :128].float(), idx, o.detach().float().cpu(), rl,
+                                      do.float(), 1)
+    dkv = rdk.clone()
+    dkv[..., :128] += rdv
+    assert_close("o", o.detach().cpu(), ro)
+    assert_close("dq", qd.grad.cpu(), rdq)
+    assert_close("dkv", kd.grad.cpu(), dkv)
+
+
+def test_token_level_backward_varlen():
+    from sfa_check import check_all, run_op, run_oracle
+    g = torch.Generator().manual_seed(17)
+    q_lens, k_lens = [3, 100, 64], [30, 100, 250]
+    cu_q = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0)), dtype=torch.int32)
+    cu_k = torch.tensor([0] + list(torch.tensor(k_lens).cumsum(0)), dtype=torch.int32)
+    Hq, Hk, D, K = 16, 2, 128, 80
+    q = torch.randn(int(cu_q[-1]), Hq, D, generator=g).bfloat16()
+    k = torch.randn(int(cu_k[-1]), Hk, D, generator=g).bfloat16()
+    v = torch.randn(int(cu_k[-1]), Hk, D, generator=g).bfloat16()
+    do = torch.randn(int(cu_q[-1]), Hq, D, generator=g).bfloat16()
+    idx = torch.randint(-1, 260, (int(cu_q[-1]), Hk, K), generator=g, dtype=torch.int32)
+    got = run_op(q, k, v, idx, 1, None, None, True, do, cu_q, cu_k, max(q_lens), max(k_lens), kernel="tcgen05")
+    ref = run_oracle(q, k, v, idx, 1, None, None, True, do, cu_q, cu_k, o_for_bwd=got["o"])
+    check_all(got, ref)
+
+
+def test_reference_signature_backward_on_tensor_cores():
+    # SparseFlashAttention.apply end to end (forward and backward on the
+    # token-level tensor-core kernels): dq, dkv = dK*scale + dV, dsink
+    Sq, B, H, D, K = 200, 2, 32, 128, 150
+    g = torch.Generator().manual_seed(23)
+    q = torch.randn(Sq, B, H, D, generator=g).bfloat16()
+    kv = torch.randn(Sq, B, D, generator=g).bfloat16()
+    sink = torch.randn(H, generator=g)
+    idx = torch.stack([torch.randperm(Sq, generator=g)[:K] for _ in range(Sq * B)]).view(Sq, B, K).to(torch.int32)
+    idx[: Sq // 4, :, K // 2:] = -1
+    do = torch.randn(Sq, B, H, D, generator=g).bfloat16()
+    dev = torch.device("cuda")
+    qg, kvg, sg = q.to(dev).requires_grad_(), kv.to(dev).requires_grad_(), sink.to(dev).requires_grad_()
+    out = ops_b200.SparseFlashAttention.apply(qg, kvg, sg, idx.to(dev), D ** -0.5)
+    out.backward(do.to(dev))
+    torch.cuda.synchronize()
+    ro, rl = O.reference_compat_forward(q.float(), kv.float(), sink, idx, D ** -0.5)
+    rdq, rdkv, rds = O.reference_compat_backward(q.float(), kv.float(), sink, idx, D ** -0.5,
+                                                 out.detach().float().cpu(), rl, do.float())
+    assert_close("out", out.detach().cpu(), ro)
+    assert_close("dq", qg.grad.cpu(), rdq)
+    assert_close("dkv", kvg.grad.cpu(), rdkv)
+    assert_close("dsink", sg.grad.cpu(), rds)
