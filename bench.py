@@ -137,7 +137,7 @@ class ClockSampler:
 # (batch 0, kv head 0) unit (decode: the forward of the first `seqs`
 # sequences).  A few seconds of fp32 work on 16 host threads each.
 CPU_SAMPLE = {"c1": {"last": 1024}, "c2": {"last": 8192}, "c3": {"last": 1024}, "c4": {"last": 64},
-              "c5": {"seqs": 16}}
+              "c5": {"seqs": 16}, "tok128": {"last": 256}}
 
 
 def cpu_sample_desc(cfg) -> str:

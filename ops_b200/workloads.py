@@ -12,6 +12,8 @@ Configurations (same numbering as the benchmark):
   c4  B1  T32768 Hq128 Hk1 Dqk576 Dv512 bs1 k2048 token-level, causal; one
       latent kv tensor (k), v = k[..., :512] (a view)
   c5  128 seqs, kv U[4096,131072], 1 query each, Hq64 Hk8 D128 bs64 S32 (forward only)
+  tok128  B1 T8192 Hq128 Hk1 D128 bs1 k2048, one shared kv tensor (the reference
+      op's own mode; not a BASELINE configuration)
 """
 from __future__ import annotations
 
@@ -52,6 +54,10 @@ CONFIGS = {
     "c4": Config("c4", 1, 32768, 128, 1, 576, 512, 1, 2048, "token"),
     "c5": Config("c5", 128, 1, 64, 8, 128, 128, 64, 32, "decode", n_seqs=128, kv_min=4096, kv_max=131072,
                  fwd_only=True),
+    # not a BASELINE configuration: the reference op's own operating mode
+    # (SparseFlashAttentionTriton: one kv tensor whose rows are keys and values,
+    # token-level top-k) at D = 128, for the token-level kernels' measurements
+    "tok128": Config("tok128", 1, 8192, 128, 1, 128, 128, 1, 2048, "token"),
 }
 
 
