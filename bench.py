@@ -361,7 +361,9 @@ def measure_config(args, cfg, world, rank, dev, split, steps, warmup, primary):
     lse = torch.empty(q.shape[:-1], dtype=torch.float32, device=dev)
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
-    dv = torch.empty_like(v)   # v = kv[..., :Dv] (c4): the caller adds dv into kv's gradient
+    # v = kv[..., :Dv] (c4, tok128): one kv tensor, one gradient dk + dv (the
+    # library sums them in fp32 when dk and dv alias)
+    dv = dk if v_view and split != "query" else torch.empty_like(v)
     scfg = S._Cfg(cfg.bs, cfg.scale, cfg.causal, False, r1 - r0, ke, _lib.SFA_DKV_AUTO, _lib.SFA_KERNEL_AUTO,
                   False, S._DQ[args.dq_mode])
     P = S.build_params(q, k, v, idx, o, lse, scfg, None, None, None, do, dq, dk, dv, None)

@@ -19,7 +19,8 @@
 // preprocess kernel (SFA.py:590-610) and the sink gradient from its partials.
 //
 // TMEM (512 columns): S [0, 64), dP [64, 128), dQ [128, 128 + D_qk), then the
-// dK^T tiles (64 columns per 128 dims) and, unless merged, the dV^T tiles.
+// dK^T tiles (64 columns per 128 dims) and, unless merged, the dV^T tiles —
+// twice when they fit, so the drain of one chunk overlaps the next chunk's MMAs.
 //
 // Warp roles (512 threads, one persistent CTA per SM):
 //   warp 0          descriptor producer: validity masks, chunk descriptors,
@@ -75,6 +76,8 @@ struct Args {
   int kst, vst;
   int ntk, ntv;                        // 128-dim tiles of dK^T / dV^T
   uint32_t col_dk, col_dv;
+  uint32_t kv_stride;                  // TMEM columns between the two dK^T/dV^T buffers (0: one buffer)
+  int nkvb;                            // dK^T/dV^T buffers (2 when TMEM allows)
   uint32_t off_do, off_k, off_v, off_p, off_ds, off_desc, off_bar;
   int64_t k_rs, v_rs;
   int32_t* status;
@@ -85,7 +88,7 @@ struct Bars {
   uint64_t sd_full, sd_empty;          // S / dP in TMEM
   uint64_t pd_full, pd_empty;          // P / dS' tiles in shared memory
   uint64_t dq_full, dq_empty;          // dQ accumulator
-  uint64_t kv_full, kv_empty;          // dK^T / dV^T tiles
+  uint64_t kv_full[2], kv_empty[2];    // dK^T / dV^T tiles (double-buffered when TMEM allows)
   uint64_t jd_full[kJD], jd_empty[kJD];
   uint32_t tmem_base;
   uint32_t pad;
@@ -138,8 +141,10 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
     mbar_init(&B.pd_empty, 1);
     mbar_init(&B.dq_full, 1);
     mbar_init(&B.dq_empty, 4);
-    mbar_init(&B.kv_full, 1);
-    mbar_init(&B.kv_empty, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&B.kv_full[i], 1);
+      mbar_init(&B.kv_empty[i], 4);
+    }
     // consumers of a descriptor: two MMA issuers, the gather pool, P/dS warps, drain warps
     for (int i = 0; i < kJD; ++i) {
       mbar_init(&B.jd_full[i], 1);
@@ -387,8 +392,11 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
           if (flags & kFirst)
             if (!(ok = wt(&B.dq_empty, (item_i & 1) ^ 1, st, 13))) break;
           if (!(ok = wt(&B.pd_full, chunk & 1, st, 14))) break;
-          if (!(ok = wt(&B.kv_empty, (chunk & 1) ^ 1, st, 15))) break;
+          const int kb = args.nkvb == 2 ? (chunk & 1) : 0;
+          const int kuse_b = args.nkvb == 2 ? (chunk >> 1) : chunk;
+          if (!(ok = wt(&B.kv_empty[kb], (kuse_b & 1) ^ 1, st, 15))) break;
           tc_fence_after();
+          const uint32_t kvoff = kb * args.kv_stride;
           const int ks = kuse % KS;
           // dQ += dS' . K: K stage as MN-major B (64-dim slabs 8 KB apart, 8-key groups 1 KB apart)
           const uint64_t kmn = smem_desc(smem_u32(sk + ks * kstage), kSlab, 1024, kSw128);
@@ -400,19 +408,19 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
           for (int j = 0; j < args.ntk; ++j) {
             const uint64_t qt = smem_desc(smem_u32(sq + 2 * j * kQSlab), kQSlab, 1024, kSw128);
             for (int k = 0; k < 8; ++k)
-              mma_bf16_ss(tmem + args.col_dk + 64 * j, qt + (uint64_t)((k * 2048) >> 4),
+              mma_bf16_ss(tmem + kvoff + args.col_dk + 64 * j, qt + (uint64_t)((k * 2048) >> 4),
                           dst_ + (uint64_t)((k * 2048) >> 4), id_kv, k != 0);
           }
           for (int j = 0; j < args.ntv; ++j) {
             const uint64_t ot = smem_desc(smem_u32(sdo + 2 * j * kQSlab), kQSlab, 1024, kSw128);
-            const uint32_t col = args.merged ? args.col_dk + 64 * j : args.col_dv + 64 * j;
+            const uint32_t col = kvoff + (args.merged ? args.col_dk + 64 * j : args.col_dv + 64 * j);
             for (int k = 0; k < 8; ++k)
               mma_bf16_ss(tmem + col, ot + (uint64_t)((k * 2048) >> 4), pt + (uint64_t)((k * 2048) >> 4), id_kv,
                           args.merged || k != 0);
           }
           mma_commit(&B.k_empty[ks]);
           mma_commit(&B.pd_empty);
-          mma_commit(&B.kv_full);
+          mma_commit(&B.kv_full[kb]);
           if (flags & kLast) {
             mma_commit(&B.dq_full);
             mma_commit(&B.q_empty);
@@ -516,6 +524,9 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
     }
   } else {
     // ============================================================ drain (warps 12-15)
+    // Each lane holds two of the chunk's keys (i and i + 32) and those keys'
+    // accumulator row offsets; a reduction takes its key's offset from the
+    // owning lane by shuffle, so the loop is shuffle + reduction only.
     const int wq = warp & 3;                 // TMEM lanes 32*wq.. = dims 32*wq.. of a 128-dim tile
     const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
     int job = 0, chunk = 0;
@@ -528,35 +539,36 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       if (flags & kSentinel) break;
       if (!(flags & kEmpty)) {
         const uint32_t mlo = d.mlo, mhi = d.mhi;
-        const int hk = d.hk;
-        const int64_t accrow = d.accrow;
-        if (!(ok = wtw(&B.kv_full, chunk & 1, st, 21))) break;
+        // row (in units of accumulator rows of h_kv heads) of keys lane and lane + 32
+        const int64_t r0 = (d.accrow + d.keys[lane]) * p.h_kv + d.hk;
+        const int64_t r1 = (d.accrow + d.keys[lane + 32]) * p.h_kv + d.hk;
+        const int kb = args.nkvb == 2 ? (chunk & 1) : 0;
+        const int kuse_b = args.nkvb == 2 ? (chunk >> 1) : chunk;
+        if (!(ok = wtw(&B.kv_full[kb], kuse_b & 1, st, 21))) break;
         tc_fence_after();
         for (int t = 0; t < args.ntk + (args.merged ? 0 : args.ntv); ++t) {
           const bool isk = t < args.ntk;
           const int j = isk ? t : t - args.ntk;
           const int D = isk ? p.d_qk : p.d_v;
-          float* acc = isk ? args.dk_acc : args.dv_acc;
-          const int dim = 128 * j + 32 * wq + lane;
-          const uint32_t col = isk ? args.col_dk + 64 * j : args.col_dv + 64 * j;
+          float* acc = (isk ? args.dk_acc : args.dv_acc) + 128 * j + 32 * wq + lane;
+          const bool dim_ok = 128 * j + 32 * wq + lane < D;
+          const uint32_t col = kb * args.kv_stride + (isk ? args.col_dk + 64 * j : args.col_dv + 64 * j);
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             float v[32];
             tmem_ld32(tl + col + 32 * hh, v);
             tmem_ld_wait();
             const uint32_t msk = hh ? mhi : mlo;
-            if (dim < D) {
-#pragma unroll 8
-              for (int i = 0; i < 32; ++i)
-                if ((msk >> i) & 1u) {
-                  const int key = d.keys[32 * hh + i];
-                  atomicAdd(acc + ((accrow + key) * p.h_kv + hk) * (int64_t)D + dim, v[i]);
-                }
+            const int64_t rr = hh ? r1 : r0;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int64_t ri = __shfl_sync(0xffffffffu, rr, i);
+              if (((msk >> i) & 1u) && dim_ok) atomicAdd(acc + ri * D, v[i]);
             }
           }
         }
         tc_fence_before();
-        warp_arrive(&B.kv_empty);
+        warp_arrive(&B.kv_empty[kb]);
         ++chunk;
       }
       warp_arrive(&B.jd_empty[js]);
@@ -600,6 +612,10 @@ static bool plan(const SfaParams& p, Plan* out, const char** why) {
   a.col_dv = a.col_dk + 64u * a.ntk;
   const uint32_t cols = a.col_dv + (a.merged ? 0u : 64u * a.ntv);
   if (cols > kTmemCols) { *why = "token-level backward: dQ plus the dK/dV tiles exceed tensor memory"; return false; }
+  // a second dK^T/dV^T buffer lets the next chunk's MMAs run while the drain reads this one
+  a.kv_stride = cols - a.col_dk;
+  a.nkvb = cols + a.kv_stride <= kTmemCols ? 2 : 1;
+  if (a.nkvb == 1) a.kv_stride = 0;
   // shared memory: Q, dO (16 KB slabs), K ring (full-chunk stages), V ring, P and dS' tiles
   const size_t budget = 227 * 1024 - 1024;
   const size_t desc = ((sizeof(Desc) * kJD + 127) / 128) * 128;
