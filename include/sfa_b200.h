@@ -66,6 +66,12 @@ enum {
                            needs rows * h_q * d_qk * 4 more workspace bytes */
 };
 
+/* Opt-in reference arithmetic (SfaParams.compat).  SFA_COMPAT_REFERENCE_P
+ * rounds the forward's probabilities the way SparseFlashAttentionTriton does
+ * before its PV matmul: stored as fp16, read back as bf16 (SFA.py:446, 456); the
+ * row sums keep the unrounded values, as there.  Default: one rounding to bf16. */
+#define SFA_COMPAT_REFERENCE_P 1
+
 /* Kernel family (SfaParams.kernel); AUTO picks the tensor-core path when it
  * supports the shape and the general CUDA-core path otherwise. */
 enum {
@@ -119,7 +125,8 @@ typedef struct SfaParams {
   int32_t dkv_mode;   /* SFA_DKV_* */
   int32_t kernel;     /* SFA_KERNEL_* */
   int32_t dq_mode;    /* SFA_DQ_* (was reserved: zero = AUTO) */
-  int32_t reserved[2];
+  int32_t compat;     /* SFA_COMPAT_* bits (was reserved: zero = none) */
+  int32_t reserved;
 } SfaParams;
 
 /* Library / ABI identification. */

@@ -6,8 +6,8 @@ Public surface:
 The kernels live in libsfa_b200.so (C ABI: include/sfa_b200.h).
 """
 from ._lib import SfaError, SfaParams, load as load_library
-from .sfa import SparseFlashAttention, reference_lse2, sparse_flash_attention
+from .sfa import SparseFlashAttention, SparseFlashAttentionCompat, reference_lse2, sparse_flash_attention
 from . import tiling
 
-__all__ = ["sparse_flash_attention", "SparseFlashAttention", "SfaError", "SfaParams", "load_library",
+__all__ = ["sparse_flash_attention", "SparseFlashAttention", "SparseFlashAttentionCompat", "SfaError", "SfaParams", "load_library",
            "reference_lse2", "tiling"]

@@ -22,6 +22,7 @@ SFA_ERR_DEVICE_TIMEOUT = -5
 SFA_DKV_AUTO, SFA_DKV_INVERTED, SFA_DKV_ATOMIC = 0, 1, 2
 SFA_KERNEL_AUTO, SFA_KERNEL_TCGEN05, SFA_KERNEL_GENERAL = 0, 1, 2
 SFA_DQ_AUTO, SFA_DQ_SEPARATE, SFA_DQ_FUSED = 0, 1, 2
+SFA_COMPAT_REFERENCE_P = 1
 SFA_SELFTEST_STATUS = (15 << 16) | 1   # status code of sfa_selftest_wait_timeout
 
 _c_void_p = ctypes.c_void_p
@@ -42,7 +43,7 @@ class SfaParams(ctypes.Structure):
         ("batch", _i32), ("q_len", _i32), ("kv_len", _i32), ("total_q", _i32), ("total_kv", _i32),
         ("h_q", _i32), ("h_kv", _i32), ("d_qk", _i32), ("d_v", _i32), ("block_size", _i32),
         ("topk", _i32), ("scale", ctypes.c_float), ("causal", _i32), ("dkv_mode", _i32),
-        ("kernel", _i32), ("dq_mode", _i32), ("reserved", _i32 * 2),
+        ("kernel", _i32), ("dq_mode", _i32), ("compat", _i32), ("reserved", _i32),
     ]
 
 

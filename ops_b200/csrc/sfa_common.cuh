@@ -8,6 +8,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -80,6 +81,11 @@ __device__ __forceinline__ int block_valid_keys(int e, int bs, int kv_len, int p
   int64_t n = end - first;
   return n > 0 ? (int)n : 0;
 }
+
+// A probability as the reference's PV matmul sees it under
+// SFA_COMPAT_REFERENCE_P: stored as fp16 (SFA.py:446), so values below fp16's
+// range flush and the mantissa is cut to 10 bits before the bf16 rounding.
+__device__ __forceinline__ float ref_p(float p) { return __half2float(__float2half_rn(p)); }
 
 __device__ __forceinline__ float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
 __device__ __forceinline__ __nv_bfloat16 f2bf(float x) { return __float2bfloat16_rn(x); }

@@ -98,8 +98,10 @@ __global__ void __launch_bounds__(kGenThreads) fwd_general_kernel(SfaParams p, i
       float lsum = 0.f;
       for (int kk = 0; kk < kKC; ++kk) {
         float pv = (srow[kk] == -INFINITY) ? 0.f : exp2f(srow[kk] - mx);
-        srow[kk] = pv;
         lsum += pv;
+        // the PV sum takes p at bf16 precision (the tensor-core kernels' operand),
+        // or as the reference rounds it (fp16, then bf16) under SFA_COMPAT_REFERENCE_P
+        srow[kk] = (p.compat & SFA_COMPAT_REFERENCE_P) ? bf2f(f2bf(ref_p(pv))) : pv;
       }
       lrow[tid] = lrow[tid] * alpha + lsum;
       mrow[tid] = mx;

@@ -612,6 +612,10 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
             pr[h] = valid ? ex2(fmaf(s[i][h], c2, m[h])) : 0.f;
             l[h] += pr[h];
           }
+          if (p.compat & SFA_COMPAT_REFERENCE_P) {
+#pragma unroll
+            for (int h = 0; h < 16; ++h) pr[h] = ref_p(pr[h]);
+          }
           // row = key within the segment; 32-byte rows, 32B swizzle (16-byte
           // halves swap when bit 2 of the row is set)
           const int rowk = c * 128 + lrow;

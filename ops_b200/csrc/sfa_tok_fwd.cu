@@ -514,6 +514,7 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
           for (int i = 0; i < 8; ++i) {
             pr[i] = ((msk >> (8 * j + i)) & 1u) ? ex2(fmaf(sv[8 * j + i], c2, nm)) : 0.f;
             l += pr[i];
+            if (p.compat & SFA_COMPAT_REFERENCE_P) pr[i] = ref_p(pr[i]);
           }
           const int jj = 4 * hh + j;
           st_shared_v4(prow + ((jj ^ (m & 7)) << 4), pack_bf16x2(pr[0], pr[1]), pack_bf16x2(pr[2], pr[3]),

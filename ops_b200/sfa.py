@@ -51,6 +51,7 @@ class _Cfg:
     kernel: int
     shared_kv: bool
     dq_mode: int = 0
+    compat: int = 0
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -114,6 +115,7 @@ def build_params(q, k, v, idx, o, lse, cfg: _Cfg, sink=None, cu_q=None, cu_k=Non
     P.dkv_mode = cfg.dkv_mode
     P.kernel = cfg.kernel
     P.dq_mode = cfg.dq_mode
+    P.compat = cfg.compat
     return P
 
 
@@ -191,7 +193,8 @@ def sparse_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bl
                            causal: bool = True, cu_seqlens_k: Optional[torch.Tensor] = None,
                            max_seqlen_q: Optional[int] = None, max_seqlen_k: Optional[int] = None,
                            dkv_mode: str = "auto", kernel: str = "auto",
-                           dq_mode: str = "auto") -> Tuple[torch.Tensor, torch.Tensor]:
+                           dq_mode: str = "auto", reference_quirks: bool = False
+                           ) -> Tuple[torch.Tensor, torch.Tensor]:
     """Block-sparse attention over selected kv blocks; returns ``(o, lse)``.
 
     Dense: ``q [B,T,Hq,Dqk]``, ``k [B,Tk,Hk,Dqk]``, ``v [B,Tk,Hk,Dv]``,
@@ -205,6 +208,14 @@ def sparse_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bl
     tensor), their rows are shared and one gradient ``dk + dv`` flows back to k.
     ``dkv_mode`` ("inverted" | "atomic"), ``dq_mode`` ("separate" | "fused") and
     ``kernel`` ("tcgen05" | "general") override the launch table ("auto").
+
+    ``reference_quirks=True`` reproduces the reference's own arithmetic and
+    lse format for bit-level comparisons with its saved values: probabilities
+    rounded to fp16 and then bf16 before the PV product (``SFA.py:446, 456``),
+    ``lse`` returned in base 2 (``SFA.py:474``) and ``+inf`` for a row with no
+    valid key when a sink is given (the reference's ``exp2(sink - m)`` with its
+    ``-1e11`` max seed overflows, ``SFA.py:381, 469-474``).  Gradients use the
+    natural-log lse internally either way.
     """
     _check_inputs(q, k, v, block_indices)
     if block_size <= 0:
@@ -224,11 +235,46 @@ def sparse_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bl
         scale = 1.0 / math.sqrt(q.shape[-1])
     shared = k is v or _leading_view(v, k)
     cfg = _Cfg(int(block_size), float(scale), bool(causal), varlen, int(max_seqlen_q), int(max_seqlen_k),
-               _DKV[dkv_mode], _KERNEL[kernel], shared, _DQ[dq_mode])
+               _DKV[dkv_mode], _KERNEL[kernel], shared, _DQ[dq_mode],
+               _lib.SFA_COMPAT_REFERENCE_P if reference_quirks else 0)
     sink = None if attn_sink is None else attn_sink.float()
     kk = _inner_contig(k)
     vv = (kk if k is v else v) if shared else _inner_contig(v)
-    return _SFAFunction.apply(_inner_contig(q), kk, vv, _idx32(block_indices), sink, cu_q, cu_k, cfg)
+    idx = _idx32(block_indices)
+    o, lse = _SFAFunction.apply(_inner_contig(q), kk, vv, idx, sink, cu_q, cu_k, cfg)
+    if reference_quirks:
+        lse = reference_lse2(lse)
+        if sink is not None:
+            lse = torch.where(_has_valid_key(idx, cfg, cu_q, cu_k, q.shape[-2], k.shape[-2]), lse,
+                              torch.full_like(lse, float("inf")))
+    return o, lse
+
+
+def _has_valid_key(idx: torch.Tensor, cfg: "_Cfg", cu_q, cu_k, hq: int, hk: int) -> torch.Tensor:
+    """[.., Hq] bool: the row selected at least one valid key (the kernels'
+    rule: block id in range, a key below kv_len and, when causal, at or before
+    the query's position).  Elementwise on the device, no host sync."""
+    bs = cfg.block_size
+    e = idx.to(torch.int64)
+    if cu_q is None:
+        T, Tk = idx.shape[1], cfg.max_k
+        pos = (torch.arange(T, device=idx.device) + (Tk - T))[None, :, None, None]
+        kv_len = torch.full_like(pos, Tk)
+    else:
+        rows = idx.shape[0]
+        r = torch.arange(rows, device=idx.device, dtype=torch.int32)
+        seq = torch.searchsorted(cu_q, r, right=True) - 1
+        q0, k0 = cu_q[seq], cu_k[seq]
+        ql, kl = cu_q[seq + 1] - q0, cu_k[seq + 1] - k0
+        pos = (r - q0 + kl - ql).to(torch.int64)[:, None, None]
+        kv_len = kl.to(torch.int64)[:, None, None]
+    first = e * bs
+    end = torch.minimum(first + bs, kv_len)
+    if cfg.causal:
+        end = torch.minimum(end, pos + 1)
+    ok = (e >= 0) & (first < kv_len) & (end > first)
+    anyk = ok.any(-1)                                    # [.., Hk]
+    return anyk.repeat_interleave(hq // hk, dim=-1)
 
 
 class SparseFlashAttention(torch.autograd.Function):
@@ -241,48 +287,73 @@ class SparseFlashAttention(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, q, kv, attn_sink, topk_idxs, sm_scale):
-        _check_inputs(q, kv, kv, topk_idxs)
-        if sm_scale is None:
-            sm_scale = 1.0 / math.sqrt(q.shape[-1])
-        cfg = _Cfg(1, float(sm_scale), False, False, q.shape[0], kv.shape[0], _lib.SFA_DKV_AUTO,
-                   _lib.SFA_KERNEL_AUTO, True)
-        qi = _inner_contig(q)
-        kvi = _inner_contig(kv)
-        idx = _idx32(topk_idxs)
-        qb = qi.permute(1, 0, 2, 3)
-        kvb = kvi.permute(1, 0, 2).unsqueeze(2)
-        ib = idx.permute(1, 0, 2).unsqueeze(2)
-        sink = None if attn_sink is None else attn_sink.float()
-        out = torch.empty_like(qi)
-        lse = torch.empty(q.shape[:-1], dtype=torch.float32, device=q.device)
-        lib = _lib.load()
-        P = build_params(qb, kvb, kvb, ib, out.permute(1, 0, 2, 3), lse.permute(1, 0, 2), cfg, sink)
-        _lib.check(lib.sfa_fwd(ctypes.byref(P), None, 0, _stream()), "sfa_fwd")
-        ctx.save_for_backward(qi, kvi, sink, idx, out, lse)
-        ctx.cfg = cfg
-        ctx.sink_given = attn_sink is not None
-        return out
+        return _reference_forward(ctx, q, kv, attn_sink, topk_idxs, sm_scale, 0)
 
     @staticmethod
     def backward(ctx, grad_out):
-        q, kv, sink, idx, out, lse = ctx.saved_tensors
-        cfg = ctx.cfg
-        lib = _lib.load()
-        dq = torch.empty_like(q)
-        dkv = torch.empty_like(kv)
-        need_dsink = ctx.sink_given and ctx.needs_input_grad[2]
-        dsink = torch.empty(q.shape[2], dtype=torch.float32, device=q.device) if need_dsink else None
-        qb = q.permute(1, 0, 2, 3)
-        kvb = kv.permute(1, 0, 2).unsqueeze(2)
-        dkvb = dkv.permute(1, 0, 2).unsqueeze(2)
-        ib = idx.permute(1, 0, 2).unsqueeze(2)
-        do = _inner_contig(grad_out)
-        P = build_params(qb, kvb, kvb, ib, out.permute(1, 0, 2, 3), lse.permute(1, 0, 2), cfg, sink,
-                         dout=do.permute(1, 0, 2, 3), dq=dq.permute(1, 0, 2, 3), dk=dkvb, dv=dkvb, dsink=dsink)
-        nbytes = lib.sfa_bwd_workspace_bytes(ctypes.byref(P))
-        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
-        _lib.check(lib.sfa_bwd(ctypes.byref(P), ws.data_ptr(), nbytes, _stream()), "sfa_bwd")
-        return dq, dkv, dsink, None, None
+        return _reference_backward(ctx, grad_out)
+
+
+def _reference_forward(ctx, q, kv, attn_sink, topk_idxs, sm_scale, compat):
+    _check_inputs(q, kv, kv, topk_idxs)
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(q.shape[-1])
+    cfg = _Cfg(1, float(sm_scale), False, False, q.shape[0], kv.shape[0], _lib.SFA_DKV_AUTO,
+               _lib.SFA_KERNEL_AUTO, True, compat=compat)
+    qi = _inner_contig(q)
+    kvi = _inner_contig(kv)
+    idx = _idx32(topk_idxs)
+    qb = qi.permute(1, 0, 2, 3)
+    kvb = kvi.permute(1, 0, 2).unsqueeze(2)
+    ib = idx.permute(1, 0, 2).unsqueeze(2)
+    sink = None if attn_sink is None else attn_sink.float()
+    out = torch.empty_like(qi)
+    lse = torch.empty(q.shape[:-1], dtype=torch.float32, device=q.device)
+    lib = _lib.load()
+    P = build_params(qb, kvb, kvb, ib, out.permute(1, 0, 2, 3), lse.permute(1, 0, 2), cfg, sink)
+    _lib.check(lib.sfa_fwd(ctypes.byref(P), None, 0, _stream()), "sfa_fwd")
+    ctx.save_for_backward(qi, kvi, sink, idx, out, lse)
+    ctx.cfg = cfg
+    ctx.sink_given = attn_sink is not None
+    return out
+
+
+def _reference_backward(ctx, grad_out):
+    q, kv, sink, idx, out, lse = ctx.saved_tensors
+    cfg = ctx.cfg
+    lib = _lib.load()
+    dq = torch.empty_like(q)
+    dkv = torch.empty_like(kv)
+    need_dsink = ctx.sink_given and ctx.needs_input_grad[2]
+    dsink = torch.empty(q.shape[2], dtype=torch.float32, device=q.device) if need_dsink else None
+    qb = q.permute(1, 0, 2, 3)
+    kvb = kv.permute(1, 0, 2).unsqueeze(2)
+    dkvb = dkv.permute(1, 0, 2).unsqueeze(2)
+    ib = idx.permute(1, 0, 2).unsqueeze(2)
+    do = _inner_contig(grad_out)
+    P = build_params(qb, kvb, kvb, ib, out.permute(1, 0, 2, 3), lse.permute(1, 0, 2), cfg, sink,
+                     dout=do.permute(1, 0, 2, 3), dq=dq.permute(1, 0, 2, 3), dk=dkvb, dv=dkvb, dsink=dsink)
+    nbytes = lib.sfa_bwd_workspace_bytes(ctypes.byref(P))
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
+    _lib.check(lib.sfa_bwd(ctypes.byref(P), ws.data_ptr(), nbytes, _stream()), "sfa_bwd")
+    return dq, dkv, dsink, None, None
+
+
+class SparseFlashAttentionCompat(SparseFlashAttention):
+    """``SparseFlashAttention`` with the reference's probability rounding
+    (fp16, then bf16, before the PV product, ``SFA.py:446, 456``): the same
+    signature and gradients, for callers that compare against outputs the
+    reference produced bit for bit.  (The reference's base-2 / +inf lse is
+    internal to its autograd context; ``sparse_flash_attention(...,
+    reference_quirks=True)`` returns it.)"""
+
+    @staticmethod
+    def forward(ctx, q, kv, attn_sink, topk_idxs, sm_scale):
+        return _reference_forward(ctx, q, kv, attn_sink, topk_idxs, sm_scale, _lib.SFA_COMPAT_REFERENCE_P)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        return _reference_backward(ctx, grad_out)
 
 
 def reference_lse2(lse: torch.Tensor) -> torch.Tensor:

@@ -61,3 +61,30 @@ def test_int64_indices_and_errors():
                                                                      device=dev), d["scale"])
     with pytest.raises(ValueError, match="bfloat16"):
         ops_b200.SparseFlashAttention.apply(q.float(), kv, sink, d["idx"].to(dev), d["scale"])
+
+
+@pytest.mark.parametrize("name", ["tok_bucket128", "tok_bucket160", "tok_bucket640", "empty_row"])
+def test_reference_quirks_mode_against_golden(name):
+    # with the reference's own rounding of p (fp16, then bf16) the op's output
+    # comes closer to the reference's saved output than with one bf16 rounding,
+    # and the returned lse is the reference's base-2 lse (+inf on a row with
+    # no valid key, as its -1e11 max seed makes it)
+    import ops_b200
+    d = load(name)
+    dev = torch.device("cuda")
+    q, kv, sink, idx = d["q"].bfloat16().to(dev), d["kv"].bfloat16().to(dev), d["sink"].to(dev), d["idx"].to(dev)
+    plain = ops_b200.SparseFlashAttention.apply(q, kv, sink, idx, d["scale"]).float().cpu()
+    quirk = ops_b200.SparseFlashAttentionCompat.apply(q, kv, sink, idx, d["scale"]).float().cpu()
+    e_plain, e_quirk = rel_l2(plain, d["out"]), rel_l2(quirk, d["out"])
+    assert e_quirk <= e_plain and e_quirk < 5e-3, (e_quirk, e_plain)
+    # the general surface with reference_quirks: base-2 lse with the reference's +inf
+    o, lse2 = ops_b200.sparse_flash_attention(q.permute(1, 0, 2, 3), kv.permute(1, 0, 2).unsqueeze(2),
+                                              kv.permute(1, 0, 2).unsqueeze(2), idx.permute(1, 0, 2).unsqueeze(2),
+                                              1, d["scale"], attn_sink=sink, causal=False, reference_quirks=True)
+    lse2 = lse2.permute(1, 0, 2).cpu()
+    ref = d["lse2"]
+    fin = torch.isfinite(ref)
+    assert torch.equal(torch.isfinite(lse2), fin) and torch.equal(lse2[~fin], ref[~fin])
+    if fin.any():
+        assert float((lse2[fin] - ref[fin]).abs().max()) < 1e-5
+    assert torch.equal(o.permute(1, 0, 2, 3).float().cpu(), quirk)

@@ -120,3 +120,33 @@ def test_reference_arm_prints_one_contract_line():
     assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert d["config"]["workload"].startswith("c1")
+
+
+def test_valid_key_mask_matches_the_oracle_rule():
+    # the reference-quirk lse marks rows with no valid key; the mask follows
+    # the kernels' (and the oracle's) validity rule, dense and varlen
+    from ops_b200 import sfa as S
+    g = torch.Generator().manual_seed(3)
+    B, T, Hk, G, Sl, bs = 2, 40, 2, 3, 4, 8
+    idx = torch.randint(-1, 7, (B, T, Hk, Sl), generator=g, dtype=torch.int32)
+    idx[:, :5] = -1
+    for causal in (True, False):
+        cfg = S._Cfg(bs, 1.0, causal, False, T, T, 0, 0, False)
+        got = S._has_valid_key(idx, cfg, None, None, Hk * G, Hk)
+        pos = torch.arange(T)
+        for b in range(B):
+            for h in range(Hk):
+                _, ok = O.key_table(idx[b, :, h], bs, pos, T, causal)
+                assert torch.equal(got[b, :, h * G:(h + 1) * G], ok.any(-1)[:, None].expand(T, G))
+    q_lens, k_lens = [3, 10, 1], [5, 30, 12]
+    cu_q = torch.tensor([0, 3, 13, 14], dtype=torch.int32)
+    cu_k = torch.tensor([0, 5, 35, 47], dtype=torch.int32)
+    vidx = torch.randint(-1, 5, (14, Hk, Sl), generator=g, dtype=torch.int32)
+    cfg = S._Cfg(bs, 1.0, True, True, 10, 30, 0, 0, False)
+    got = S._has_valid_key(vidx, cfg, cu_q, cu_k, Hk * G, Hk)
+    for i in range(3):
+        q0, q1, kl = int(cu_q[i]), int(cu_q[i + 1]), k_lens[i]
+        pos = torch.arange(q1 - q0) + kl - (q1 - q0)
+        for h in range(Hk):
+            _, ok = O.key_table(vidx[q0:q1, h], bs, pos, kl, True)
+            assert torch.equal(got[q0:q1, h * G:(h + 1) * G], ok.any(-1)[:, None].expand(q1 - q0, G))
