@@ -338,6 +338,11 @@ def measure_config(args, cfg, world, rank, dev, split, steps, warmup, primary):
     lib = _lib.load()
     d = W.make_inputs(cfg, dev, seed=rank_seed(rank if split == "batch" else 0))
     q, k, v, idx, do = d["q"], d["k"], d["v"], d["idx"], d["do"]
+    if getattr(args, "as_tokens", False) and cfg.bs > 1:
+        # the same selected keys as token-level indices: runs the token-level
+        # kernels (query-centric dK/dV with fp32 reductions) on this workload
+        idx = W.blocks_to_tokens(idx, cfg.bs)
+        cfg = W.scaled(cfg, bs=1, S=cfg.S * cfg.bs, name=cfg.name + "-as-tokens")
     v_view = v.data_ptr() == k.data_ptr()            # v = kv[..., :Dv] (MLA latent)
     T = cfg.T
     r0, r1, ke = 0, T, T
@@ -820,6 +825,9 @@ def main():
     ap.add_argument("--balance", choices=["pairs", "cost"], default="cost",
                     help="--split query: balance rows by selected pairs, or by a cost that also counts the "
                          "dK/dV pass's jobs and batches (ops_b200/shard.py row_cost)")
+    ap.add_argument("--as-tokens", action="store_true",
+                    help="expand a block-level configuration's indices to token level (the same selected keys), "
+                         "so the token-level kernels and their query-centric dK/dV run on it")
     ap.add_argument("--split", choices=["auto", "units", "batch", "query"], default="auto",
                     help="with N > 1: 'units' deals (batch, kv head) units out to the ranks (strong scaling; "
                          "the default when they divide evenly), 'query' splits one batch's query rows "

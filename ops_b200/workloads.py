@@ -190,6 +190,17 @@ def sfa_flops(pairs_qhead: int, d_qk: int, d_v: int) -> Flops:
     return Flops(2.0 * pairs_qhead * (d_qk + d_v), 2.0 * pairs_qhead * (3 * d_qk + 2 * d_v))
 
 
+def blocks_to_tokens(idx: torch.Tensor, bs: int) -> torch.Tensor:
+    """Token-level indices that select the same keys as block indices: slot
+    s*bs + j holds e*bs + j for the block e in slot s (-1 stays -1).  Keys past
+    kv_len or the causal limit are dropped by the op's own validity rule, so
+    the selected (query, key) pairs are the same."""
+    j = torch.arange(bs, device=idx.device, dtype=idx.dtype)
+    e = idx.unsqueeze(-1)
+    t = torch.where(e >= 0, e * bs + j, torch.full_like(e * bs + j, -1))
+    return t.flatten(-2)
+
+
 def count_pairs(idx: torch.Tensor, bs: int, q_len: int, kv_len: int, causal: bool = True,
                 q_pos: Optional[torch.Tensor] = None, kv_lens: Optional[torch.Tensor] = None) -> int:
     """Valid (query, kv head, key) triples; times Hq/Hk gives (query-head, key) pairs.

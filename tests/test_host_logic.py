@@ -70,6 +70,17 @@ def test_pair_count_matches_oracle(name):
     assert (f.fwd, f.bwd) == (g.fwd, g.bwd)
 
 
+def test_block_indices_as_tokens_select_the_same_pairs():
+    # c1's block indices expanded to token level select the same (query, key)
+    # pairs, partial blocks and -1 slots included
+    cfg = W.scaled(W.CONFIGS["c1"], T=1000)
+    idx = W.make_indices(cfg)
+    tok = W.blocks_to_tokens(idx, cfg.bs)
+    assert tok.shape == (*idx.shape[:-1], idx.shape[-1] * cfg.bs)
+    assert W.count_pairs(idx, cfg.bs, cfg.T, cfg.T) == W.count_pairs(tok, 1, cfg.T, cfg.T)
+    assert ((tok < 0) == (idx < 0).repeat_interleave(cfg.bs, -1)).all()
+
+
 def test_reference_tiling_buckets():
     assert tiling.resolve_tiling_config(128).BLOCK_N == 64
     assert tiling.resolve_tiling_config(150).BLOCK_K_BWD == 40
