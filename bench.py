@@ -314,7 +314,9 @@ def config_dict(cfg, n, split, balance="cost"):
 def kernel_flops(name, P, cfg, fl, fused_dq):
     """Algorithmic FLOPs a kernel owns (recomputation not counted).  With the
     fused dQ the key-centric pass performs every backward product (S, dP, dQ,
-    dK, dV); the separate dQ pass owns S, dP and dQ, leaving dK and dV."""
+    dK, dV); the separate dQ pass owns S, dP and dQ, leaving dK and dV; the
+    two-pass token-level backward's first pass owns S and dP, its gradient
+    half dQ, dK and dV."""
     two_p = 2.0 * P
     if name.startswith("fwd_"):
         return fl.fwd
@@ -324,6 +326,12 @@ def kernel_flops(name, P, cfg, fl, fused_dq):
         return fl.bwd if fused_dq else two_p * (cfg.Dqk + cfg.Dv)
     if name in ("bwd_general", "bwd_tok"):
         return fl.bwd
+    # the two-pass token-level backward: S and dP in the first pass, dQ, dK and
+    # dV in the gradient half
+    if name == "bwd_mla_sdp":
+        return two_p * (cfg.Dqk + cfg.Dv)
+    if name == "bwd_tok_grad":
+        return two_p * (2 * cfg.Dqk + cfg.Dv)
     return 0.0
 
 

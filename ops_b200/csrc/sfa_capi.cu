@@ -151,7 +151,8 @@ static int select_family(const SfaParams& p, bool bwd, std::string* why) {
   const char* tc_why = "";
   bool tc_ok;
   if (bwd)
-    tc_ok = p.block_size == 1 ? tok_bwd_supported(p, &tc_why) : tc_bwd_supported(p, &tc_why);
+    tc_ok = p.block_size == 1 ? (tok_bwd_supported(p, &tc_why) || mla_bwd_supported(p, &tc_why))
+                              : tc_bwd_supported(p, &tc_why);
   else
     tc_ok = p.block_size == 1 ? tok_fwd_supported(p, &tc_why) : tc_fwd_supported(p, &tc_why);
   if (p.kernel == SFA_KERNEL_TCGEN05) {
@@ -200,6 +201,12 @@ BwdLayout bwd_layout(const SfaParams& p, int family, int dkv_mode, int dq_mode) 
       off = align256(off + sizeof(float) * kvr * p.h_kv * p.d_v);
     } else {
       L.dv_acc = L.dk_acc;
+    }
+    const char* why = "";
+    L.two_pass = family == SFA_KERNEL_TCGEN05 && p.block_size == 1 && !tok_bwd_supported(p, &why);
+    if (L.two_pass) {
+      L.mla_pd = off;
+      off = align256(off + mla_ws_bytes(p));
     }
   } else {
     const int64_t nlists = (int64_t)L.units * L.nblk;
@@ -366,8 +373,9 @@ int sfa_bwd_dq(const SfaParams* p, void* workspace, size_t workspace_bytes, void
     if (e == cudaSuccess && dv_acc != dk_acc) e = cudaMemsetAsync(dv_acc, 0, sizeof(float) * kvr * p->h_kv * p->d_v, st);
     note_memset("memset_dkdv_acc", st);
     if (e == cudaSuccess)
-      e = fam == SFA_KERNEL_TCGEN05 ? launch_bwd_tok(*p, delta, dk_acc, dv_acc, st)
-                                    : launch_bwd_general(*p, delta, dk_acc, dv_acc, st);
+      e = fam != SFA_KERNEL_TCGEN05 ? launch_bwd_general(*p, delta, dk_acc, dv_acc, st)
+          : L.two_pass              ? launch_bwd_mla(*p, delta, dk_acc, dv_acc, ws + L.mla_pd, st)
+                                    : launch_bwd_tok(*p, delta, dk_acc, dv_acc, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "sfa_bwd_dq");
   return SFA_OK;

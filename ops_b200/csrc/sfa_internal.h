@@ -30,6 +30,7 @@ struct BwdLayout {
   size_t sched;        // int32 work counter               (inverted path)
   size_t dq_acc;       // float [rows * h_q * d_qk]       (fused dQ)
   size_t dkv_part;     // float [units*nblk*nranges][2][64][d_qk] (row-range split)
+  size_t mla_pd;       // bf16 P and dS' of one wave (two-pass token-level backward)
   size_t total;
   int inv_nsub;        // 128-row sub-chunks per unit in the index counts (padded)
   int sub_per_range;   // sub-chunks per row range of the key-centric pass
@@ -41,6 +42,7 @@ struct BwdLayout {
   bool atomic_dkv;
   bool inverted_dkv;
   bool fused_dq;
+  bool two_pass;       // token-level backward in two passes (head dims above 256)
 };
 
 constexpr int kPreRows = 16;  // query rows per preprocess CTA (x h_q must stay a multiple of 16: the
@@ -77,6 +79,21 @@ cudaError_t launch_fwd_tok(const SfaParams& p, cudaStream_t st);
 // accumulators (zeroed by the caller) of the atomic workspace layout
 bool tok_bwd_supported(const SfaParams& p, const char** why);
 cudaError_t launch_bwd_tok(const SfaParams& p, const float* delta, float* dk_acc, float* dv_acc, cudaStream_t st);
+// its two-pass form's gradient half: rows [r0, r1) with P and dS' read from the
+// workspace rows [r1 - r0][h_q][ld] (bf16)
+bool tok_bwd_parts_supported(const SfaParams& p, const char** why);
+cudaError_t launch_bwd_tok_parts(const SfaParams& p, float* dk_acc, float* dv_acc, const void* pws, const void* dsws,
+                                 int64_t ld, int r0, int r1, cudaStream_t st);
+// two-pass token-level backward for head dims above 256 (sfa_mla_bwd.cu): the
+// stacked [S ; dP] pass writes P and dS' to a workspace of mla_ws_bytes, the
+// gradient half adds dk/dv into the fp32 accumulators and writes dq; rows go
+// through in waves of mla_wave_rows
+bool mla_bwd_supported(const SfaParams& p, const char** why);
+int64_t mla_ws_ld(const SfaParams& p);
+int64_t mla_wave_rows(const SfaParams& p);
+size_t mla_ws_bytes(const SfaParams& p);
+cudaError_t launch_bwd_mla(const SfaParams& p, const float* delta, float* dk_acc, float* dv_acc, void* pd,
+                           cudaStream_t st);
 bool tc_fwd_supported(const SfaParams& p, const char** why);
 bool tc_bwd_supported(const SfaParams& p, const char** why);
 cudaError_t launch_fwd_tc(const SfaParams& p, cudaStream_t st);

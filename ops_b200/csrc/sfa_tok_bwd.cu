@@ -32,6 +32,14 @@
 //   warps 12-15     drain: dK^T / dV^T tiles (thread = dim) -> fp32 reductions.
 // Every wait is bounded (~2 s); on expiry the kernel records (5 << 16) | site in
 // the status word and returns.
+//
+// Two-pass form (head dims above 256, sfa_mla_bwd.cu): P and dS' come from the
+// workspace the first pass wrote, so S and dP are not formed here.  The work
+// item gains a part index (a 192-dim range of the head dims): Q, dO and the K
+// slabs of that range only, dQ of the range in TMEM (columns from 0), the P
+// and dS' tiles of each chunk loaded by TMA (4-D box: 64 slots x the head
+// tile) into two tile buffers, and the drain and the dq epilogue offset to
+// the range.
 #include "sfa_common.cuh"
 #include "sfa_internal.h"
 #include "sfa_tc_common.cuh"
@@ -53,6 +61,8 @@ constexpr int kSlab = 64 * 128;        // 64 rows x 64 dims bf16
 constexpr int kQSlab = 128 * 128;      // 128 head rows x 64 dims bf16
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColDP = 64, kColDQ = 128;
+constexpr int kPartSlabs = 3;          // two-pass form: 64-dim slabs of q/k per part
+constexpr int kTileBytes = 2 * kQSlab; // two-pass form: P and dS' tiles of one chunk
 
 enum : int { kFirst = 1, kLast = 2, kEmpty = 4, kSentinel = 8 };
 
@@ -60,6 +70,7 @@ struct Desc {
   uint32_t mlo, mhi;
   int flags;
   int row, hk, hg, b, tq;
+  int part, nqi, nvi, chunk, wrow;     // two-pass form: dim part, its q/k and dO slabs, chunk, wave row
   int64_t kbase, vbase;                // gather rows of key 0 (K / V maps)
   int64_t accrow;                      // accumulator row of key 0: b * kv_len (dense) or kv0 (varlen)
   int keys[kKeys];
@@ -81,6 +92,12 @@ struct Args {
   uint32_t off_do, off_k, off_v, off_p, off_ds, off_desc, off_bar;
   int64_t k_rs, v_rs;
   int32_t* status;
+  // two-pass form
+  int parts;                           // dim parts per (row, head tile); 0: one-pass form
+  int nq_all, nv_all;                  // 64-dim slabs of d_qk / d_v
+  int r0;                              // first row of the wave
+  uint32_t col_dq;                     // TMEM column of dQ
+  uint32_t off_tiles;                  // P / dS' tile buffers [2][kTileBytes]
 };
 
 struct Bars {
@@ -93,6 +110,7 @@ struct Bars {
   uint32_t tmem_base;
   uint32_t pad;
   uint64_t k_full[4], k_empty[4], v_full[4], v_empty[4];
+  uint64_t t_full[2], t_empty[2];      // two-pass form: P / dS' tile buffers
 };
 
 __device__ __forceinline__ bool wt(uint64_t* bar, uint32_t parity, int32_t* status, int site) {
@@ -105,17 +123,23 @@ __device__ __forceinline__ bool wtw(uint64_t* bar, uint32_t parity, int32_t* sta
   return __all_sync(0xffffffffu, wt(bar, parity, status, site));
 }
 
-__device__ __forceinline__ void decode_item(const Args& a, int item, int& row, int& hk, int& hg) {
+__device__ __forceinline__ void decode_item(const Args& a, int item, int& row, int& hk, int& hg, int& part) {
+  part = 0;
+  if (a.parts) {
+    part = item % a.parts;              // the parts of one row run side by side: its P / dS' rows stay in L2
+    item /= a.parts;
+  }
   hg = item % a.n_hg;
   const int r = item / a.n_hg;
   hk = r % a.p.h_kv;
-  row = r / a.p.h_kv;
+  row = a.r0 + r / a.p.h_kv;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
 sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CUtensorMap tmq,
                    const __grid_constant__ CUtensorMap tmdo, const __grid_constant__ CUtensorMap tmk,
-                   const __grid_constant__ CUtensorMap tmv) {
+                   const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmp,
+                   const __grid_constant__ CUtensorMap tmds) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const SfaParams& p = args.p;
@@ -125,6 +149,8 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
   uint8_t* sv = sbase + args.off_v;
   uint8_t* spp = sbase + args.off_p;
   uint8_t* sds = sbase + args.off_ds;
+  uint8_t* stile = sbase + args.off_tiles;
+  const bool two = args.parts != 0;
   Desc* jd = reinterpret_cast<Desc*>(sbase + args.off_desc);
   Bars& B = *reinterpret_cast<Bars*>(sbase + args.off_bar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -145,20 +171,30 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       mbar_init(&B.kv_full[i], 1);
       mbar_init(&B.kv_empty[i], 4);
     }
-    // consumers of a descriptor: two MMA issuers, the gather pool, P/dS warps, drain warps
+    // consumers of a descriptor: two MMA issuers (one in the two-pass form), the
+    // gather pool, P/dS warps, drain warps
     for (int i = 0; i < kJD; ++i) {
       mbar_init(&B.jd_full[i], 1);
-      mbar_init(&B.jd_empty[i], 2 + kGatherWarps + 4 + 4);
+      mbar_init(&B.jd_empty[i], (two ? 1 : 2) + kGatherWarps + 4 + 4);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&B.t_full[i], 1);
+      mbar_init(&B.t_empty[i], 1);
     }
     // one arrival per slab position of a stage
     for (int i = 0; i < KS; ++i) { mbar_init(&B.k_full[i], NQ); mbar_init(&B.k_empty[i], 1); }
     for (int i = 0; i < VS; ++i) { mbar_init(&B.v_full[i], NV); mbar_init(&B.v_empty[i], 1); }
     fence_barrier_init();
   }
-  // head rows past the tile's HG stay zero (TMA writes HG rows of Q and dO)
-  if (args.HG < 128)
+  // head rows past the tile's HG stay zero (TMA writes HG rows of Q and dO, and
+  // of the two-pass form's P / dS' tiles)
+  if (args.HG < 128) {
     for (int i = threadIdx.x; i < (NQ + NV) * kQSlab / 16; i += kThreads)   // Q and dO are adjacent
       reinterpret_cast<uint4*>(sq)[i] = make_uint4(0, 0, 0, 0);
+    if (two)
+      for (int i = threadIdx.x; i < 2 * kTileBytes / 16; i += kThreads)
+        reinterpret_cast<uint4*>(stile)[i] = make_uint4(0, 0, 0, 0);
+  }
   fence_proxy_async_smem();
   if (warp == 1) {
     tmem_alloc(&B.tmem_base, kTmemCols);
@@ -169,6 +205,10 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
     prefetch_tmap(&tmdo);
     prefetch_tmap(&tmk);
     prefetch_tmap(&tmv);
+    if (two) {
+      prefetch_tmap(&tmp);
+      prefetch_tmap(&tmds);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -178,12 +218,16 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
 
   if (warp == 0) {
     // ============================================================ descriptor producer
-    int job = 0, item_i = 0;
+    int job = 0, item_i = 0, tile = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < args.nitems && ok; item += gridDim.x) {
-      int row, hk, hg;
-      decode_item(args, item, row, hk, hg);
+      int row, hk, hg, part;
+      decode_item(args, item, row, hk, hg, part);
       const Row r = row_info(p, row);
+      // slabs of this item's dims: all of them, or the part's (two-pass form)
+      const int s0q = part * kPartSlabs;
+      const int nqi = two ? min(kPartSlabs, args.nq_all - s0q) : NQ;
+      const int nvi = two ? max(0, min(kPartSlabs, args.nv_all - s0q)) : NV;
       const int32_t* idx = p.block_indices + r.b * p.i_sb + r.tq * p.i_st + (int64_t)hk * p.i_sh;
       const int nch = (p.topk + kKeys - 1) / kKeys;
       uint32_t my_lo = 0, my_hi = 0;
@@ -209,6 +253,7 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
             Desc& d = jd[js];
             d.flags = kFirst | kLast | kEmpty;
             d.row = row; d.hk = hk; d.hg = hg; d.b = r.b; d.tq = (int)r.tq;
+            d.part = part; d.nqi = nqi; d.nvi = nvi;
             mbar_arrive(&B.jd_full[js]);
           }
         }
@@ -219,11 +264,12 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       if (lane == 0) {
         ok = wt(&B.q_empty, (item_i & 1) ^ 1, st, 2);
         if (ok) {
-          mbar_arrive_expect_tx(&B.q_full, (uint32_t)(args.HG * 128 * (NQ + NV)));
-          for (int s = 0; s < NQ; ++s)
-            tma_load_4d(sq + s * kQSlab, &tmq, &B.q_full, s * 64, hk * args.G + hg * 128, (int)r.tq, r.b);
-          for (int s = 0; s < NV; ++s)
-            tma_load_4d(sdo + s * kQSlab, &tmdo, &B.q_full, s * 64, hk * args.G + hg * 128, (int)r.tq, r.b);
+          mbar_arrive_expect_tx(&B.q_full, (uint32_t)(args.HG * 128 * (nqi + nvi)));
+          for (int s = 0; s < nqi; ++s)
+            tma_load_4d(sq + s * kQSlab, &tmq, &B.q_full, (s0q + s) * 64, hk * args.G + hg * 128, (int)r.tq, r.b);
+          for (int s = 0; s < nvi; ++s)
+            tma_load_4d(sdo + s * kQSlab, &tmdo, &B.q_full, (s0q + s) * 64, hk * args.G + hg * 128, (int)r.tq,
+                        r.b);
         }
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -242,6 +288,19 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         if (!((hi >> lane) & 1u)) e1 = fk;
         const int js = job % kJD;
         if (lane == 0) ok = wt(&B.jd_empty[js], ((job / kJD) & 1) ^ 1, st, 3);
+        // two-pass form: this chunk's P and dS' tiles into tile buffer tile % 2
+        if (two && lane == 0 && ok) {
+          const int tb = tile & 1;
+          ok = wt(&B.t_empty[tb], ((tile >> 1) & 1) ^ 1, st, 22);
+          if (ok) {
+            mbar_arrive_expect_tx(&B.t_full[tb], (uint32_t)(2 * args.HG * 128));
+            uint8_t* tdst = stile + tb * kTileBytes;
+            const int wrow = row - args.r0;
+            tma_load_4d(tdst, &tmp, &B.t_full[tb], c * kKeys, hk * args.G + hg * 128, wrow, 0);
+            tma_load_4d(tdst + kQSlab, &tmds, &B.t_full[tb], c * kKeys, hk * args.G + hg * 128, wrow, 0);
+          }
+        }
+        if (two) ++tile;
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (!ok) break;
         Desc& d = jd[js];
@@ -251,6 +310,7 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
           d.mlo = lo; d.mhi = hi;
           d.flags = (c == cfirst ? kFirst : 0) | (c == clast ? kLast : 0);
           d.row = row; d.hk = hk; d.hg = hg; d.b = r.b; d.tq = (int)r.tq;
+          d.part = part; d.nqi = nqi; d.nvi = nvi; d.chunk = c;
           d.kbase = kbase; d.vbase = vbase; d.accrow = accrow;
         }
         __syncwarp();
@@ -287,6 +347,7 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       }
       const int e0 = d.keys[lane], e1 = d.keys[lane + 32];
       const int64_t kbase = d.kbase, vbase = d.vbase;
+      const int nqi = d.nqi, kcol0 = d.part * kPartSlabs;
       __syncwarp();
       if (lane == 0) mbar_arrive(&B.jd_empty[js]);
       int kq[4];
@@ -305,15 +366,20 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
           const int pos = isk ? s_ * NQ + sl : KS * NQ + s_ * NV + sl;
           if (pos % kGatherWarps != g) continue;
           uint64_t* full = isk ? &B.k_full[s_] : &B.v_full[s_];
+          // a K slot of a part with fewer slabs (two-pass form) gets a plain arrive
+          const bool real = !isk || sl < nqi;
           if (lane == 0) {
             ok = wt(isk ? &B.k_empty[s_] : &B.v_empty[s_], ((use / nst) & 1) ^ 1, st, 6);
-            if (ok) mbar_arrive_expect_tx(full, (uint32_t)kSlab);
+            if (ok) {
+              if (real) mbar_arrive_expect_tx(full, (uint32_t)kSlab);
+              else mbar_arrive(full);
+            }
           }
           ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-          if (ok && lane < 16)
+          if (ok && real && lane < 16)
             gather4((isk ? sk + s_ * kstage : sv + s_ * vstage) + sl * kSlab + quad * 512, isk ? &tmk : &tmv, full,
-                    sl * 64, (int)(base + kq[0] * step), (int)(base + kq[1] * step), (int)(base + kq[2] * step),
-                    (int)(base + kq[3] * step));
+                    ((isk ? kcol0 : 0) + sl) * 64, (int)(base + kq[0] * step), (int)(base + kq[1] * step),
+                    (int)(base + kq[2] * step), (int)(base + kq[3] * step));
         }
       }
       ++kuse;
@@ -322,7 +388,8 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
     }
   } else if (warp == 1) {
     // ============================================================ MMA issuer A: S, dP
-    if (lane == 0) {
+    // (the two-pass form has no S / dP: P and dS' come from the workspace)
+    if (lane == 0 && !two) {
       const uint32_t id_s = idesc_bf16(128, kKeys, false, false);
       int job = 0, kuse = 0, vuse = 0, item_i = 0, chunk = 0;
       bool ok = true;
@@ -376,11 +443,7 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
   } else if (warp == 2) {
     // ============================================================ MMA issuer B: dQ, dK^T, dV^T
     if (lane == 0) {
-      const uint32_t id_q = idesc_bf16(128, (uint32_t)p.d_qk, false, true);
       const uint32_t id_kv = idesc_bf16(128, kKeys, true, true);
-      const uint64_t dsd = smem_desc(smem_u32(sds), 16, 1024, kSw128);     // dS' [heads][keys], K-major
-      const uint64_t dst_ = smem_desc(smem_u32(sds), 0, 1024, kSw128);     // dS'^T as MN-major B
-      const uint64_t pt = smem_desc(smem_u32(spp), 0, 1024, kSw128);       // P^T as MN-major B
       int job = 0, kuse = 0, item_i = 0, chunk = 0;
       bool ok = true;
       while (ok) {
@@ -389,9 +452,26 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         const int flags = jd[js].flags;
         if (flags & kSentinel) break;
         if (!(flags & kEmpty)) {
-          if (flags & kFirst)
+          const int nqi = jd[js].nqi, nvi = jd[js].nvi;
+          // P and dS' tiles: formed in this kernel, or (two-pass form) tile buffer chunk % 2
+          const uint8_t* tp = two ? stile + (chunk & 1) * kTileBytes : spp;
+          const uint8_t* tds = two ? tp + kQSlab : sds;
+          const uint64_t dsd = smem_desc(smem_u32(tds), 16, 1024, kSw128);    // dS' [heads][keys], K-major
+          const uint64_t dst_ = smem_desc(smem_u32(tds), 0, 1024, kSw128);    // dS'^T as MN-major B
+          const uint64_t pt = smem_desc(smem_u32(tp), 0, 1024, kSw128);       // P^T as MN-major B
+          const uint32_t id_q = idesc_bf16(128, (uint32_t)(nqi * 64), false, true);
+          const int ntk = two ? (nqi * 64 + 127) / 128 : args.ntk;
+          const int ntv = two ? (nvi * 64 + 127) / 128 : args.ntv;
+          if (flags & kFirst) {
             if (!(ok = wt(&B.dq_empty, (item_i & 1) ^ 1, st, 13))) break;
-          if (!(ok = wt(&B.pd_full, chunk & 1, st, 14))) break;
+            if (two && !(ok = wt(&B.q_full, item_i & 1, st, 23))) break;
+          }
+          if (two) {
+            if (!(ok = wt(&B.t_full[chunk & 1], (chunk >> 1) & 1, st, 24))) break;
+            if (!(ok = wt(&B.k_full[kuse % KS], (kuse / KS) & 1, st, 25))) break;
+          } else if (!(ok = wt(&B.pd_full, chunk & 1, st, 14))) {
+            break;
+          }
           const int kb = args.nkvb == 2 ? (chunk & 1) : 0;
           const int kuse_b = args.nkvb == 2 ? (chunk >> 1) : chunk;
           if (!(ok = wt(&B.kv_empty[kb], (kuse_b & 1) ^ 1, st, 15))) break;
@@ -402,16 +482,16 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
           const uint64_t kmn = smem_desc(smem_u32(sk + ks * kstage), kSlab, 1024, kSw128);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            mma_bf16_ss(tmem + kColDQ, dsd + (uint64_t)((k * 32) >> 4), kmn + (uint64_t)((k * 2048) >> 4), id_q,
+            mma_bf16_ss(tmem + args.col_dq, dsd + (uint64_t)((k * 32) >> 4), kmn + (uint64_t)((k * 2048) >> 4), id_q,
                         !((flags & kFirst) && k == 0));
           // dK^T tile j = Q^T (dims 128j.., MN-major: 64-dim slabs 16 KB apart) . dS'^T
-          for (int j = 0; j < args.ntk; ++j) {
+          for (int j = 0; j < ntk; ++j) {
             const uint64_t qt = smem_desc(smem_u32(sq + 2 * j * kQSlab), kQSlab, 1024, kSw128);
             for (int k = 0; k < 8; ++k)
               mma_bf16_ss(tmem + kvoff + args.col_dk + 64 * j, qt + (uint64_t)((k * 2048) >> 4),
                           dst_ + (uint64_t)((k * 2048) >> 4), id_kv, k != 0);
           }
-          for (int j = 0; j < args.ntv; ++j) {
+          for (int j = 0; j < ntv; ++j) {
             const uint64_t ot = smem_desc(smem_u32(sdo + 2 * j * kQSlab), kQSlab, 1024, kSw128);
             const uint32_t col = kvoff + (args.merged ? args.col_dk + 64 * j : args.col_dv + 64 * j);
             for (int k = 0; k < 8; ++k)
@@ -419,7 +499,7 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
                           args.merged || k != 0);
           }
           mma_commit(&B.k_empty[ks]);
-          mma_commit(&B.pd_empty);
+          mma_commit(two ? &B.t_empty[chunk & 1] : &B.pd_empty);
           mma_commit(&B.kv_full[kb]);
           if (flags & kLast) {
             mma_commit(&B.dq_full);
@@ -452,11 +532,38 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       const bool hv = d.hg * 128 + m < args.G;
       const int row = d.row, b = d.b, tq = d.tq;
       const uint32_t mlo = d.mlo, mhi = d.mhi;
+      // dq dims of this item: all, or the part's (two-pass form)
+      const int dqn = d.nqi * 64;
       __nv_bfloat16* dqrow = reinterpret_cast<__nv_bfloat16*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)tq * p.dq_st +
-                             (int64_t)h * p.dq_sh;
+                             (int64_t)h * p.dq_sh + (two ? d.part * kPartSlabs * 64 : 0);
       if (flags & kEmpty) {
         if (hv)
-          for (int i = 0; i < p.d_qk; i += 8) *reinterpret_cast<uint4*>(dqrow + i) = make_uint4(0, 0, 0, 0);
+          for (int i = 0; i < dqn; i += 8) *reinterpret_cast<uint4*>(dqrow + i) = make_uint4(0, 0, 0, 0);
+        warp_arrive(&B.jd_empty[js]);
+        ++job;
+        continue;
+      }
+      if (two) {
+        // P and dS' come from the workspace: only the dq epilogue runs here
+        if (flags & kLast) {
+          if (!(ok = wtw(&B.dq_full, item_i & 1, st, 26))) break;
+          tc_fence_after();
+          for (int c0 = 0; c0 < dqn; c0 += 32) {
+            float o[32];
+            tmem_ld32(tl + args.col_dq + c0, o);
+            tmem_ld_wait();
+            if (hv) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 8)
+                *reinterpret_cast<uint4*>(dqrow + c0 + i) =
+                    make_uint4(pack_bf16x2(o[i], o[i + 1]), pack_bf16x2(o[i + 2], o[i + 3]),
+                               pack_bf16x2(o[i + 4], o[i + 5]), pack_bf16x2(o[i + 6], o[i + 7]));
+            }
+          }
+          tc_fence_before();
+          warp_arrive(&B.dq_empty);
+          ++item_i;
+        }
         warp_arrive(&B.jd_empty[js]);
         ++job;
         continue;
@@ -503,9 +610,9 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       if (flags & kLast) {
         if (!(ok = wtw(&B.dq_full, item_i & 1, st, 19))) break;
         tc_fence_after();
-        for (int c0 = 0; c0 < p.d_qk; c0 += 32) {
+        for (int c0 = 0; c0 < dqn; c0 += 32) {
           float o[32];
-          tmem_ld32(tl + kColDQ + c0, o);
+          tmem_ld32(tl + args.col_dq + c0, o);
           tmem_ld_wait();
           if (hv) {
 #pragma unroll
@@ -542,16 +649,19 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         // row (in units of accumulator rows of h_kv heads) of keys lane and lane + 32
         const int64_t r0 = (d.accrow + d.keys[lane]) * p.h_kv + d.hk;
         const int64_t r1 = (d.accrow + d.keys[lane + 32]) * p.h_kv + d.hk;
+        // dims of this item (the part's, in the two-pass form) and its tiles
+        const int nk = d.nqi * 64, nv = d.nvi * 64, d0 = two ? d.part * kPartSlabs * 64 : 0;
+        const int ntk = (nk + 127) / 128, ntv = (nv + 127) / 128;
         const int kb = args.nkvb == 2 ? (chunk & 1) : 0;
         const int kuse_b = args.nkvb == 2 ? (chunk >> 1) : chunk;
         if (!(ok = wtw(&B.kv_full[kb], kuse_b & 1, st, 21))) break;
         tc_fence_after();
-        for (int t = 0; t < args.ntk + (args.merged ? 0 : args.ntv); ++t) {
-          const bool isk = t < args.ntk;
-          const int j = isk ? t : t - args.ntk;
+        for (int t = 0; t < ntk + (args.merged ? 0 : ntv); ++t) {
+          const bool isk = t < ntk;
+          const int j = isk ? t : t - ntk;
           const int D = isk ? p.d_qk : p.d_v;
-          float* acc = (isk ? args.dk_acc : args.dv_acc) + 128 * j + 32 * wq + lane;
-          const bool dim_ok = 128 * j + 32 * wq + lane < D;
+          float* acc = (isk ? args.dk_acc : args.dv_acc) + d0 + 128 * j + 32 * wq + lane;
+          const bool dim_ok = 128 * j + 32 * wq + lane < (isk ? nk : nv);
           const uint32_t col = kb * args.kv_stride + (isk ? args.col_dk + 64 * j : args.col_dv + 64 * j);
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
@@ -587,7 +697,9 @@ struct Plan {
   size_t smem;
 };
 
-static bool plan(const SfaParams& p, Plan* out, const char** why) {
+// two: the two-pass form's gradient half (parts of kPartSlabs slabs; P and dS'
+// from the workspace)
+static bool plan(const SfaParams& p, Plan* out, const char** why, bool two = false) {
   const int G = p.h_q / p.h_kv;
   Args& a = out->a;
   a = Args{};
@@ -596,19 +708,25 @@ static bool plan(const SfaParams& p, Plan* out, const char** why) {
   a.HG = G < 128 ? G : 128;
   a.n_hg = (G + 127) / 128;
   if (G > 128 && G % 128) { *why = "query heads per kv head must be <= 128 or a multiple of 128"; return false; }
-  a.nq = p.d_qk / 64;
-  a.nv = p.d_v / 64;
+  a.nq_all = p.d_qk / 64;
+  a.nv_all = p.d_v / 64;
+  a.parts = two ? (a.nq_all + kPartSlabs - 1) / kPartSlabs : 0;
+  a.nq = two ? kPartSlabs : a.nq_all;
+  a.nv = two ? kPartSlabs : a.nv_all;
   int64_t krows = 0, vrows = 0;
   a.k_rs = gather_rows(p, p.k_sb, p.k_st, p.k_sh, p.d_qk, &krows);
   a.v_rs = gather_rows(p, p.v_sb, p.v_st, p.v_sh, p.d_v, &vrows);
   if (!a.k_rs || !a.v_rs) { *why = "k/v batch, token and head strides must fold into evenly spaced rows"; return false; }
   if (krows > INT32_MAX || vrows > INT32_MAX) { *why = "too many kv rows for 32-bit gather coordinates"; return false; }
-  a.vsrc_k = (p.v == p.k && p.v_sb == p.k_sb && p.v_st == p.k_st && p.v_sh == p.k_sh && p.d_v <= p.d_qk) ? 1 : 0;
+  // the two-pass form gathers no V (dP is not formed here)
+  a.vsrc_k = (two || (p.v == p.k && p.v_sb == p.k_sb && p.v_st == p.k_st && p.v_sh == p.k_sh && p.d_v <= p.d_qk))
+                 ? 1 : 0;
   a.merged = p.dk == p.dv ? 1 : 0;
-  a.ntk = (p.d_qk + 127) / 128;
-  a.ntv = (p.d_v + 127) / 128;
-  // TMEM: S, dP, dQ, dK^T tiles, dV^T tiles
-  a.col_dk = kColDQ + (uint32_t)((p.d_qk + 31) / 32 * 32);
+  a.ntk = (a.nq * 64 + 127) / 128;
+  a.ntv = (a.nv * 64 + 127) / 128;
+  // TMEM: S, dP (one-pass form), dQ, dK^T tiles, dV^T tiles
+  a.col_dq = two ? 0u : kColDQ;
+  a.col_dk = a.col_dq + (uint32_t)(a.nq * 64);
   a.col_dv = a.col_dk + 64u * a.ntk;
   const uint32_t cols = a.col_dv + (a.merged ? 0u : 64u * a.ntv);
   if (cols > kTmemCols) { *why = "token-level backward: dQ plus the dK/dV tiles exceed tensor memory"; return false; }
@@ -616,14 +734,16 @@ static bool plan(const SfaParams& p, Plan* out, const char** why) {
   a.kv_stride = cols - a.col_dk;
   a.nkvb = cols + a.kv_stride <= kTmemCols ? 2 : 1;
   if (a.nkvb == 1) a.kv_stride = 0;
-  // shared memory: Q, dO (16 KB slabs), K ring (full-chunk stages), V ring, P and dS' tiles
+  // shared memory: Q, dO (16 KB slabs), K ring (full-chunk stages), V ring, and
+  // the P and dS' tiles (formed here: one pair; two-pass form: two pairs loaded by TMA)
   const size_t budget = 227 * 1024 - 1024;
   const size_t desc = ((sizeof(Desc) * kJD + 127) / 128) * 128;
   const size_t bars = ((sizeof(Bars) + 127) / 128) * 128;
   const size_t kst = (size_t)a.nq * kSlab, vst = a.vsrc_k ? 0 : (size_t)a.nv * kSlab;
   // regions after Q / dO must cover the 128-dim tiles the dK^T / dV^T MMAs read
   // (a 64-dim Q or dO reads its neighbour's slab for the ignored rows)
-  const size_t fixed = (size_t)(a.nq + a.nv) * kQSlab + 2 * 16384 + desc + bars;
+  const size_t tiles = two ? 2 * (size_t)kTileBytes : 2 * 16384;
+  const size_t fixed = (size_t)(a.nq + a.nv) * kQSlab + tiles + desc + bars;
   int ks = 2, vs = a.vsrc_k ? 0 : 2;
   if (fixed + ks * kst + vs * vst > budget) { *why = "head dims too large for shared memory"; return false; }
   while (ks < 4 || (!a.vsrc_k && vs < 4)) {
@@ -639,12 +759,39 @@ static bool plan(const SfaParams& p, Plan* out, const char** why) {
   a.off_v = a.off_k + (uint32_t)(ks * kst);
   a.off_p = a.off_v + (uint32_t)(vs * vst);
   a.off_ds = a.off_p + 16384;
-  a.off_desc = a.off_ds + 16384;
+  a.off_tiles = a.off_p;
+  a.off_desc = a.off_p + (uint32_t)tiles;
   a.off_bar = a.off_desc + (uint32_t)desc;
   out->smem = a.off_bar + bars + 1024;
   a.nrows = num_rows_host(p);
   a.nitems = a.nrows * p.h_kv * a.n_hg;
   return true;
+}
+
+static cudaError_t launch(const Plan& pl, const SfaParams& p, const CUtensorMap& tp, const CUtensorMap& tds,
+                          cudaStream_t stream) {
+  const Args& a = pl.a;
+  const bool vl = p.cu_seqlens_q != nullptr;
+  const int64_t qrows = vl ? p.total_q : p.q_len;
+  const int64_t nb = vl ? 1 : p.batch;
+  CUtensorMap tq, tdo, tk, tv;
+  cudaError_t e = make_tmap_bf16_4d(&tq, p.q, {(uint64_t)p.d_qk, (uint64_t)p.h_q, (uint64_t)qrows, (uint64_t)nb},
+                                    {p.q_sh, p.q_st, p.q_sb}, {64u, (uint32_t)a.HG, 1u, 1u});
+  if (e != cudaSuccess) return e;
+  e = make_tmap_bf16_4d(&tdo, p.dout, {(uint64_t)p.d_v, (uint64_t)p.h_q, (uint64_t)qrows, (uint64_t)nb},
+                        {p.do_sh, p.do_st, p.do_sb}, {64u, (uint32_t)a.HG, 1u, 1u});
+  if (e != cudaSuccess) return e;
+  int64_t krows = 0, vrows = 0;
+  gather_rows(p, p.k_sb, p.k_st, p.k_sh, p.d_qk, &krows);
+  gather_rows(p, p.v_sb, p.v_st, p.v_sh, p.d_v, &vrows);
+  if ((e = make_tmap_rows(&tk, p.k, (uint64_t)p.d_qk, (uint64_t)krows, a.k_rs)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows(&tv, p.v, (uint64_t)p.d_v, (uint64_t)vrows, a.v_rs)) != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(tokb::sfa_tok_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+  if (e != cudaSuccess) return e;
+  const int grid = a.nitems < device_sm_count() ? a.nitems : device_sm_count();
+  tokb::sfa_tok_bwd_kernel<<<grid, tokb::kThreads, pl.smem, stream>>>(a, tq, tdo, tk, tv, tp, tds);
+  note_launch(a.parts ? "bwd_tok_grad" : "bwd_tok", stream);
+  return cudaGetLastError();
 }
 
 }  // namespace tokb
@@ -671,6 +818,11 @@ bool tok_bwd_supported(const SfaParams& p, const char** why) {
   return tokb::plan(p, &pl, why);
 }
 
+bool tok_bwd_parts_supported(const SfaParams& p, const char** why) {
+  tokb::Plan pl;
+  return tokb::plan(p, &pl, why, true);
+}
+
 cudaError_t launch_bwd_tok(const SfaParams& p, const float* delta, float* dk_acc, float* dv_acc,
                            cudaStream_t stream) {
   tokb::Plan pl;
@@ -681,28 +833,36 @@ cudaError_t launch_bwd_tok(const SfaParams& p, const float* delta, float* dk_acc
   a.delta = delta;
   a.dk_acc = dk_acc;
   a.dv_acc = dv_acc;
-  const bool vl = p.cu_seqlens_q != nullptr;
-  const int64_t qrows = vl ? p.total_q : p.q_len;
-  const int64_t nb = vl ? 1 : p.batch;
-  CUtensorMap tq, tdo, tk, tv;
-  cudaError_t e = make_tmap_bf16_4d(&tq, p.q, {(uint64_t)p.d_qk, (uint64_t)p.h_q, (uint64_t)qrows, (uint64_t)nb},
-                                    {p.q_sh, p.q_st, p.q_sb}, {64u, (uint32_t)a.HG, 1u, 1u});
-  if (e != cudaSuccess) return e;
-  e = make_tmap_bf16_4d(&tdo, p.dout, {(uint64_t)p.d_v, (uint64_t)p.h_q, (uint64_t)qrows, (uint64_t)nb},
-                        {p.do_sh, p.do_st, p.do_sb}, {64u, (uint32_t)a.HG, 1u, 1u});
-  if (e != cudaSuccess) return e;
-  int64_t krows = 0, vrows = 0;
-  gather_rows(p, p.k_sb, p.k_st, p.k_sh, p.d_qk, &krows);
-  gather_rows(p, p.v_sb, p.v_st, p.v_sh, p.d_v, &vrows);
-  if ((e = make_tmap_rows(&tk, p.k, (uint64_t)p.d_qk, (uint64_t)krows, a.k_rs)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows(&tv, p.v, (uint64_t)p.d_v, (uint64_t)vrows, a.v_rs)) != cudaSuccess) return e;
   a.status = device_status_ptr();
-  e = cudaFuncSetAttribute(tokb::sfa_tok_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+  // the P / dS' maps are unused in the one-pass form: any valid map will do
+  CUtensorMap dummy;
+  cudaError_t e = make_tmap_bf16_4d(&dummy, p.q, {64u, 1u, 1u, 1u}, {64, 64, 64}, {64u, 1u, 1u, 1u});
   if (e != cudaSuccess) return e;
-  const int grid = a.nitems < device_sm_count() ? a.nitems : device_sm_count();
-  tokb::sfa_tok_bwd_kernel<<<grid, tokb::kThreads, pl.smem, stream>>>(a, tq, tdo, tk, tv);
-  note_launch("bwd_tok", stream);
-  return cudaGetLastError();
+  return tokb::launch(pl, p, dummy, dummy, stream);
+}
+
+cudaError_t launch_bwd_tok_parts(const SfaParams& p, float* dk_acc, float* dv_acc, const void* pws, const void* dsws,
+                                 int64_t ld, int r0, int r1, cudaStream_t stream) {
+  tokb::Plan pl;
+  const char* why = "";
+  if (!tokb::plan(p, &pl, &why, true)) return cudaErrorInvalidValue;
+  tokb::Args& a = pl.a;
+  a.r0 = r0;
+  a.nitems = (r1 - r0) * p.h_kv * a.n_hg * a.parts;
+  if (a.nitems <= 0) return cudaSuccess;
+  a.dk_acc = dk_acc;
+  a.dv_acc = dv_acc;
+  a.status = device_status_ptr();
+  // P / dS' workspace rows of this wave: [r1 - r0][h_q][ld] bf16, a box of 64 slots x HG heads
+  CUtensorMap tp, tds;
+  const uint64_t wr = (uint64_t)(r1 - r0);
+  cudaError_t e = make_tmap_bf16_4d(&tp, pws, {(uint64_t)ld, (uint64_t)p.h_q, wr, 1u},
+                                    {ld, ld * p.h_q, ld * p.h_q * (int64_t)wr}, {64u, (uint32_t)a.HG, 1u, 1u});
+  if (e != cudaSuccess) return e;
+  e = make_tmap_bf16_4d(&tds, dsws, {(uint64_t)ld, (uint64_t)p.h_q, wr, 1u},
+                        {ld, ld * p.h_q, ld * p.h_q * (int64_t)wr}, {64u, (uint32_t)a.HG, 1u, 1u});
+  if (e != cudaSuccess) return e;
+  return tokb::launch(pl, p, tp, tds, stream);
 }
 
 }  // namespace sfa

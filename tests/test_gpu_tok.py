@@ -231,3 +231,79 @@ def test_reference_signature_backward_on_tensor_cores():
     assert_close("dq", qg.grad.cpu(), rdq)
     assert_close("dkv", kvg.grad.cpu(), rdkv)
     assert_close("dsink", sg.grad.cpu(), rds)
+
+
+# ---------------------------------------------------------------------------
+# backward for head dims above 256: the two-pass form (a stacked [S ; dP]
+# pass writes P and dS' to a workspace, the gradient half reads them per
+# 192-dim part of the head dims); v is k or k's leading dims
+# ---------------------------------------------------------------------------
+def _check_latent_bwd(q, k, idx, Dv, causal=True, sink=None, cu_q=None, cu_k=None, max_q=None, max_k=None):
+    dev = torch.device("cuda")
+    qd = q.to(dev).requires_grad_()
+    kd = k.to(dev).requires_grad_()
+    sd = None if sink is None else sink.to(dev).requires_grad_()
+    vd = kd if Dv == k.shape[-1] else kd[..., :Dv]
+    do = _do(q, k[..., :Dv])
+    o, lse = ops_b200.sparse_flash_attention(
+        qd, kd, vd, idx.to(dev), 1, attn_sink=sd, causal=causal, kernel="tcgen05",
+        cu_seqlens=None if cu_q is None else cu_q.to(dev), cu_seqlens_k=None if cu_k is None else cu_k.to(dev),
+        max_seqlen_q=max_q, max_seqlen_k=max_k)
+    o.backward(do.to(dev))
+    torch.cuda.synchronize()
+    v = k[..., :Dv].float()
+    ro, rl = O.sfa_forward(q.float(), k.float(), v, idx, 1, None, sink, causal, cu_q, cu_k)
+    rdq, rdk, rdv, rds = O.sfa_backward(q.float(), k.float(), v, idx, o.detach().float().cpu(), rl, do.float(), 1,
+                                        None, sink, causal, cu_q, cu_k)
+    dkv = rdk.clone()
+    dkv[..., :Dv] += rdv                               # one tensor: its gradient is dk + dv
+    assert_close("o", o.detach().cpu(), ro)
+    assert_lse(lse.detach().cpu(), rl)
+    assert_close("dq", qd.grad.cpu(), rdq)
+    assert_close("dkv", kd.grad.cpu(), dkv)
+    if sink is not None:
+        assert_close("dsink", sd.grad.cpu(), rds, maxabs=2e-2, rl2=5e-3)
+
+
+def _two_pass_selected(q, k, Dv):
+    # the backward plan takes the two-pass token-level form on tensor cores
+    dev = torch.device("cuda")
+    qd, kd = q[:1, :8].to(dev), k[:1, :8].to(dev)
+    idx = torch.zeros(1, 8, k.shape[2], 1, dtype=torch.int32, device=dev)
+    o = torch.empty(*qd.shape[:-1], Dv, dtype=qd.dtype, device=dev)
+    lse = torch.empty(qd.shape[:-1], device=dev)
+    cfg = S._Cfg(1, q.shape[-1] ** -0.5, True, False, 8, 8, 0, _lib.SFA_KERNEL_TCGEN05, True)
+    P = S.build_params(qd, kd, kd[..., :Dv], idx, o, lse, cfg, None, None, None, torch.empty_like(o),
+                       torch.empty_like(qd), torch.empty_like(kd), torch.empty_like(kd))
+    return _lib.load().sfa_select_kernel(ctypes.byref(P), 1) == _lib.SFA_KERNEL_TCGEN05
+
+
+@pytest.mark.parametrize("B,T,Hq,Hk,Dqk,Dv,K,causal", [
+    (1, 300, 128, 1, 576, 512, 256, True),    # MLA: two 64-head groups, three 192-dim parts
+    (2, 200, 64, 2, 320, 256, 130, True),     # 32 heads a group, parts of 3 + 2 slabs, partial chunk
+    (1, 150, 16, 1, 384, 384, 64, False),     # v is k, 16 heads, non-causal
+])
+def test_two_pass_backward(B, T, Hq, Hk, Dqk, Dv, K, causal):
+    q, k, _, idx = _inputs(B, T, Hq, Hk, Dqk, Dv, K, seed=Hq + Dqk + 3, causal=causal, edge=True)
+    assert _two_pass_selected(q, k, Dv)
+    sink = torch.randn(Hq, generator=torch.Generator().manual_seed(9))
+    _check_latent_bwd(q, k, idx, Dv, causal, sink)
+
+
+def test_two_pass_backward_in_waves(monkeypatch):
+    # rows go through in waves of 37 (the last one ragged); results as in one wave
+    monkeypatch.setenv("SFA_MLA_WAVE_ROWS", "37")
+    q, k, _, idx = _inputs(1, 200, 128, 1, 576, 512, 192, seed=31, edge=True)
+    _check_latent_bwd(q, k, idx, 512)
+
+
+def test_two_pass_backward_varlen():
+    g = torch.Generator().manual_seed(41)
+    q_lens, k_lens = [3, 100, 64], [30, 100, 250]
+    cu_q = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0)), dtype=torch.int32)
+    cu_k = torch.tensor([0] + list(torch.tensor(k_lens).cumsum(0)), dtype=torch.int32)
+    Hq, Hk, Dqk, Dv, K = 64, 1, 576, 512, 80
+    q = torch.randn(int(cu_q[-1]), Hq, Dqk, generator=g).bfloat16()
+    k = torch.randn(int(cu_k[-1]), Hk, Dqk, generator=g).bfloat16()
+    idx = torch.randint(-1, 260, (int(cu_q[-1]), Hk, K), generator=g, dtype=torch.int32)
+    _check_latent_bwd(q, k, idx, Dv, True, None, cu_q, cu_k, max(q_lens), max(k_lens))
