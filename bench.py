@@ -284,11 +284,13 @@ def scaling_kind(split):
     return "weak" if split == "batch" else "strong"
 
 
-def config_dict(cfg, n, split, balance="cost"):
+def config_dict(cfg, n, split, balance="cost", paged=False):
     if cfg.fwd_only:
         return {"workload": f"{cfg.name}: varlen decode forward, {cfg.n_seqs} sequences x 1 query, kv "
                             f"lengths U[{cfg.kv_min}, {cfg.kv_max}], Hq={cfg.Hq}, Hk={cfg.Hk}, Dqk={cfg.Dqk}, "
-                            f"Dv={cfg.Dv}, block_size={cfg.bs}, S={cfg.S} uniform blocks, q/k/v ~ N(0,1)",
+                            f"Dv={cfg.Dv}, block_size={cfg.bs}, S={cfg.S} uniform blocks, q/k/v ~ N(0,1)"
+                            + (f", paged kv cache ({cfg.bs}-row pages at shuffled pool places, block table)"
+                               if paged else ""),
                 "global_batch": cfg.n_seqs,
                 "parallelism": "single GPU" if n == 1 else f"{n} ranks x {cfg.n_seqs // n} sequences",
                 "l2": "flushed between timed steps (256 MiB memset)"}
@@ -659,7 +661,18 @@ def measure_decode(args, cfg, world, rank, dev, steps, warmup, primary):
     o = torch.empty(q.shape[0], cfg.Hq, cfg.Dv, dtype=q.dtype, device=dev)
     lse = torch.empty(q.shape[0], cfg.Hq, dtype=torch.float32, device=dev)
     scfg = S._Cfg(cfg.bs, cfg.scale, True, True, 1, d["max_k"], _lib.SFA_DKV_AUTO, _lib.SFA_KERNEL_AUTO, False)
+    paged = getattr(args, "paged", False)
+    if paged:
+        # the same cache as 64-row pages at shuffled places of one pool, reached
+        # through a block table (the serving layout)
+        kp, vp, table = W.page_kv(k, v, cu_k, cfg.bs, seed=rank_seed(rank) + 1)
+        del d["k"], d["v"], k, v
+        torch.cuda.empty_cache()
+        k = kp.view(-1, *kp.shape[2:])
+        v = vp.view(-1, *vp.shape[2:])
     P = S.build_params(q, k, v, idx, o, lse, scfg, None, cu_q, cu_k)
+    if paged:
+        P.block_table, P.bt_stride, P.page_size = table.data_ptr(), table.stride(0), cfg.bs
     fam = lib.sfa_select_kernel(ctypes.byref(P), 0)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
@@ -697,8 +710,12 @@ def measure_decode(args, cfg, world, rank, dev, steps, warmup, primary):
 
     def e2e_step():
         qd, ixd = (host[n].to(dev, non_blocking=True) for n in ("q", "idx"))
-        oo, _ = ops_b200.sparse_flash_attention(qd, k, v, ixd, cfg.bs, cu_seqlens=cu_qd, cu_seqlens_k=cu_kd,
-                                                max_seqlen_q=1, max_seqlen_k=d["max_k"])
+        if paged:
+            oo, _ = ops_b200.sparse_flash_attention_paged(qd, kp, vp, ixd, table, d["kv_lens"], cfg.bs,
+                                                          max_seqlen_q=1, max_seqlen_k=d["max_k"])
+        else:
+            oo, _ = ops_b200.sparse_flash_attention(qd, k, v, ixd, cfg.bs, cu_seqlens=cu_qd, cu_seqlens_k=cu_kd,
+                                                    max_seqlen_q=1, max_seqlen_k=d["max_k"])
         o_h.copy_(oo, non_blocking=True)
 
     e2e_step()
@@ -726,7 +743,7 @@ def measure_decode(args, cfg, world, rank, dev, steps, warmup, primary):
         "metric": DECODE_METRIC, "value": bytes_all / (step_max * 1e-3) / 1e9,
         "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": step_max,
         "higher_is_better": True, "scaling": "strong" if n_local != cfg.n_seqs else "weak", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic", "config": config_dict(cfg, world, "units"),
+        "dtype": "bf16", "data": "synthetic", "config": config_dict(cfg, world, "units", paged=paged),
         "tflops": 2.0 * keys * G * (cfg.Dqk + cfg.Dv) / (step_ms * 1e-3) / 1e12,
         "kernel_family": {1: "tcgen05", 2: "general"}.get(fam, str(fam)),
         "roofline": {"bound": "hbm", "kernel": "fwd", "achieved": gbs, "peak": hbm, "unit": "GB/s",
@@ -833,6 +850,9 @@ def main():
     ap.add_argument("--balance", choices=["pairs", "cost"], default="cost",
                     help="--split query: balance rows by selected pairs, or by a cost that also counts the "
                          "dK/dV pass's jobs and batches (ops_b200/shard.py row_cost)")
+    ap.add_argument("--paged", action="store_true",
+                    help="decode configurations (c5): the kv cache as 64-row pages of a shuffled pool, reached "
+                         "through a block table (sparse_flash_attention_paged)")
     ap.add_argument("--as-tokens", action="store_true",
                     help="expand a block-level configuration's indices to token level (the same selected keys), "
                          "so the token-level kernels and their query-centric dK/dV run on it")

@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define SFA_ABI_VERSION 1
+#define SFA_ABI_VERSION 2
 
 enum {
   SFA_OK = 0,
@@ -126,7 +126,16 @@ typedef struct SfaParams {
   int32_t kernel;     /* SFA_KERNEL_* */
   int32_t dq_mode;    /* SFA_DQ_* (was reserved: zero = AUTO) */
   int32_t compat;     /* SFA_COMPAT_* bits (was reserved: zero = none) */
-  int32_t reserved;
+  /* Paged kv cache (forward only; no reference counterpart): when block_table
+   * is non-NULL, k and v are page pools of total_kv rows (page p holds rows
+   * [p*page_size, (p+1)*page_size), row stride k_st / v_st), the call is
+   * varlen, cu_seqlens_k gives only the kv lengths (cu_seqlens_k[s+1] -
+   * cu_seqlens_k[s]), and kv position t of sequence s is pool row
+   * block_table[s*bt_stride + t/page_size]*page_size + t%page_size.  With
+   * block_size > 1, page_size must be a multiple of block_size. */
+  int32_t page_size;
+  const int32_t* block_table;
+  int64_t bt_stride;
 } SfaParams;
 
 /* Library / ABI identification. */

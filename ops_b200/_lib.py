@@ -28,6 +28,7 @@ SFA_SELFTEST_STATUS = (15 << 16) | 1   # status code of sfa_selftest_wait_timeou
 _c_void_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
+ABI_VERSION = 2
 
 
 class SfaParams(ctypes.Structure):
@@ -43,7 +44,8 @@ class SfaParams(ctypes.Structure):
         ("batch", _i32), ("q_len", _i32), ("kv_len", _i32), ("total_q", _i32), ("total_kv", _i32),
         ("h_q", _i32), ("h_kv", _i32), ("d_qk", _i32), ("d_v", _i32), ("block_size", _i32),
         ("topk", _i32), ("scale", ctypes.c_float), ("causal", _i32), ("dkv_mode", _i32),
-        ("kernel", _i32), ("dq_mode", _i32), ("compat", _i32), ("reserved", _i32),
+        ("kernel", _i32), ("dq_mode", _i32), ("compat", _i32), ("page_size", _i32),
+        ("block_table", _c_void_p), ("bt_stride", _i64),
     ]
 
 
@@ -96,7 +98,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.argtypes = args
         fn.restype = res
-    if lib.sfa_abi_version() != 1:
+    if lib.sfa_abi_version() != ABI_VERSION:
         raise ImportError("libsfa_b200.so ABI version mismatch")
     _lib = lib
     return lib

@@ -133,6 +133,14 @@ static int validate(const SfaParams* p, bool bwd) {
     return fail(SFA_ERR_INVALID_ARGUMENT, "unknown kernel family");
   if (bwd && p->dq_mode != SFA_DQ_AUTO && p->dq_mode != SFA_DQ_SEPARATE && p->dq_mode != SFA_DQ_FUSED)
     return fail(SFA_ERR_INVALID_ARGUMENT, "unknown dq_mode");
+  if (p->block_table) {
+    if (bwd) return fail(SFA_ERR_UNSUPPORTED, "a paged kv cache is a forward (decode) format: no backward");
+    if (!p->cu_seqlens_q) return fail(SFA_ERR_INVALID_ARGUMENT, "a paged kv cache needs the varlen layout");
+    if (p->page_size <= 0 || p->page_size % p->block_size)
+      return fail(SFA_ERR_INVALID_ARGUMENT, "page_size must be a positive multiple of block_size");
+    if (p->bt_stride < (p->kv_len + p->page_size - 1) / p->page_size)
+      return fail(SFA_ERR_INVALID_ARGUMENT, "bt_stride must cover ceil(kv_len / page_size) pages a sequence");
+  }
   return SFA_OK;
 }
 
@@ -261,7 +269,7 @@ extern "C" {
 int sfa_abi_version(void) { return SFA_ABI_VERSION; }
 
 const char* sfa_build_info(void) {
-  return "sfa_b200 sm_100a (tcgen05/TMA/TMEM + CUDA-core general family), ABI " "1";
+  return "sfa_b200 sm_100a (tcgen05/TMA/TMEM + CUDA-core general family), ABI " "2";
 }
 
 const char* sfa_last_error_string(void) { return g_err.c_str(); }

@@ -31,10 +31,11 @@ struct Row {
   int b;          // batch index used with *_sb strides (0 for varlen)
   int t;          // query index within its sequence
   int64_t tq;     // token index used with *_st strides for q/o/lse/indices
-  int64_t kv0;    // first kv token (used with *_st strides for k/v)
+  int64_t kv0;    // first kv token (used with *_st strides for k/v; 0 for a paged cache)
   int kv_len;     // kv length of the sequence
   int q_len;      // query length of the sequence
   int pos;        // causal position of the query
+  int seq;        // sequence index (dense: b)
 };
 
 __device__ __forceinline__ Row row_info(const SfaParams& p, int row) {
@@ -46,6 +47,7 @@ __device__ __forceinline__ Row row_info(const SfaParams& p, int row) {
     r.kv0 = 0;
     r.kv_len = p.kv_len;
     r.q_len = p.q_len;
+    r.seq = r.b;
   } else {
     int lo = 0, hi = p.batch;  // find s with cu[s] <= row < cu[s+1]
     while (hi - lo > 1) {
@@ -57,12 +59,25 @@ __device__ __forceinline__ Row row_info(const SfaParams& p, int row) {
     r.b = 0;
     r.t = row - q0;
     r.tq = row;
-    r.kv0 = k0;
+    // a paged cache addresses rows through the block table (kv_row)
+    r.kv0 = p.block_table ? 0 : k0;
     r.kv_len = __ldg(p.cu_seqlens_k + lo + 1) - k0;
     r.q_len = __ldg(p.cu_seqlens_q + lo + 1) - q0;
+    r.seq = lo;
   }
   r.pos = r.t + r.kv_len - r.q_len;
   return r;
+}
+
+// Row of kv position t (0 <= t < kv_len) of the row's sequence: kv0 + t, or,
+// for a paged cache, its page's rows in the pool.  With block_size > 1 the
+// caller passes a block's first key (page_size is a multiple of block_size,
+// so the block's keys are consecutive rows).
+__device__ __forceinline__ int64_t kv_row(const SfaParams& p, const Row& r, int t) {
+  if (p.block_table == nullptr) return r.kv0 + t;
+  const int ps = p.page_size;
+  const int pg = __ldg(p.block_table + (int64_t)r.seq * p.bt_stride + t / ps);
+  return (int64_t)pg * ps + t % ps;
 }
 
 __device__ __forceinline__ int num_rows(const SfaParams& p) {

@@ -65,17 +65,21 @@ __global__ void __launch_bounds__(kGenThreads) fwd_general_kernel(SfaParams p, i
   __syncthreads();
 
   for (int base = 0; base < L; base += kKC) {
-    if (tid < kKC) keyid[tid] = slot_key(idx, base + tid, p.block_size, p.topk, r, p.causal);
+    // keyid: the kv row of each slot's key (kv0 + key, or its row in a paged cache), -1 if invalid
+    if (tid < kKC) {
+      const int key = slot_key(idx, base + tid, p.block_size, p.topk, r, p.causal);
+      keyid[tid] = key >= 0 ? (int)kv_row(p, r, key) : -1;
+    }
     __syncthreads();
     int any = __syncthreads_or(tid < kKC && keyid[tid] >= 0);
     if (!any) continue;
     for (int i = tid; i < kKC * Dq; i += kGenThreads) {
       int kk = i / Dq, d = i - kk * Dq, key = keyid[kk];
-      ks[i] = key >= 0 ? bf2f(kb[(r.kv0 + key) * p.k_st + d]) : 0.f;
+      ks[i] = key >= 0 ? bf2f(kb[(int64_t)key * p.k_st + d]) : 0.f;
     }
     for (int i = tid; i < kKC * Dv; i += kGenThreads) {
       int kk = i / Dv, d = i - kk * Dv, key = keyid[kk];
-      vs[i] = key >= 0 ? bf2f(vb[(r.kv0 + key) * p.v_st + d]) : 0.f;
+      vs[i] = key >= 0 ? bf2f(vb[(int64_t)key * p.v_st + d]) : 0.f;
     }
     __syncthreads();
     for (int i = tid; i < nh * kKC; i += kGenThreads) {

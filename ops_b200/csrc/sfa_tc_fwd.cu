@@ -70,7 +70,8 @@ enum : int { kFirst = 1, kLast = 2, kSentinel = 4 };
 
 struct JobDesc {
   int row, hk, b, tq, kv0, kv_len, pos, nblk, flags;
-  int blocks[kSegBlocks];
+  int blocks[kSegBlocks];   // block ids (the softmax's key positions)
+  int prow[kSegBlocks];     // kv row of each block's first key (kv0 + 64 e, or its page's rows)
 };
 
 template <int D>
@@ -274,7 +275,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int bi = 2 * c + half;
-      const int row = bi < d.nblk ? d.kv0 + d.blocks[bi] * 64 : args.oob_row;
+      const int row = bi < d.nblk ? d.prow[bi] : args.oob_row;
 #pragma unroll
       for (int cd = 0; cd < D / 64; ++cd)
         tma_load_4d(dst + cd * 128 * 128 + half * 64 * 128, map, full, cd * 64, d.hk, row, d.b);
@@ -295,9 +296,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
   };
   // TMA row of block slot i of a segment (block ids in registers; a missing
   // block reads rows past the tensor map, i.e. zeros)
-  auto blk_row = [&](const int (&rb)[kSegBlocks], int i, int nb, int kv0) {
-    return i < nb ? kv0 + rb[i] * 64 : args.oob_row;
-  };
+  auto blk_row = [&](const int (&rb)[kSegBlocks], int i, int nb) { return i < nb ? rb[i] : args.oob_row; };
 
   if (warp == 0) {
     // ============================================================ K producer
@@ -358,7 +357,12 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
         const int v0 = __shfl_sync(0xffffffffu, pl0, gi & 31);
         const int v1 = __shfl_sync(0xffffffffu, pl1, gi & 31);
         const int blk = gi < 32 ? v0 : v1;
-        if (lane < nb) d.blocks[lane] = blk;
+        // the block's first kv row (through the block table for a paged cache)
+        const int prow = lane < nb ? (int)kv_row(p, r, blk * 64) : 0;
+        if (lane < nb) {
+          d.blocks[lane] = blk;
+          d.prow[lane] = prow;
+        }
         if (lane == 0) {
           d.row = row;
           d.hk = hk;
@@ -370,10 +374,10 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
           d.nblk = nb;
           d.flags = (seg == 0 ? kFirst : 0) | (seg == nseg - 1 ? kLast : 0);
         }
-        // the segment's block ids into lane 0's registers
+        // the segment's block rows into lane 0's registers
         int rb[kSegBlocks];
 #pragma unroll
-        for (int i = 0; i < kSegBlocks; ++i) rb[i] = __shfl_sync(0xffffffffu, blk, i);
+        for (int i = 0; i < kSegBlocks; ++i) rb[i] = __shfl_sync(0xffffffffu, prow, i);
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&sm.jd_full[js]);
@@ -384,8 +388,8 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
               const int s = use % KS;
               ok = wt(&sm.k_empty[s], ((use / KS) & 1) ^ 1, st, 1);
               if (ok)
-                load_chunk(&tmk, sm.kst[s], &sm.k_full[s], blk_row(rb, 2 * c, nb, (int)r.kv0),
-                           blk_row(rb, 2 * c + 1, nb, (int)r.kv0), hk, r.b);
+                load_chunk(&tmk, sm.kst[s], &sm.k_full[s], blk_row(rb, 2 * c, nb), blk_row(rb, 2 * c + 1, nb), hk,
+                           r.b);
               ++use;
             }
           }

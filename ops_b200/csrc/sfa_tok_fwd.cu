@@ -238,6 +238,10 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         const int fk = lo ? f0 : f1;
         if (!((lo >> lane) & 1u)) e0 = fk;
         if (!((hi >> lane) & 1u)) e1 = fk;
+        if (p.block_table) {                   // paged cache: the keys' rows in the page pool
+          e0 = (int)kv_row(p, r, e0);
+          e1 = (int)kv_row(p, r, e1);
+        }
         const int js = job % kJD;
         if (lane == 0) ok = wt(&B.jd_empty[js], ((job / kJD) & 1) ^ 1, st, 3);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;

@@ -250,6 +250,67 @@ def sparse_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bl
     return o, lse
 
 
+def sparse_flash_attention_paged(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                                 block_indices: torch.Tensor, block_table: torch.Tensor, cache_seqlens: torch.Tensor,
+                                 block_size: int = 64, scale: Optional[float] = None,
+                                 cu_seqlens: Optional[torch.Tensor] = None, attn_sink: Optional[torch.Tensor] = None,
+                                 causal: bool = True, max_seqlen_q: Optional[int] = None,
+                                 max_seqlen_k: Optional[int] = None, kernel: str = "auto"
+                                 ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Sparse attention forward over a paged kv cache (the serving / decode
+    format); returns ``(o, lse)``, no autograd.
+
+    ``k_cache [num_pages, page_size, Hk, Dqk]`` and ``v_cache [num_pages,
+    page_size, Hk, Dv]`` are page pools (``v_cache`` may be ``k_cache`` or its
+    leading dims); ``block_table [n, max_pages]`` (int32) maps sequence s's
+    logical page j to a pool page; ``cache_seqlens [n]`` are the kv lengths.
+    ``q [total_q, Hq, Dqk]`` with ``cu_seqlens [n + 1]`` (default: one query per
+    sequence, the decode step); ``block_indices [total_q, Hk, S]`` selects
+    logical blocks (tokens when ``block_size`` is 1) of each sequence, exactly
+    as on the contiguous varlen surface.  ``page_size`` must be a multiple of
+    ``block_size``.  ``max_seqlen_k`` left unset is read back with a host sync.
+    """
+    _check_inputs(q, k_cache, v_cache, block_indices)
+    if k_cache.dim() != 4 or v_cache.dim() != 4:
+        raise ValueError("k_cache / v_cache must be [num_pages, page_size, Hk, D] page pools")
+    n = block_table.shape[0]
+    npg, ps, hk = k_cache.shape[0], k_cache.shape[1], k_cache.shape[2]
+    for name, c in (("k_cache", k_cache), ("v_cache", v_cache)):
+        if c.shape[:3] != k_cache.shape[:3] or c.stride(-1) != 1 or c.stride(0) != ps * c.stride(1):
+            raise ValueError(f"{name}: pages must be [page_size, Hk, D] row ranges of one pool, innermost dim "
+                             "contiguous")
+    if cu_seqlens is None:
+        if q.shape[0] != n:
+            raise ValueError("without cu_seqlens, q must hold one query per sequence")
+        cu_q = torch.arange(n + 1, dtype=torch.int32, device=q.device)
+        max_seqlen_q = 1
+    else:
+        cu_q = cu_seqlens.to(torch.int32).contiguous()
+        if max_seqlen_q is None:
+            max_seqlen_q = int((cu_q[1:] - cu_q[:-1]).max().item()) if n else 0
+    lens = cache_seqlens.to(torch.int32)
+    cu_k = torch.cat([torch.zeros(1, dtype=torch.int32, device=q.device), lens.cumsum(0, dtype=torch.int32)])
+    if max_seqlen_k is None:
+        max_seqlen_k = int(lens.max().item()) if n else 0
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    # the pools as rows: [num_pages * page_size, Hk, D] (page p = rows p*ps .. p*ps + ps - 1)
+    kpool = torch.as_strided(k_cache, (npg * ps, hk, k_cache.shape[3]), (k_cache.stride(1), k_cache.stride(2), 1))
+    vpool = torch.as_strided(v_cache, (npg * ps, hk, v_cache.shape[3]), (v_cache.stride(1), v_cache.stride(2), 1))
+    table = block_table.to(torch.int32)
+    table = table if table.stride(-1) == 1 else table.contiguous()
+    cfg = _Cfg(int(block_size), float(scale), bool(causal), True, int(max_seqlen_q), int(max_seqlen_k),
+               _lib.SFA_DKV_AUTO, _KERNEL[kernel], False)
+    sink = None if attn_sink is None else attn_sink.float()
+    qq, idx = _inner_contig(q), _idx32(block_indices)
+    o = qq.new_empty(*qq.shape[:-1], v_cache.shape[-1])
+    lse = torch.empty(qq.shape[:-1], dtype=torch.float32, device=q.device)
+    P = build_params(qq, kpool, vpool, idx, o, lse, cfg, sink, cu_q, cu_k)
+    P.block_table, P.bt_stride, P.page_size = table.data_ptr(), table.stride(0), ps
+    _lib.check(_lib.load().sfa_fwd(ctypes.byref(P), None, 0, _stream()), "sfa_fwd (paged)")
+    return o, lse
+
+
 def _has_valid_key(idx: torch.Tensor, cfg: "_Cfg", cu_q, cu_k, hq: int, hk: int) -> torch.Tensor:
     """[.., Hq] bool: the row selected at least one valid key (the kernels'
     rule: block id in range, a key below kv_len and, when causal, at or before

@@ -150,6 +150,39 @@ def make_decode(cfg: Config, device="cpu", seed=0, dtype=torch.bfloat16):
                 kv_lens=kv_lens)
 
 
+def page_kv(k: torch.Tensor, v: torch.Tensor, cu_k: torch.Tensor, page_size: int, seed: int = 0):
+    """A varlen kv cache ([total_kv, Hk, D] rows, sequence s at rows cu_k[s]..)
+    laid out as a paged cache: every sequence's rows cut into pages of
+    page_size rows, the pages placed at shuffled positions of one pool.
+    Returns (k_pool, v_pool, block_table) with pools [num_pages, page_size,
+    Hk, D] (rows past a sequence's end zero) and block_table [n, max_pages]
+    int32 (-1 past a sequence's pages).  Vectorised, on k's device."""
+    dev = k.device
+    cu = cu_k.to(device=dev, dtype=torch.int64)
+    lens = cu[1:] - cu[:-1]
+    n = lens.numel()
+    npg = (lens + page_size - 1) // page_size
+    total = int(npg.sum())
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    perm = torch.randperm(total, generator=gen, device=dev)
+    seq = torch.repeat_interleave(torch.arange(n, device=dev), npg)          # sequence of each page
+    first = torch.cumsum(npg, 0) - npg
+    j = torch.arange(total, device=dev) - first[seq]                          # page index within its sequence
+    table = torch.full((n, int(npg.max()) if n else 0), -1, dtype=torch.int32, device=dev)
+    table[seq, j] = perm.to(torch.int32)
+    r = torch.arange(page_size, device=dev)
+    pos = j[:, None] * page_size + r[None, :]                                 # kv position of each pool row
+    ok = pos < lens[seq][:, None]
+    src = (cu[:-1][seq][:, None] + pos)[ok]
+    dst = (perm[:, None] * page_size + r[None, :])[ok]
+    pools = []
+    for t in (k, v):
+        pool = torch.zeros(total * page_size, *t.shape[1:], dtype=t.dtype, device=dev)
+        pool[dst] = t[src]
+        pools.append(pool.view(total, page_size, *t.shape[1:]))
+    return pools[0], pools[1], table
+
+
 def make_inputs(cfg: Config, device="cpu", seed=0, dtype=torch.bfloat16, with_do=True):
     """Dense configs: dict(q, k, v, idx, do).  Decode: see make_decode."""
     if cfg.mode == "decode":

@@ -27,7 +27,7 @@ def test_library_loads_and_exports_all_declared_symbols():
     for n in names:
         assert hasattr(lib, n), n
         assert n in _lib.EXPORTS, f"{n} has no ctypes signature"
-    assert lib.sfa_abi_version() == 1
+    assert lib.sfa_abi_version() == _lib.ABI_VERSION == 2
     assert b"sm_100a" in lib.sfa_build_info()
 
 
@@ -103,3 +103,22 @@ def test_backward_plan_is_consistent_with_the_launch_table():
     P.dq_mode = 5
     assert lib.sfa_bwd_plan(ctypes.byref(P), ctypes.byref(dkv), ctypes.byref(dq)) == _lib.SFA_ERR_INVALID_ARGUMENT
     assert "dq_mode" in lib.sfa_last_error_string().decode()
+
+
+def test_paged_cache_rules_without_gpu():
+    # a paged kv cache is a varlen forward format: the backward is refused, the
+    # page size must hold whole blocks and the table must cover kv_len
+    lib = _lib.load()
+    fake = 0x30000
+    paged = dict(block_table=fake, bt_stride=4, page_size=64, cu_seqlens_q=fake, cu_seqlens_k=fake,
+                 total_q=1, total_kv=256, kv_len=200)
+    P = _params(**paged)
+    assert lib.sfa_select_kernel(ctypes.byref(P), 0) >= 0
+    Pb = _params(dout=fake, dq=fake, dk=fake, dv=fake + 0x1000, **paged)
+    assert lib.sfa_select_kernel(ctypes.byref(Pb), 1) == _lib.SFA_ERR_UNSUPPORTED
+    assert "backward" in lib.sfa_last_error_string().decode()
+    for bad, msg in ((dict(page_size=96), "page_size"), (dict(bt_stride=3), "bt_stride"),
+                     (dict(cu_seqlens_q=None, cu_seqlens_k=None), "varlen")):
+        P = _params(**{**paged, **bad})
+        assert lib.sfa_select_kernel(ctypes.byref(P), 0) == _lib.SFA_ERR_INVALID_ARGUMENT
+        assert msg in lib.sfa_last_error_string().decode()

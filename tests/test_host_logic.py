@@ -161,3 +161,22 @@ def test_valid_key_mask_matches_the_oracle_rule():
         for h in range(Hk):
             _, ok = O.key_table(vidx[q0:q1, h], bs, pos, kl, True)
             assert torch.equal(got[q0:q1, h * G:(h + 1) * G], ok.any(-1)[:, None].expand(q1 - q0, G))
+
+
+def test_page_kv_keeps_every_row_and_table_maps_back():
+    # the paged layout holds every sequence's rows once, at the rows the block
+    # table names (the kernels' mapping: page table[s][t // ps], row t % ps)
+    g = torch.Generator().manual_seed(4)
+    lens = torch.tensor([5, 64, 65, 130])
+    cu = torch.cat([torch.zeros(1, dtype=torch.int64), lens.cumsum(0)])
+    k = torch.randn(int(cu[-1]), 2, 8, generator=g)
+    v = torch.randn(int(cu[-1]), 2, 4, generator=g)
+    kp, vp, table = W.page_kv(k, v, cu, 64, seed=1)
+    assert kp.shape[1:] == (64, 2, 8) and vp.shape[1:] == (64, 2, 4)
+    assert kp.shape[0] == int(((lens + 63) // 64).sum())
+    for s in range(lens.numel()):
+        t = torch.arange(int(lens[s]))
+        pg = table[s, t // 64].long()
+        assert torch.equal(kp[pg, t % 64], k[cu[s] + t])
+        assert torch.equal(vp[pg, t % 64], v[cu[s] + t])
+    assert sorted(table[table >= 0].tolist()) == list(range(kp.shape[0]))
