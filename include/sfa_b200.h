@@ -242,6 +242,38 @@ int sfa_reset_device_status(void* stream);
 #define SFA_SELFTEST_STATUS ((15 << 16) | 1)
 int sfa_selftest_wait_timeout(void* stream, uint32_t limit_us);
 
+/* ------------------------------------------------------------------------
+ * Top-k token indexer: the step before the op, producing its token-level
+ * indices (the reference consumes topk_idxs and has no indexer, SFA.py:90).
+ * Scores follow the lightning-indexer formula of DeepSeek-V3.2's sparse
+ * attention:  I[t, s] = sum_h w[t, h] * ReLU(q_idx[t, h] . k_idx[s]),  s a key
+ * of t's sequence (s <= t + kv_len - q_len when causal).  The output row of t
+ * holds the indices of the topk highest scores (ties: the lower index first)
+ * in ascending order, then -1 when fewer keys exist — the layout the op's
+ * token-level surface and the reference take as-is.
+ *
+ * Dense layout: q_idx [B, Tq, H, D] bf16, k_idx [B, Tk, D] bf16 (one head
+ * shared by every query head), weights [B, Tq, H] fp32, out [B, Tq, topk]
+ * int32; strides in elements, innermost dims contiguous.  H is 64 or 32,
+ * D is 64 or 128, topk <= 4096 (fp32 scores of a row go through shared
+ * memory: Tk <= 49152).  The workspace holds fp32 scores for a wave of rows. */
+typedef struct SfaIndexerParams {
+  const void* q_idx;
+  const void* k_idx;
+  const float* weights;
+  int32_t* out;
+  int64_t q_sb, q_st, q_sh;
+  int64_t k_sb, k_st;
+  int64_t w_sb, w_st;
+  int64_t o_sb, o_st;
+  int32_t batch, q_len, kv_len, heads, dim, topk;
+  int32_t causal;
+  int32_t reserved;
+} SfaIndexerParams;
+
+size_t sfa_indexer_workspace_bytes(const SfaIndexerParams* p);
+int sfa_indexer_topk(const SfaIndexerParams* p, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

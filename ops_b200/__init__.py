@@ -5,12 +5,15 @@ Public surface:
   SparseFlashAttention.apply(q, kv, attn_sink, topk_idxs, sm_scale) -> out   # reference signature
   sparse_flash_attention_paged(q, k_cache, v_cache, block_indices, block_table, cache_seqlens, ...)
                                                       # forward over a paged kv cache (decode)
+  lightning_indexer_topk(q_idx, k_idx, weights, topk) -> token indices for the op
 The kernels live in libsfa_b200.so (C ABI: include/sfa_b200.h).
 """
 from ._lib import SfaError, SfaParams, load as load_library
 from .sfa import (SparseFlashAttention, SparseFlashAttentionCompat, reference_lse2, sparse_flash_attention,
                   sparse_flash_attention_paged)
 from . import tiling
+from .indexer import lightning_indexer_topk
 
 __all__ = ["sparse_flash_attention", "sparse_flash_attention_paged", "SparseFlashAttention",
-           "SparseFlashAttentionCompat", "SfaError", "SfaParams", "load_library", "reference_lse2", "tiling"]
+           "SparseFlashAttentionCompat", "SfaError", "SfaParams", "load_library", "reference_lse2", "tiling",
+           "lightning_indexer_topk"]

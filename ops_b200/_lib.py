@@ -49,6 +49,18 @@ class SfaParams(ctypes.Structure):
     ]
 
 
+class SfaIndexerParams(ctypes.Structure):
+    """Field-for-field mirror of ``SfaIndexerParams`` in include/sfa_b200.h."""
+
+    _fields_ = [
+        ("q_idx", _c_void_p), ("k_idx", _c_void_p), ("weights", _c_void_p), ("out", _c_void_p),
+        ("q_sb", _i64), ("q_st", _i64), ("q_sh", _i64), ("k_sb", _i64), ("k_st", _i64),
+        ("w_sb", _i64), ("w_st", _i64), ("o_sb", _i64), ("o_st", _i64),
+        ("batch", _i32), ("q_len", _i32), ("kv_len", _i32), ("heads", _i32), ("dim", _i32), ("topk", _i32),
+        ("causal", _i32), ("reserved", _i32),
+    ]
+
+
 EXPORTS = {
     "sfa_abi_version": ([], _i32),
     "sfa_build_info": ([], ctypes.c_char_p),
@@ -74,6 +86,8 @@ EXPORTS = {
     "sfa_launch_trace": ([ctypes.POINTER(_c_void_p), _i32], _i32),
     "sfa_launch_trace_count": ([], _i32),
     "sfa_launch_trace_name": ([_i32], ctypes.c_char_p),
+    "sfa_indexer_workspace_bytes": ([ctypes.POINTER(SfaIndexerParams)], ctypes.c_size_t),
+    "sfa_indexer_topk": ([ctypes.POINTER(SfaIndexerParams), _c_void_p, ctypes.c_size_t, _c_void_p], _i32),
 }
 
 _lib = None

@@ -31,12 +31,14 @@ def test_library_loads_and_exports_all_declared_symbols():
     assert b"sm_100a" in lib.sfa_build_info()
 
 
-def test_struct_layout_matches_header():
-    fields = [f[0] for f in _lib.SfaParams._fields_]
+@pytest.mark.parametrize("struct", ["SfaParams", "SfaIndexerParams"])
+def test_struct_layout_matches_header(struct):
+    cls = getattr(_lib, struct)
+    fields = [f[0] for f in cls._fields_]
     prog = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void){",
-            'printf("%zu\\n", sizeof(SfaParams));']
+            f'printf("%zu\\n", sizeof({struct}));']
     for f in fields:
-        prog.append(f'printf("%zu\\n", offsetof(SfaParams, {f}));')
+        prog.append(f'printf("%zu\\n", offsetof({struct}, {f}));')
     prog.append("return 0;}")
     with tempfile.TemporaryDirectory() as d:
         c = os.path.join(d, "t.c")
@@ -44,9 +46,9 @@ def test_struct_layout_matches_header():
         exe = os.path.join(d, "t")
         subprocess.run(["gcc", c, "-o", exe], check=True)
         out = [int(x) for x in subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()]
-    assert out[0] == ctypes.sizeof(_lib.SfaParams)
+    assert out[0] == ctypes.sizeof(cls)
     for f, off in zip(fields, out[1:]):
-        assert getattr(_lib.SfaParams, f).offset == off, f
+        assert getattr(cls, f).offset == off, f
 
 
 def _params(**kw):
@@ -121,4 +123,22 @@ def test_paged_cache_rules_without_gpu():
                      (dict(cu_seqlens_q=None, cu_seqlens_k=None), "varlen")):
         P = _params(**{**paged, **bad})
         assert lib.sfa_select_kernel(ctypes.byref(P), 0) == _lib.SFA_ERR_INVALID_ARGUMENT
+        assert msg in lib.sfa_last_error_string().decode()
+
+
+def test_indexer_argument_validation_without_gpu():
+    lib = _lib.load()
+    fake = 0x40000
+    base = dict(q_idx=fake, k_idx=fake, weights=fake, out=fake, q_sb=64 * 64 * 128, q_st=64 * 128, q_sh=128,
+                k_sb=64 * 128, k_st=128, w_sb=64 * 64, w_st=64, o_sb=64 * 8, o_st=8,
+                batch=1, q_len=64, kv_len=64, heads=64, dim=128, topk=8, causal=1)
+    P = _lib.SfaIndexerParams(**base)
+    assert lib.sfa_indexer_workspace_bytes(ctypes.byref(P)) == 64 * 128 * 4
+    for bad, code, msg in ((dict(heads=48), _lib.SFA_ERR_UNSUPPORTED, "heads"),
+                           (dict(dim=96), _lib.SFA_ERR_UNSUPPORTED, "dim"),
+                           (dict(topk=0), _lib.SFA_ERR_INVALID_ARGUMENT, "topk"),
+                           (dict(kv_len=60000), _lib.SFA_ERR_UNSUPPORTED, "kv_len"),
+                           (dict(q_idx=0), _lib.SFA_ERR_INVALID_ARGUMENT, "non-NULL")):
+        P = _lib.SfaIndexerParams(**{**base, **bad})
+        assert lib.sfa_indexer_topk(ctypes.byref(P), None, 0, None) == code
         assert msg in lib.sfa_last_error_string().decode()

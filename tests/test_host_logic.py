@@ -180,3 +180,26 @@ def test_page_kv_keeps_every_row_and_table_maps_back():
         assert torch.equal(kp[pg, t % 64], k[cu[s] + t])
         assert torch.equal(vp[pg, t % 64], v[cu[s] + t])
     assert sorted(table[table >= 0].tolist()) == list(range(kp.shape[0]))
+
+
+def test_indexer_oracle_selection_rule():
+    from oracle import indexer_oracle as IO
+    # scores with ties: the lower index wins, output ascending, -1 tail
+    sc = torch.tensor([[[1.0, 3.0, 3.0, 2.0, 3.0, 0.5]]])
+    q = torch.zeros(1, 1, 1, 1)
+    k = torch.zeros(1, 6, 1)
+    w = torch.zeros(1, 1, 1)
+    got = IO.indexer_topk(q, k, w, 2, causal=False, scores=sc)
+    assert got.tolist() == [[[1, 2]]]
+    got = IO.indexer_topk(q, k, w, 4, causal=False, scores=sc)
+    assert got.tolist() == [[[1, 2, 3, 4]]]
+    got = IO.indexer_topk(q, k, w, 8, causal=False, scores=sc)
+    assert got.tolist() == [[[0, 1, 2, 3, 4, 5, -1, -1]]]
+    # causal with Tq == Tk: row t sees keys 0..t
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(1, 5, 2, 4, generator=g)
+    k = torch.randn(1, 5, 4, generator=g)
+    w = torch.rand(1, 5, 2, generator=g)
+    got = IO.indexer_topk(q, k, w, 3, causal=True)
+    assert got[0, 0].tolist() == [0, -1, -1] and got[0, 1].tolist() == [0, 1, -1]
+    assert (got[0, 4] >= 0).all()
