@@ -788,6 +788,60 @@ def compact(line, cpu):
     return out
 
 
+def measure_indexer(dev, T=32768, H=64, D=128, topk=2048, steps=5, warmup=3):
+    """The top-k token indexer on config 4's sequence (T = 32768, causal) with
+    DeepSeek-V3.2's indexer shape (64 heads x 128 dims, top-2048): scoring
+    FLOPs 2 * H * D per (query, key) pair, per-kernel CUDA-event times."""
+    import torch
+
+    from ops_b200 import _lib
+    from ops_b200.indexer import lightning_indexer_topk
+
+    lib = _lib.load()
+    g = torch.Generator(device=dev).manual_seed(11)
+    q = torch.randn(1, T, H, D, generator=g, device=dev).bfloat16()
+    k = torch.randn(1, T, D, generator=g, device=dev).bfloat16()
+    w = torch.rand(1, T, H, generator=g, device=dev) / H
+    for _ in range(warmup):
+        lightning_indexer_topk(q, k, w, topk)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    NEV = 32
+    kern = {}
+    tot = 0.0
+    for _ in range(steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        tr = [torch.cuda.Event(enable_timing=True) for _ in range(NEV)]
+        for e in tr:
+            e.record(stream)
+        torch.cuda.synchronize()
+        hs = (ctypes.c_void_p * NEV)(*[e.cuda_event for e in tr])
+        a.record(stream)
+        lib.sfa_launch_trace(hs, NEV)
+        lightning_indexer_topk(q, k, w, topk)
+        n = lib.sfa_launch_trace_count()
+        names = [lib.sfa_launch_trace_name(j).decode() for j in range(n)]
+        lib.sfa_launch_trace(None, 0)
+        b.record(stream)
+        torch.cuda.synchronize()
+        tot += a.elapsed_time(b) / steps
+        prev = a
+        for j in range(n):
+            kern[names[j]] = kern.get(names[j], 0.0) + prev.elapsed_time(tr[j]) / steps
+            prev = tr[j]
+    pairs = T * (T + 1) // 2
+    flops = 2.0 * H * D * pairs
+    peak, _, kind = peaks()
+    sc = kern.get("indexer_score", 0.0)
+    return {"workload": f"top-{topk} token indexer, B=1, T={T} causal, {H} heads x {D} dims (config 4's "
+                        "sequence, DeepSeek-V3.2 indexer shape), q/k ~ N(0,1)",
+            "ms_per_call": tot, "tflops": flops / (tot * 1e-3) / 1e12,
+            "kernels": {n: round(m, 4) for n, m in kern.items()},
+            "roofline": {"bound": "tensor", "kernel": "indexer_score", "achieved": flops / (sc * 1e-3) / 1e12,
+                         "peak": peak, "unit": "TFLOP/s", "frac": flops / (sc * 1e-3) / 1e12 / peak,
+                         "peak_kind": f"{kind} bf16 burst", "algorithmic": f"2*H*D per causal pair: {flops:.3e} FLOP"}}
+
+
 def run_ours(args, cfg):
     import datetime
 
@@ -828,6 +882,9 @@ def run_ours(args, cfg):
         return
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(cfg)
+    if world == 1 and args.configs != "none":
+        # the step before the op: the top-k indexer that produces token-level indices
+        line["indexer"] = measure_indexer(torch.device("cuda", local))
     if extra:
         line["configs"] = {n: compact(s, c) for n, (s, c) in extra.items()}
     print(json.dumps(line), flush=True)
@@ -850,6 +907,8 @@ def main():
     ap.add_argument("--balance", choices=["pairs", "cost"], default="cost",
                     help="--split query: balance rows by selected pairs, or by a cost that also counts the "
                          "dK/dV pass's jobs and batches (ops_b200/shard.py row_cost)")
+    ap.add_argument("--indexer", action="store_true",
+                    help="measure only the top-k token indexer (config 4's sequence) and print its line")
     ap.add_argument("--paged", action="store_true",
                     help="decode configurations (c5): the kv cache as 64-row pages of a shuffled pool, reached "
                          "through a block table (sparse_flash_attention_paged)")
@@ -870,7 +929,11 @@ def main():
         cfg = W.scaled(cfg, T=args.seq)
     if args.batch or args.seq:
         args.configs = "none"
-    if args.impl == "reference":
+    if args.indexer:
+        import torch
+        torch.cuda.set_device(0)
+        print(json.dumps(measure_indexer(torch.device("cuda", 0))), flush=True)
+    elif args.impl == "reference":
         run_reference(args, cfg)
     else:
         run_ours(args, cfg)
