@@ -28,7 +28,8 @@
 //   warp 1          MMA issuer A: S and dP;
 //   warp 2          MMA issuer B: dQ, dK^T, dV^T;
 //   warps 3, 8-11   gather pool: K (and V) slabs, a fixed owner per ring position;
-//   warps 4-7       P / dS' (thread = head row) and the dq epilogue;
+//   warps 4-7       P / dS' (thread = head row) and the dq epilogue (two-pass
+//                   form: the second half of the drain and the dq epilogue);
 //   warps 12-15     drain: dK^T / dV^T tiles (thread = dim) -> fp32 reductions.
 // Every wait is bounded (~2 s); on expiry the kernel records (5 << 16) | site in
 // the status word and returns.
@@ -169,7 +170,7 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
     mbar_init(&B.dq_empty, 4);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&B.kv_full[i], 1);
-      mbar_init(&B.kv_empty[i], 4);
+      mbar_init(&B.kv_empty[i], two ? 8 : 4);     // the two-pass form drains from eight warps
     }
     // consumers of a descriptor: two MMA issuers (one in the two-pass form), the
     // gather pool, P/dS warps, drain warps
@@ -215,6 +216,51 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
   tc_fence_after();
   const uint32_t tmem = B.tmem_base;
   const int quad = lane & 15;
+
+  // Drain of one chunk's dK^T / dV^T tiles (TMEM lanes = dims, columns = keys)
+  // into the fp32 accumulators, key halves [h_lo, h_hi) of 32 keys each.  Each
+  // lane holds two of the chunk's keys (i and i + 32) and those keys'
+  // accumulator rows; a reduction takes its key's row from the owning lane by
+  // shuffle, so the loop is shuffle + reduction, a warp covering 32
+  // consecutive dims (128 bytes) of one key per instruction.
+  auto drain_chunk = [&](const Desc& d, int chunk, int h_lo, int h_hi, int site) -> bool {
+    const int wq = warp & 3;                 // TMEM lanes 32*wq.. = dims 32*wq.. of a 128-dim tile
+    const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
+    const uint32_t mlo = d.mlo, mhi = d.mhi;
+    // accumulator row (units of h_kv-head rows; below 2^31, as the gather rows) of keys lane, lane + 32
+    const int r0 = (int)((d.accrow + d.keys[lane]) * p.h_kv + d.hk);
+    const int r1 = (int)((d.accrow + d.keys[lane + 32]) * p.h_kv + d.hk);
+    // dims of this item (the part's, in the two-pass form) and its tiles
+    const int nk = d.nqi * 64, nv = d.nvi * 64, d0 = two ? d.part * kPartSlabs * 64 : 0;
+    const int ntk = (nk + 127) / 128, ntv = (nv + 127) / 128;
+    const int kb = args.nkvb == 2 ? (chunk & 1) : 0;
+    const int kuse_b = args.nkvb == 2 ? (chunk >> 1) : chunk;
+    if (!wtw(&B.kv_full[kb], kuse_b & 1, st, site)) return false;
+    tc_fence_after();
+    for (int t = 0; t < ntk + (args.merged ? 0 : ntv); ++t) {
+      const bool isk = t < ntk;
+      const int j = isk ? t : t - ntk;
+      const int D = isk ? p.d_qk : p.d_v;
+      float* acc = (isk ? args.dk_acc : args.dv_acc) + d0 + 128 * j + 32 * wq + lane;
+      const bool dim_ok = 128 * j + 32 * wq + lane < (isk ? nk : nv);
+      const uint32_t col = kb * args.kv_stride + (isk ? args.col_dk + 64 * j : args.col_dv + 64 * j);
+      for (int hh = h_lo; hh < h_hi; ++hh) {
+        float v[32];
+        tmem_ld32(tl + col + 32 * hh, v);
+        tmem_ld_wait();
+        const uint32_t msk = hh ? mhi : mlo;
+        const int rr = hh ? r1 : r0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int ri = __shfl_sync(0xffffffffu, rr, i);
+          if (((msk >> i) & 1u) && dim_ok) atomicAdd(acc + (int64_t)ri * D, v[i]);
+        }
+      }
+    }
+    tc_fence_before();
+    warp_arrive(&B.kv_empty[kb]);
+    return true;
+  };
 
   if (warp == 0) {
     // ============================================================ descriptor producer
@@ -544,7 +590,10 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         continue;
       }
       if (two) {
-        // P and dS' come from the workspace: only the dq epilogue runs here
+        // P and dS' come from the workspace: these warps drain keys 32-63 of the
+        // chunk's dK^T / dV^T tiles and run the dq epilogue
+        if (!(ok = drain_chunk(d, chunk, 1, 2, 27))) break;
+        ++chunk;
         if (flags & kLast) {
           if (!(ok = wtw(&B.dq_full, item_i & 1, st, 26))) break;
           tc_fence_after();
@@ -631,11 +680,7 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
     }
   } else {
     // ============================================================ drain (warps 12-15)
-    // Each lane holds two of the chunk's keys (i and i + 32) and those keys'
-    // accumulator row offsets; a reduction takes its key's offset from the
-    // owning lane by shuffle, so the loop is shuffle + reduction only.
-    const int wq = warp & 3;                 // TMEM lanes 32*wq.. = dims 32*wq.. of a 128-dim tile
-    const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
+    // (keys 0-31 of each chunk in the two-pass form, where warps 4-7 take 32-63)
     int job = 0, chunk = 0;
     bool ok = true;
     while (ok) {
@@ -645,40 +690,7 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       const int flags = d.flags;
       if (flags & kSentinel) break;
       if (!(flags & kEmpty)) {
-        const uint32_t mlo = d.mlo, mhi = d.mhi;
-        // row (in units of accumulator rows of h_kv heads) of keys lane and lane + 32
-        const int64_t r0 = (d.accrow + d.keys[lane]) * p.h_kv + d.hk;
-        const int64_t r1 = (d.accrow + d.keys[lane + 32]) * p.h_kv + d.hk;
-        // dims of this item (the part's, in the two-pass form) and its tiles
-        const int nk = d.nqi * 64, nv = d.nvi * 64, d0 = two ? d.part * kPartSlabs * 64 : 0;
-        const int ntk = (nk + 127) / 128, ntv = (nv + 127) / 128;
-        const int kb = args.nkvb == 2 ? (chunk & 1) : 0;
-        const int kuse_b = args.nkvb == 2 ? (chunk >> 1) : chunk;
-        if (!(ok = wtw(&B.kv_full[kb], kuse_b & 1, st, 21))) break;
-        tc_fence_after();
-        for (int t = 0; t < ntk + (args.merged ? 0 : ntv); ++t) {
-          const bool isk = t < ntk;
-          const int j = isk ? t : t - ntk;
-          const int D = isk ? p.d_qk : p.d_v;
-          float* acc = (isk ? args.dk_acc : args.dv_acc) + d0 + 128 * j + 32 * wq + lane;
-          const bool dim_ok = 128 * j + 32 * wq + lane < (isk ? nk : nv);
-          const uint32_t col = kb * args.kv_stride + (isk ? args.col_dk + 64 * j : args.col_dv + 64 * j);
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            float v[32];
-            tmem_ld32(tl + col + 32 * hh, v);
-            tmem_ld_wait();
-            const uint32_t msk = hh ? mhi : mlo;
-            const int64_t rr = hh ? r1 : r0;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int64_t ri = __shfl_sync(0xffffffffu, rr, i);
-              if (((msk >> i) & 1u) && dim_ok) atomicAdd(acc + ri * D, v[i]);
-            }
-          }
-        }
-        tc_fence_before();
-        warp_arrive(&B.kv_empty[kb]);
+        if (!(ok = drain_chunk(d, chunk, 0, two ? 1 : 2, 21))) break;
         ++chunk;
       }
       warp_arrive(&B.jd_empty[js]);
