@@ -61,7 +61,7 @@ constexpr int kJD = 4;
 constexpr int kSlab = 64 * 128;        // 64 rows x 64 dims bf16
 constexpr int kQSlab = 128 * 128;      // 128 head rows x 64 dims bf16
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColDP = 64, kColDQ = 128;
+constexpr uint32_t kSDCols = 128;      // one S / dP buffer: S [0, 64), dP [64, 128)
 constexpr int kPartSlabs = 3;          // two-pass form: 64-dim slabs of q/k per part
 constexpr int kTileBytes = 2 * kQSlab; // two-pass form: P and dS' tiles of one chunk
 
@@ -98,13 +98,14 @@ struct Args {
   int nq_all, nv_all;                  // 64-dim slabs of d_qk / d_v
   int r0;                              // first row of the wave
   uint32_t col_dq;                     // TMEM column of dQ
+  int nsd, npd;                        // S / dP buffers in TMEM, P / dS' tile pairs in shared memory
   uint32_t off_tiles;                  // P / dS' tile buffers [2][kTileBytes]
 };
 
 struct Bars {
   uint64_t q_full, q_empty;
-  uint64_t sd_full, sd_empty;          // S / dP in TMEM
-  uint64_t pd_full, pd_empty;          // P / dS' tiles in shared memory
+  uint64_t sd_full[2], sd_empty[2];    // S / dP in TMEM (double-buffered when TMEM allows)
+  uint64_t pd_full[2], pd_empty[2];    // P / dS' tiles in shared memory (double-buffered when it fits)
   uint64_t dq_full, dq_empty;          // dQ accumulator
   uint64_t kv_full[2], kv_empty[2];    // dK^T / dV^T tiles (double-buffered when TMEM allows)
   uint64_t jd_full[kJD], jd_empty[kJD];
@@ -162,10 +163,12 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
   if (threadIdx.x == 0) {
     mbar_init(&B.q_full, 1);
     mbar_init(&B.q_empty, 1);
-    mbar_init(&B.sd_full, 1);
-    mbar_init(&B.sd_empty, 4);
-    mbar_init(&B.pd_full, 4);
-    mbar_init(&B.pd_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&B.sd_full[i], 1);
+      mbar_init(&B.sd_empty[i], 4);
+      mbar_init(&B.pd_full[i], 4);
+      mbar_init(&B.pd_empty[i], 1);
+    }
     mbar_init(&B.dq_full, 1);
     mbar_init(&B.dq_empty, 4);
     for (int i = 0; i < 2; ++i) {
@@ -449,7 +452,8 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
             if (!(ok = wt(&B.q_full, item_i & 1, st, 8))) break;
             ++item_i;
           }
-          if (!(ok = wt(&B.sd_empty, (chunk & 1) ^ 1, st, 9))) break;
+          const int sb = chunk % args.nsd;
+          if (!(ok = wt(&B.sd_empty[sb], ((chunk / args.nsd) & 1) ^ 1, st, 9))) break;
           const int ks = kuse % KS;
           if (!(ok = wt(&B.k_full[ks], (kuse / KS) & 1, st, 10))) break;
           tc_fence_after();
@@ -458,7 +462,7 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
             const uint64_t qd = smem_desc(smem_u32(sq + s * kQSlab), 16, 1024, kSw128);
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              mma_bf16_ss(tmem + kColS, qd + (uint64_t)((k * 32) >> 4), kd + (uint64_t)((k * 32) >> 4), id_s,
+              mma_bf16_ss(tmem + sb * kSDCols, qd + (uint64_t)((k * 32) >> 4), kd + (uint64_t)((k * 32) >> 4), id_s,
                           (s | k) != 0);
           }
           const uint8_t* vstg = sk + ks * kstage;
@@ -473,11 +477,11 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
             const uint64_t od = smem_desc(smem_u32(sdo + s * kQSlab), 16, 1024, kSw128);
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              mma_bf16_ss(tmem + kColDP, od + (uint64_t)((k * 32) >> 4), vd + (uint64_t)((k * 32) >> 4), id_s,
+              mma_bf16_ss(tmem + sb * kSDCols + 64, od + (uint64_t)((k * 32) >> 4), vd + (uint64_t)((k * 32) >> 4), id_s,
                           (s | k) != 0);
           }
           if (!args.vsrc_k) mma_commit(&B.v_empty[vs]);
-          mma_commit(&B.sd_full);
+          mma_commit(&B.sd_full[sb]);
           ++kuse;
           ++vuse;
           ++chunk;
@@ -500,8 +504,9 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         if (!(flags & kEmpty)) {
           const int nqi = jd[js].nqi, nvi = jd[js].nvi;
           // P and dS' tiles: formed in this kernel, or (two-pass form) tile buffer chunk % 2
-          const uint8_t* tp = two ? stile + (chunk & 1) * kTileBytes : spp;
-          const uint8_t* tds = two ? tp + kQSlab : sds;
+          const int pb = chunk % args.npd;
+          const uint8_t* tp = two ? stile + (chunk & 1) * kTileBytes : spp + pb * 32768;
+          const uint8_t* tds = two ? tp + kQSlab : sds + pb * 32768;
           const uint64_t dsd = smem_desc(smem_u32(tds), 16, 1024, kSw128);    // dS' [heads][keys], K-major
           const uint64_t dst_ = smem_desc(smem_u32(tds), 0, 1024, kSw128);    // dS'^T as MN-major B
           const uint64_t pt = smem_desc(smem_u32(tp), 0, 1024, kSw128);       // P^T as MN-major B
@@ -515,7 +520,7 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
           if (two) {
             if (!(ok = wt(&B.t_full[chunk & 1], (chunk >> 1) & 1, st, 24))) break;
             if (!(ok = wt(&B.k_full[kuse % KS], (kuse / KS) & 1, st, 25))) break;
-          } else if (!(ok = wt(&B.pd_full, chunk & 1, st, 14))) {
+          } else if (!(ok = wt(&B.pd_full[pb], (chunk / args.npd) & 1, st, 14))) {
             break;
           }
           const int kb = args.nkvb == 2 ? (chunk & 1) : 0;
@@ -545,7 +550,7 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
                           args.merged || k != 0);
           }
           mma_commit(&B.k_empty[ks]);
-          mma_commit(two ? &B.t_empty[chunk & 1] : &B.pd_empty);
+          mma_commit(two ? &B.t_empty[chunk & 1] : &B.pd_empty[pb]);
           mma_commit(&B.kv_full[kb]);
           if (flags & kLast) {
             mma_commit(&B.dq_full);
@@ -624,15 +629,16 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         if (!(lse2 > -INFINITY)) lse2 = INFINITY;          // a row with no mass: P = 0
       }
       // the P / dS' tiles are free once the previous chunk's MMAs read them
-      if (!(ok = wtw(&B.pd_empty, (chunk & 1) ^ 1, st, 17))) break;
-      if (!(ok = wtw(&B.sd_full, chunk & 1, st, 18))) break;
+      const int pb = chunk % args.npd, sb = chunk % args.nsd;
+      if (!(ok = wtw(&B.pd_empty[pb], ((chunk / args.npd) & 1) ^ 1, st, 17))) break;
+      if (!(ok = wtw(&B.sd_full[sb], (chunk / args.nsd) & 1, st, 18))) break;
       tc_fence_after();
-      const uint32_t prow = smem_u32(spp) + m * 128, drow = smem_u32(sds) + m * 128;
+      const uint32_t prow = smem_u32(spp + pb * 32768) + m * 128, drow = smem_u32(sds + pb * 32768) + m * 128;
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         float sv[32], dv[32];
-        tmem_ld32(tl + kColS + hh * 32, sv);
-        tmem_ld32(tl + kColDP + hh * 32, dv);
+        tmem_ld32(tl + sb * kSDCols + hh * 32, sv);
+        tmem_ld32(tl + sb * kSDCols + 64 + hh * 32, dv);
         tmem_ld_wait();
         const uint32_t msk = hv ? (hh ? mhi : mlo) : 0u;
 #pragma unroll
@@ -652,9 +658,9 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         }
       }
       tc_fence_before();
-      warp_arrive(&B.sd_empty);
+      warp_arrive(&B.sd_empty[sb]);
       fence_proxy_async_smem();
-      warp_arrive(&B.pd_full);
+      warp_arrive(&B.pd_full[pb]);
       ++chunk;
       if (flags & kLast) {
         if (!(ok = wtw(&B.dq_full, item_i & 1, st, 19))) break;
@@ -736,11 +742,18 @@ static bool plan(const SfaParams& p, Plan* out, const char** why, bool two = fal
   a.merged = p.dk == p.dv ? 1 : 0;
   a.ntk = (a.nq * 64 + 127) / 128;
   a.ntv = (a.nv * 64 + 127) / 128;
-  // TMEM: S, dP (one-pass form), dQ, dK^T tiles, dV^T tiles
-  a.col_dq = two ? 0u : kColDQ;
-  a.col_dk = a.col_dq + (uint32_t)(a.nq * 64);
-  a.col_dv = a.col_dk + 64u * a.ntk;
-  const uint32_t cols = a.col_dv + (a.merged ? 0u : 64u * a.ntv);
+  // TMEM: S / dP buffers (one-pass form; two when they fit beside the rest, so
+  // the next chunk's S and dP are formed while the P / dS' warps read this
+  // one's), dQ, dK^T tiles, dV^T tiles
+  auto layout = [&](int nsd) {
+    a.nsd = nsd;
+    a.col_dq = two ? 0u : (uint32_t)nsd * kSDCols;
+    a.col_dk = a.col_dq + (uint32_t)(a.nq * 64);
+    a.col_dv = a.col_dk + 64u * a.ntk;
+    return a.col_dv + (a.merged ? 0u : 64u * a.ntv);
+  };
+  uint32_t cols = layout(two ? 1 : 2);
+  if (cols > kTmemCols && !two) cols = layout(1);
   if (cols > kTmemCols) { *why = "token-level backward: dQ plus the dK/dV tiles exceed tensor memory"; return false; }
   // a second dK^T/dV^T buffer lets the next chunk's MMAs run while the drain reads this one
   a.kv_stride = cols - a.col_dk;
@@ -754,9 +767,13 @@ static bool plan(const SfaParams& p, Plan* out, const char** why, bool two = fal
   const size_t kst = (size_t)a.nq * kSlab, vst = a.vsrc_k ? 0 : (size_t)a.nv * kSlab;
   // regions after Q / dO must cover the 128-dim tiles the dK^T / dV^T MMAs read
   // (a 64-dim Q or dO reads its neighbour's slab for the ignored rows)
-  const size_t tiles = two ? 2 * (size_t)kTileBytes : 2 * 16384;
-  const size_t fixed = (size_t)(a.nq + a.nv) * kQSlab + tiles + desc + bars;
   int ks = 2, vs = a.vsrc_k ? 0 : 2;
+  // one P / dS' pair: a second one (the P / dS' warps a chunk ahead of the
+  // gradient MMAs) measured slower at tok128, 8.76 against 8.38 ms for the
+  // backward, while a second S / dP buffer in TMEM measured even (8.34)
+  a.npd = 1;
+  const size_t tiles = two ? 2 * (size_t)kTileBytes : (size_t)a.npd * 32768;
+  const size_t fixed = (size_t)(a.nq + a.nv) * kQSlab + tiles + desc + bars;
   if (fixed + ks * kst + vs * vst > budget) { *why = "head dims too large for shared memory"; return false; }
   while (ks < 4 || (!a.vsrc_k && vs < 4)) {
     const bool grow_k = a.vsrc_k || ks <= vs;
