@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define SFA_ABI_VERSION 2
+#define SFA_ABI_VERSION 3
 
 enum {
   SFA_OK = 0,
@@ -71,6 +71,12 @@ enum {
  * before its PV matmul: stored as fp16, read back as bf16 (SFA.py:446, 456); the
  * row sums keep the unrounded values, as there.  Default: one rounding to bf16. */
 #define SFA_COMPAT_REFERENCE_P 1
+
+/* kv storage (SfaParams.kv_dtype). */
+enum {
+  SFA_KV_BF16 = 0,
+  SFA_KV_FP8_E4M3 = 1   /* e4m3 bytes + one fp32 scale per kv row (forward only) */
+};
 
 /* Kernel family (SfaParams.kernel); AUTO picks the tensor-core path when it
  * supports the shape and the general CUDA-core path otherwise. */
@@ -136,6 +142,16 @@ typedef struct SfaParams {
   int32_t page_size;
   const int32_t* block_table;
   int64_t bt_stride;
+  /* fp8 kv (forward only; no reference counterpart): with kv_dtype =
+   * SFA_KV_FP8_E4M3, k points to e4m3 bytes (strides in bytes; v must be k or
+   * its leading d_v dims, the MLA latent) and kv_scale to one fp32 scale per
+   * kv row, indexed b*ks_sb + t*ks_st + h*ks_sh (t the kv row, through the
+   * block table when paged): key = e4m3 value * scale, rounded to bf16 for
+   * the bf16 MMAs (exact when the scales are powers of two). */
+  int32_t kv_dtype;   /* SFA_KV_* */
+  int32_t reserved;
+  const float* kv_scale;
+  int64_t ks_sb, ks_st, ks_sh;
 } SfaParams;
 
 /* Library / ABI identification. */

@@ -23,12 +23,13 @@ SFA_DKV_AUTO, SFA_DKV_INVERTED, SFA_DKV_ATOMIC = 0, 1, 2
 SFA_KERNEL_AUTO, SFA_KERNEL_TCGEN05, SFA_KERNEL_GENERAL = 0, 1, 2
 SFA_DQ_AUTO, SFA_DQ_SEPARATE, SFA_DQ_FUSED = 0, 1, 2
 SFA_COMPAT_REFERENCE_P = 1
+SFA_KV_BF16, SFA_KV_FP8_E4M3 = 0, 1
 SFA_SELFTEST_STATUS = (15 << 16) | 1   # status code of sfa_selftest_wait_timeout
 
 _c_void_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 class SfaParams(ctypes.Structure):
@@ -46,6 +47,8 @@ class SfaParams(ctypes.Structure):
         ("topk", _i32), ("scale", ctypes.c_float), ("causal", _i32), ("dkv_mode", _i32),
         ("kernel", _i32), ("dq_mode", _i32), ("compat", _i32), ("page_size", _i32),
         ("block_table", _c_void_p), ("bt_stride", _i64),
+        ("kv_dtype", _i32), ("reserved", _i32), ("kv_scale", _c_void_p),
+        ("ks_sb", _i64), ("ks_st", _i64), ("ks_sh", _i64),
     ]
 
 

@@ -133,6 +133,14 @@ static int validate(const SfaParams* p, bool bwd) {
     return fail(SFA_ERR_INVALID_ARGUMENT, "unknown kernel family");
   if (bwd && p->dq_mode != SFA_DQ_AUTO && p->dq_mode != SFA_DQ_SEPARATE && p->dq_mode != SFA_DQ_FUSED)
     return fail(SFA_ERR_INVALID_ARGUMENT, "unknown dq_mode");
+  if (p->kv_dtype != SFA_KV_BF16 && p->kv_dtype != SFA_KV_FP8_E4M3)
+    return fail(SFA_ERR_INVALID_ARGUMENT, "unknown kv_dtype");
+  if (p->kv_dtype == SFA_KV_FP8_E4M3) {
+    if (bwd) return fail(SFA_ERR_UNSUPPORTED, "fp8 kv is a forward (inference) format: no backward");
+    if (!p->kv_scale) return fail(SFA_ERR_INVALID_ARGUMENT, "fp8 kv needs kv_scale");
+    if (p->v != p->k || p->v_sb != p->k_sb || p->v_st != p->k_st || p->v_sh != p->k_sh || p->d_v > p->d_qk)
+      return fail(SFA_ERR_INVALID_ARGUMENT, "fp8 kv: v must be k or its leading d_v dims (one latent kv tensor)");
+  }
   if (p->block_table) {
     if (bwd) return fail(SFA_ERR_UNSUPPORTED, "a paged kv cache is a forward (decode) format: no backward");
     if (!p->cu_seqlens_q) return fail(SFA_ERR_INVALID_ARGUMENT, "a paged kv cache needs the varlen layout");
@@ -269,7 +277,7 @@ extern "C" {
 int sfa_abi_version(void) { return SFA_ABI_VERSION; }
 
 const char* sfa_build_info(void) {
-  return "sfa_b200 sm_100a (tcgen05/TMA/TMEM + CUDA-core general family), ABI " "2";
+  return "sfa_b200 sm_100a (tcgen05/TMA/TMEM + CUDA-core general family), ABI " "3";
 }
 
 const char* sfa_last_error_string(void) { return g_err.c_str(); }

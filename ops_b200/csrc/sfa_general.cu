@@ -15,10 +15,18 @@
 #include "sfa_common.cuh"
 #include "sfa_internal.h"
 
+#include <cuda_fp8.h>
+
 namespace sfa {
 
 constexpr int kGenThreads = 128;
 constexpr int kKC = 16;
+
+// one e4m3 byte as float (through the CUDA fp8 conversion)
+static __device__ __forceinline__ float fp8_e4m3_to_float(uint8_t x) {
+  const __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)x, __NV_E4M3);
+  return __half2float(__half(h));
+}
 
 static __device__ __forceinline__ const __nv_bfloat16* bfp(const void* p) {
   return reinterpret_cast<const __nv_bfloat16*>(p);
@@ -73,13 +81,27 @@ __global__ void __launch_bounds__(kGenThreads) fwd_general_kernel(SfaParams p, i
     __syncthreads();
     int any = __syncthreads_or(tid < kKC && keyid[tid] >= 0);
     if (!any) continue;
-    for (int i = tid; i < kKC * Dq; i += kGenThreads) {
-      int kk = i / Dq, d = i - kk * Dq, key = keyid[kk];
-      ks[i] = key >= 0 ? bf2f(kb[(int64_t)key * p.k_st + d]) : 0.f;
-    }
-    for (int i = tid; i < kKC * Dv; i += kGenThreads) {
-      int kk = i / Dv, d = i - kk * Dv, key = keyid[kk];
-      vs[i] = key >= 0 ? bf2f(vb[(int64_t)key * p.v_st + d]) : 0.f;
+    if (p.kv_dtype == SFA_KV_FP8_E4M3) {
+      // e4m3 rows times their row scale (v is k's leading dims)
+      const uint8_t* k8 = static_cast<const uint8_t*>(p.k) + r.b * p.k_sb + (int64_t)hk * p.k_sh;
+      const float* sc = p.kv_scale + r.b * p.ks_sb + (int64_t)hk * p.ks_sh;
+      for (int i = tid; i < kKC * Dq; i += kGenThreads) {
+        int kk = i / Dq, d = i - kk * Dq, key = keyid[kk];
+        ks[i] = key >= 0 ? fp8_e4m3_to_float(k8[(int64_t)key * p.k_st + d]) * __ldg(sc + (int64_t)key * p.ks_st) : 0.f;
+      }
+      for (int i = tid; i < kKC * Dv; i += kGenThreads) {
+        int kk = i / Dv, d = i - kk * Dv, key = keyid[kk];
+        vs[i] = key >= 0 ? fp8_e4m3_to_float(k8[(int64_t)key * p.k_st + d]) * __ldg(sc + (int64_t)key * p.ks_st) : 0.f;
+      }
+    } else {
+      for (int i = tid; i < kKC * Dq; i += kGenThreads) {
+        int kk = i / Dq, d = i - kk * Dq, key = keyid[kk];
+        ks[i] = key >= 0 ? bf2f(kb[(int64_t)key * p.k_st + d]) : 0.f;
+      }
+      for (int i = tid; i < kKC * Dv; i += kGenThreads) {
+        int kk = i / Dv, d = i - kk * Dv, key = keyid[kk];
+        vs[i] = key >= 0 ? bf2f(vb[(int64_t)key * p.v_st + d]) : 0.f;
+      }
     }
     __syncthreads();
     for (int i = tid; i < nh * kKC; i += kGenThreads) {

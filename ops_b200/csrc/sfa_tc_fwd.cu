@@ -788,6 +788,7 @@ bool tc_fwd_supported(const SfaParams& p, const char** why) {
   const int G = p.h_q / p.h_kv;
   if (device_cc() != 100) { *why = "needs an sm_100 device"; return false; }
   if (p.block_size != 64) { *why = "block_size must be 64"; return false; }
+  if (p.kv_dtype != SFA_KV_BF16) { *why = "fp8 kv: the token-level and CUDA-core kernels read it"; return false; }
   if (p.topk > fwd::kMaxTopk) { *why = "topk must be <= 64"; return false; }
   if (p.d_qk != p.d_v || (p.d_qk != 64 && p.d_qk != 128)) { *why = "head dim must be 64 or 128 (D_qk == D_v)"; return false; }
   if (G > fwd::kNH) { *why = "query heads per kv head must be <= 16"; return false; }

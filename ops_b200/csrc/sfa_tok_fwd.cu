@@ -46,6 +46,8 @@
 #include "sfa_tc_host.h"
 #include "sfa_tok_common.cuh"
 
+#include <cuda_fp8.h>
+
 namespace sfa {
 using namespace tc;
 using namespace tok;
@@ -70,6 +72,7 @@ struct Desc {
   int flags;
   int row, hk, hg, vp, b, tq;
   int64_t kbase, vbase;              // K / V gather rows of key 0 of this item's sequence / kv head
+  int64_t sbase;                     // fp8 kv: scale index of key 0
   int keys[kKeys];                   // key ids (an invalid slot repeats a valid key of the chunk)
 };
 
@@ -80,6 +83,7 @@ struct Args {
   int kst, vst;                      // ring stages (2 slabs each)
   uint32_t off_k, off_v, off_p, off_desc, off_bar;   // smem offsets (Q at 0)
   int64_t k_rs, v_rs;                // element strides of one gather row (k / v)
+  int fp8;                           // kv stored as e4m3 + row scales: slabs converted to bf16 here
   int32_t* status;
 };
 
@@ -105,6 +109,39 @@ __device__ __forceinline__ bool wtw(uint64_t* bar, uint32_t parity, int32_t* sta
 }
 
 
+
+// Two e4m3 kv rows (64 dims each, at byte offsets o0 / o1 of kv) into rows
+// `lane` and `lane + 32` of a bf16 64 x 64 slab, times their row scales, with
+// the 128-byte swizzle of the TMA copies (16-byte group g of row j at
+// group g ^ (j & 7)).  Exact when the scales are powers of two.
+__device__ __forceinline__ void fp8_rows_to_slab(uint8_t* slab, const uint8_t* kv, int64_t o0, int64_t o1, float s0,
+                                                 float s1, int lane) {
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const uint4* src = reinterpret_cast<const uint4*>(kv + (r ? o1 : o0));
+    const float sc = r ? s1 : s0;
+    const int j = lane + 32 * r;
+    uint8_t* row = slab + j * 128;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 w = __ldg(src + q);                      // 16 e4m3 values: dims 16q .. 16q + 15
+      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+      uint32_t o[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(words[i] & 0xffffu), __NV_E4M3);
+        const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(words[i] >> 16), __NV_E4M3);
+        const float2 a = __half22float2(__half2(lo)), b = __half22float2(__half2(hi));
+        o[2 * i] = pack_bf16x2(a.x * sc, a.y * sc);
+        o[2 * i + 1] = pack_bf16x2(b.x * sc, b.y * sc);
+      }
+      // two 16-byte groups (8 dims each) of the bf16 row
+      const int g0 = 2 * q, g1 = 2 * q + 1;
+      *reinterpret_cast<uint4*>(row + ((g0 ^ (j & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4*>(row + ((g1 ^ (j & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+  }
+}
 
 // Item index -> (row, kv head, head tile, V part); the parts of one (row, kv
 // head, head tile) are consecutive so the CTAs computing them run together
@@ -198,6 +235,7 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       const uint32_t chunks = __ballot_sync(0xffffffffu, (my_lo | my_hi) != 0u);
       const int64_t kbase = ((int64_t)r.b * p.k_sb + r.kv0 * p.k_st + (int64_t)hk * p.k_sh) / args.k_rs;
       const int64_t vbase = ((int64_t)r.b * p.v_sb + r.kv0 * p.v_st + (int64_t)hk * p.v_sh) / args.v_rs;
+      const int64_t sbase = (int64_t)r.b * p.ks_sb + r.kv0 * p.ks_st + (int64_t)hk * p.ks_sh;
       if (chunks == 0u) {
         // nothing selected: one descriptor tells the softmax warps to write zeros
         if (lane == 0) {
@@ -255,6 +293,7 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
           d.row = row; d.hk = hk; d.hg = hg; d.vp = vp; d.b = r.b; d.tq = (int)r.tq;
           d.kbase = kbase;
           d.vbase = vbase;
+          d.sbase = sbase;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&B.jd_full[js]);
@@ -295,8 +334,14 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         continue;
       }
       const int e0 = d.keys[lane], e1 = d.keys[lane + 32];
-      const int64_t kbase = d.kbase, vbase = d.vbase;
+      const int64_t kbase = d.kbase, vbase = d.vbase, sbase = d.sbase;
       const int vp = d.vp;
+      // fp8 kv: this lane's two keys' row scales (keys lane and lane + 32 of the chunk)
+      float sc0 = 0.f, sc1 = 0.f;
+      if (args.fp8) {
+        sc0 = __ldg(p.kv_scale + sbase + (int64_t)e0 * p.ks_st);
+        sc1 = __ldg(p.kv_scale + sbase + (int64_t)e1 * p.ks_st);
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&B.jd_empty[js]);
       int kq[4];
@@ -322,12 +367,23 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
             if (lane == 0) {
               ok = wt(isk ? &B.k_empty[s_] : &B.v_empty[s_], ((use / nst) & 1) ^ 1, st, 7);
               if (ok) {
-                if (real) mbar_arrive_expect_tx(full, (uint32_t)kSlab);
-                else mbar_arrive(full);
+                if (!real) mbar_arrive(full);
+                else if (!args.fp8) mbar_arrive_expect_tx(full, (uint32_t)kSlab);
               }
             }
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-            if (ok && real && lane < 16) {
+            if (ok && real && args.fp8) {
+              // e4m3 rows -> bf16 slab: lane l converts keys l and l + 32 (64 dims each), stores
+              // them 128B-swizzled as TMA would, and the warp arrives once its stores are visible
+              // to the tensor cores
+              uint8_t* dst = (isk ? sk : sv) + s_ * 2 * kSlab + h * kSlab;
+              const int col = (isk ? 0 : d0) + (2 * t + h) * 64;
+              fp8_rows_to_slab(dst, static_cast<const uint8_t*>(p.k), (base + (int64_t)e0 * step) * args.k_rs + col,
+                               (base + (int64_t)e1 * step) * args.k_rs + col, sc0, sc1, lane);
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(full);
+            } else if (ok && real && lane < 16) {
               uint8_t* dst = (isk ? sk : sv) + s_ * 2 * kSlab + h * kSlab + quad * 512;
               gather4(dst, isk ? &tmk : &tmv, full, (isk ? 0 : d0) + (2 * t + h) * 64, (int)(base + kq[0] * step),
                       (int)(base + kq[1] * step), (int)(base + kq[2] * step), (int)(base + kq[3] * step));
@@ -590,6 +646,7 @@ static bool plan(const SfaParams& p, Plan* out, const char** why) {
   a.k_rs = gather_rows(p, p.k_sb, p.k_st, p.k_sh, p.d_qk, &krows);
   a.v_rs = gather_rows(p, p.v_sb, p.v_st, p.v_sh, p.d_v, &vrows);
   if (!a.k_rs || !a.v_rs) { *why = "k/v batch, token and head strides must fold into evenly spaced rows"; return false; }
+  a.fp8 = p.kv_dtype == SFA_KV_FP8_E4M3 ? 1 : 0;
   if (krows > INT32_MAX || vrows > INT32_MAX) { *why = "too many kv rows for 32-bit gather coordinates"; return false; }
   // shared memory: Q (nq slabs of 16 KB), P (16 KB), K / V rings of 2-slab (16 KB) stages
   const size_t budget = 227 * 1024 - 1024;
@@ -625,8 +682,12 @@ bool tok_fwd_supported(const SfaParams& p, const char** why) {
     return false;
   }
   if (!(p.scale > 0.f)) { *why = "needs a positive softmax scale"; return false; }
-  if (!tma_compatible(p.q, p.q_sb, p.q_st, p.q_sh) || !tma_compatible(p.k, p.k_sb, p.k_st, p.k_sh) ||
-      !tma_compatible(p.v, p.v_sb, p.v_st, p.v_sh)) {
+  const bool fp8 = p.kv_dtype == SFA_KV_FP8_E4M3;
+  // fp8 kv rows are read 16 bytes at a time: byte strides multiples of 16
+  const bool kv_ok = fp8 ? ((reinterpret_cast<uintptr_t>(p.k) & 15) == 0 && p.k_sb % 16 == 0 && p.k_st % 16 == 0 &&
+                            p.k_sh % 16 == 0)
+                         : (tma_compatible(p.k, p.k_sb, p.k_st, p.k_sh) && tma_compatible(p.v, p.v_sb, p.v_st, p.v_sh));
+  if (!tma_compatible(p.q, p.q_sb, p.q_st, p.q_sh) || !kv_ok) {
     *why = "q/k/v need 16-byte aligned base and strides";
     return false;
   }
@@ -651,11 +712,17 @@ cudaError_t launch_fwd_tok(const SfaParams& p, cudaStream_t stream) {
   cudaError_t e = make_tmap_bf16_4d(&tq, p.q, {(uint64_t)p.d_qk, (uint64_t)p.h_q, (uint64_t)qrows, (uint64_t)nb},
                                     {p.q_sh, p.q_st, p.q_sb}, {64u, (uint32_t)a.HG, 1u, 1u});
   if (e != cudaSuccess) return e;
-  int64_t krows = 0, vrows = 0;
-  tok::gather_rows(p, p.k_sb, p.k_st, p.k_sh, p.d_qk, &krows);
-  tok::gather_rows(p, p.v_sb, p.v_st, p.v_sh, p.d_v, &vrows);
-  if ((e = tok::make_tmap_rows(&tk, p.k, (uint64_t)p.d_qk, (uint64_t)krows, a.k_rs)) != cudaSuccess) return e;
-  if ((e = tok::make_tmap_rows(&tv, p.v, (uint64_t)p.d_v, (uint64_t)vrows, a.v_rs)) != cudaSuccess) return e;
+  if (a.fp8) {
+    // fp8 rows are converted by the gather warps, not copied by TMA: the maps go unused
+    tk = tq;
+    tv = tq;
+  } else {
+    int64_t krows = 0, vrows = 0;
+    tok::gather_rows(p, p.k_sb, p.k_st, p.k_sh, p.d_qk, &krows);
+    tok::gather_rows(p, p.v_sb, p.v_st, p.v_sh, p.d_v, &vrows);
+    if ((e = tok::make_tmap_rows(&tk, p.k, (uint64_t)p.d_qk, (uint64_t)krows, a.k_rs)) != cudaSuccess) return e;
+    if ((e = tok::make_tmap_rows(&tv, p.v, (uint64_t)p.d_v, (uint64_t)vrows, a.v_rs)) != cudaSuccess) return e;
+  }
   a.status = device_status_ptr();
   e = cudaFuncSetAttribute(tokf::sfa_tok_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
   if (e != cudaSuccess) return e;

@@ -311,6 +311,72 @@ def sparse_flash_attention_paged(q: torch.Tensor, k_cache: torch.Tensor, v_cache
     return o, lse
 
 
+def quantize_kv_fp8(kv: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """e4m3 copy of a kv tensor with one power-of-two fp32 scale per row (its
+    last dim): ``kv ~= kv_fp8 * scale[..., None]``.  Power-of-two scales make
+    the kernels' dequantisation (e4m3 value * scale -> bf16) exact, so a
+    forward over ``(kv_fp8, scale)`` equals one over the dequantised bf16 kv."""
+    amax = kv.detach().abs().amax(-1).float()
+    e = torch.ceil(torch.log2(torch.clamp(amax, min=1e-30) / 448.0))
+    scale = torch.where(amax > 0, torch.exp2(e), torch.ones_like(amax))
+    q = (kv.detach().float() / scale[..., None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return q, scale
+
+
+def sparse_flash_attention_fp8kv(q: torch.Tensor, kv_fp8: torch.Tensor, kv_scale: torch.Tensor,
+                                 block_indices: torch.Tensor, d_v: int, block_size: int = 1,
+                                 scale: Optional[float] = None, cu_seqlens: Optional[torch.Tensor] = None,
+                                 attn_sink: Optional[torch.Tensor] = None, causal: bool = True,
+                                 cu_seqlens_k: Optional[torch.Tensor] = None, max_seqlen_q: Optional[int] = None,
+                                 max_seqlen_k: Optional[int] = None, kernel: str = "auto"
+                                 ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Forward (no autograd) over one latent kv tensor stored as e4m3 with a
+    fp32 scale per row — the MLA cache format: keys are ``kv_fp8 * scale``
+    over all ``Dqk`` dims, values their first ``d_v`` dims.  Layouts as
+    ``sparse_flash_attention`` (dense ``kv_fp8 [B, Tk, Hk, Dqk]``,
+    ``kv_scale [B, Tk, Hk]``; varlen drops B).  The kernels gather half the
+    bytes of a bf16 cache and widen the rows to bf16 in shared memory; see
+    ``quantize_kv_fp8``."""
+    if not q.is_cuda or q.dtype != torch.bfloat16:
+        raise ValueError("q must be a bfloat16 CUDA tensor")
+    if kv_fp8.dtype not in (torch.float8_e4m3fn, torch.uint8) or not kv_fp8.is_cuda:
+        raise ValueError("kv_fp8 must be a float8_e4m3fn (or uint8) CUDA tensor")
+    if kv_scale.dtype != torch.float32 or tuple(kv_scale.shape) != tuple(kv_fp8.shape[:-1]):
+        raise ValueError("kv_scale must be fp32 with kv_fp8's shape minus the last dim")
+    if block_indices.numel() == 0:
+        raise ValueError("block indices tensor is empty. Cannot determine effective topk.")
+    varlen = cu_seqlens is not None
+    if varlen:
+        cu_q = cu_seqlens.to(torch.int32).contiguous()
+        cu_k = (cu_seqlens_k if cu_seqlens_k is not None else cu_seqlens).to(torch.int32).contiguous()
+        if max_seqlen_q is None:
+            max_seqlen_q = int((cu_q[1:] - cu_q[:-1]).max().item()) if cu_q.numel() > 1 else 0
+        if max_seqlen_k is None:
+            max_seqlen_k = int((cu_k[1:] - cu_k[:-1]).max().item()) if cu_k.numel() > 1 else 0
+    else:
+        cu_q = cu_k = None
+        max_seqlen_q, max_seqlen_k = q.shape[1], kv_fp8.shape[1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    k8 = _inner_contig(kv_fp8.view(torch.uint8))
+    v8 = k8[..., :d_v]
+    cfg = _Cfg(int(block_size), float(scale), bool(causal), varlen, int(max_seqlen_q), int(max_seqlen_k),
+               _lib.SFA_DKV_AUTO, _KERNEL[kernel], True)
+    sink = None if attn_sink is None else attn_sink.float()
+    qq, idx = _inner_contig(q), _idx32(block_indices)
+    o = qq.new_empty(*qq.shape[:-1], d_v)
+    lse = torch.empty(qq.shape[:-1], dtype=torch.float32, device=q.device)
+    P = build_params(qq, k8, v8, idx, o, lse, cfg, sink, cu_q, cu_k)
+    P.kv_dtype = _lib.SFA_KV_FP8_E4M3
+    P.kv_scale = kv_scale.data_ptr()
+    if varlen:
+        P.ks_sb, P.ks_st, P.ks_sh = 0, kv_scale.stride(0), kv_scale.stride(1)
+    else:
+        P.ks_sb, P.ks_st, P.ks_sh = kv_scale.stride(0), kv_scale.stride(1), kv_scale.stride(2)
+    _lib.check(_lib.load().sfa_fwd(ctypes.byref(P), None, 0, _stream()), "sfa_fwd (fp8 kv)")
+    return o, lse
+
+
 def _has_valid_key(idx: torch.Tensor, cfg: "_Cfg", cu_q, cu_k, hq: int, hk: int) -> torch.Tensor:
     """[.., Hq] bool: the row selected at least one valid key (the kernels'
     rule: block id in range, a key below kv_len and, when causal, at or before

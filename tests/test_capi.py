@@ -27,7 +27,7 @@ def test_library_loads_and_exports_all_declared_symbols():
     for n in names:
         assert hasattr(lib, n), n
         assert n in _lib.EXPORTS, f"{n} has no ctypes signature"
-    assert lib.sfa_abi_version() == _lib.ABI_VERSION == 2
+    assert lib.sfa_abi_version() == _lib.ABI_VERSION == 3
     assert b"sm_100a" in lib.sfa_build_info()
 
 
@@ -141,4 +141,17 @@ def test_indexer_argument_validation_without_gpu():
                            (dict(q_idx=0), _lib.SFA_ERR_INVALID_ARGUMENT, "non-NULL")):
         P = _lib.SfaIndexerParams(**{**base, **bad})
         assert lib.sfa_indexer_topk(ctypes.byref(P), None, 0, None) == code
+        assert msg in lib.sfa_last_error_string().decode()
+
+
+def test_fp8_kv_rules_without_gpu():
+    lib = _lib.load()
+    fake = 0x50000
+    P = _params(kv_dtype=_lib.SFA_KV_FP8_E4M3, kv_scale=fake, block_size=1, topk=8)
+    assert lib.sfa_select_kernel(ctypes.byref(P), 0) >= 0
+    Pb = _params(kv_dtype=_lib.SFA_KV_FP8_E4M3, kv_scale=fake, dout=fake, dq=fake, dk=fake, dv=fake + 0x1000)
+    assert lib.sfa_select_kernel(ctypes.byref(Pb), 1) == _lib.SFA_ERR_UNSUPPORTED
+    for bad, msg in ((dict(kv_scale=None), "kv_scale"), (dict(v=fake + 0x100), "latent"), (dict(kv_dtype=5), "kv_dtype")):
+        P = _params(**{**dict(kv_dtype=_lib.SFA_KV_FP8_E4M3, kv_scale=fake), **bad})
+        assert lib.sfa_select_kernel(ctypes.byref(P), 0) == _lib.SFA_ERR_INVALID_ARGUMENT
         assert msg in lib.sfa_last_error_string().decode()

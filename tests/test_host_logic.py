@@ -203,3 +203,19 @@ def test_indexer_oracle_selection_rule():
     got = IO.indexer_topk(q, k, w, 3, causal=True)
     assert got[0, 0].tolist() == [0, -1, -1] and got[0, 1].tolist() == [0, 1, -1]
     assert (got[0, 4] >= 0).all()
+
+
+def test_fp8_kv_quantisation_is_exact_in_bf16():
+    # power-of-two row scales: e4m3 value * scale is a bf16 value, so the
+    # kernels' widening to bf16 loses nothing beyond the e4m3 rounding itself
+    from ops_b200.sfa import quantize_kv_fp8
+    g = torch.Generator().manual_seed(2)
+    kv = (torch.randn(3, 50, 1, 576, generator=g) * torch.rand(3, 50, 1, 1, generator=g) * 30).bfloat16()
+    kv[0, 0] = 0
+    q8, sc = quantize_kv_fp8(kv)
+    assert q8.dtype == torch.float8_e4m3fn and sc.shape == kv.shape[:-1]
+    assert torch.equal(torch.log2(sc), torch.round(torch.log2(sc)))            # powers of two
+    deq = q8.float() * sc[..., None]
+    assert torch.equal(deq.bfloat16().float(), deq)                             # exact in bf16
+    rel = ((deq - kv.float()).abs() / kv.float().abs().amax(-1, keepdim=True).clamp_min(1e-6)).max()
+    assert float(rel) <= 2 ** -4                                                # e4m3: 3 mantissa bits
