@@ -842,6 +842,45 @@ def measure_indexer(dev, T=32768, H=64, D=128, topk=2048, steps=5, warmup=3):
                          "peak_kind": f"{kind} bf16 burst", "algorithmic": f"2*H*D per causal pair: {flops:.3e} FLOP"}}
 
 
+def measure_fp8kv(dev, steps=5, warmup=3):
+    """Config 4's forward (T = 32768, MLA) over the e4m3 latent cache against
+    the bf16 cache, same indices; CUDA events per call, L2 flushed between."""
+    import torch
+
+    import ops_b200
+    from ops_b200 import workloads as W
+
+    cfg = W.CONFIGS["c4"]
+    d = W.make_inputs(cfg, dev, seed=0, with_do=False)
+    q, k, idx = d["q"], d["k"], d["idx"]
+    kv8, sc = ops_b200.quantize_kv_fp8(k)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        tot = 0.0
+        for _ in range(steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            torch.cuda.synchronize()
+            tot += a.elapsed_time(b) / steps
+        return tot
+
+    bf = timed(lambda: ops_b200.sparse_flash_attention(q, k, k[..., :cfg.Dv], idx, 1))
+    f8 = timed(lambda: ops_b200.sparse_flash_attention_fp8kv(q, kv8, sc, idx, cfg.Dv))
+    pairs = W.count_pairs(idx, 1, cfg.T, cfg.T) * cfg.Hq
+    fl = 2.0 * pairs * (cfg.Dqk + cfg.Dv)
+    return {"workload": "c4 forward (T=32768, Hq=128 on one latent kv head, Dqk 576 / Dv 512, top-2048) over "
+                        "an e4m3 cache with power-of-two row scales vs the bf16 cache",
+            "bf16_ms": bf, "fp8_ms": f8, "bf16_tflops": fl / (bf * 1e-3) / 1e12, "fp8_tflops": fl / (f8 * 1e-3) / 1e12,
+            "kv_cache_bytes": {"bf16": k.numel() * 2, "fp8": kv8.numel() + sc.numel() * 4}}
+
+
 def run_ours(args, cfg):
     import datetime
 
@@ -885,6 +924,9 @@ def run_ours(args, cfg):
     if world == 1 and args.configs != "none":
         # the step before the op: the top-k indexer that produces token-level indices
         line["indexer"] = measure_indexer(torch.device("cuda", local))
+        torch.cuda.empty_cache()
+        # config 4's forward over an e4m3 latent kv cache
+        line["fp8_kv"] = measure_fp8kv(torch.device("cuda", local))
     if extra:
         line["configs"] = {n: compact(s, c) for n, (s, c) in extra.items()}
     print(json.dumps(line), flush=True)
@@ -909,6 +951,8 @@ def main():
                          "dK/dV pass's jobs and batches (ops_b200/shard.py row_cost)")
     ap.add_argument("--indexer", action="store_true",
                     help="measure only the top-k token indexer (config 4's sequence) and print its line")
+    ap.add_argument("--fp8-kv", action="store_true",
+                    help="measure only config 4's forward over an e4m3 latent kv cache against the bf16 cache")
     ap.add_argument("--paged", action="store_true",
                     help="decode configurations (c5): the kv cache as 64-row pages of a shuffled pool, reached "
                          "through a block table (sparse_flash_attention_paged)")
@@ -929,10 +973,11 @@ def main():
         cfg = W.scaled(cfg, T=args.seq)
     if args.batch or args.seq:
         args.configs = "none"
-    if args.indexer:
+    if args.indexer or args.fp8_kv:
         import torch
         torch.cuda.set_device(0)
-        print(json.dumps(measure_indexer(torch.device("cuda", 0))), flush=True)
+        out = measure_indexer(torch.device("cuda", 0)) if args.indexer else measure_fp8kv(torch.device("cuda", 0))
+        print(json.dumps(out), flush=True)
     elif args.impl == "reference":
         run_reference(args, cfg)
     else:
