@@ -216,7 +216,9 @@ __device__ __forceinline__ bool reduce_round(float (&v)[16], float lw, int j, in
   return true;
 }
 
-template <int D>
+// PAGED: the kv cache is a page pool reached through the block table (the
+// unpaged instantiation keeps block ids, not rows, in its registers)
+template <int D, bool PAGED>
 __global__ void __launch_bounds__(kThreads, 1)
 sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUtensorMap tmq,
                   const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv) {
@@ -275,7 +277,7 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int bi = 2 * c + half;
-      const int row = bi < d.nblk ? d.prow[bi] : args.oob_row;
+      const int row = bi >= d.nblk ? args.oob_row : PAGED ? d.prow[bi] : d.kv0 + d.blocks[bi] * 64;
 #pragma unroll
       for (int cd = 0; cd < D / 64; ++cd)
         tma_load_4d(dst + cd * 128 * 128 + half * 64 * 128, map, full, cd * 64, d.hk, row, d.b);
@@ -296,7 +298,10 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
   };
   // TMA row of block slot i of a segment (block ids in registers; a missing
   // block reads rows past the tensor map, i.e. zeros)
-  auto blk_row = [&](const int (&rb)[kSegBlocks], int i, int nb) { return i < nb ? rb[i] : args.oob_row; };
+  // (rb holds block ids, or with a paged cache the blocks' rows)
+  auto blk_row = [&](const int (&rb)[kSegBlocks], int i, int nb, int kv0) {
+    return i >= nb ? args.oob_row : PAGED ? rb[i] : kv0 + rb[i] * 64;
+  };
 
   if (warp == 0) {
     // ============================================================ K producer
@@ -357,11 +362,12 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
         const int v0 = __shfl_sync(0xffffffffu, pl0, gi & 31);
         const int v1 = __shfl_sync(0xffffffffu, pl1, gi & 31);
         const int blk = gi < 32 ? v0 : v1;
-        // the block's first kv row (through the block table for a paged cache)
-        const int prow = lane < nb ? (int)kv_row(p, r, blk * 64) : 0;
+        // a paged cache: the block's first row in the page pool
+        constexpr bool paged = PAGED;
+        const int prow = paged && lane < nb ? (int)kv_row(p, r, blk * 64) : 0;
         if (lane < nb) {
           d.blocks[lane] = blk;
-          d.prow[lane] = prow;
+          if (paged) d.prow[lane] = prow;
         }
         if (lane == 0) {
           d.row = row;
@@ -374,10 +380,10 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
           d.nblk = nb;
           d.flags = (seg == 0 ? kFirst : 0) | (seg == nseg - 1 ? kLast : 0);
         }
-        // the segment's block rows into lane 0's registers
+        // the segment's block ids (rows, when paged) into lane 0's registers
         int rb[kSegBlocks];
 #pragma unroll
-        for (int i = 0; i < kSegBlocks; ++i) rb[i] = __shfl_sync(0xffffffffu, prow, i);
+        for (int i = 0; i < kSegBlocks; ++i) rb[i] = __shfl_sync(0xffffffffu, paged ? prow : blk, i);
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&sm.jd_full[js]);
@@ -388,8 +394,8 @@ sfa_fwd_tc_kernel(const __grid_constant__ Args args, const __grid_constant__ CUt
               const int s = use % KS;
               ok = wt(&sm.k_empty[s], ((use / KS) & 1) ^ 1, st, 1);
               if (ok)
-                load_chunk(&tmk, sm.kst[s], &sm.k_full[s], blk_row(rb, 2 * c, nb), blk_row(rb, 2 * c + 1, nb), hk,
-                           r.b);
+                load_chunk(&tmk, sm.kst[s], &sm.k_full[s], blk_row(rb, 2 * c, nb, (int)r.kv0),
+                           blk_row(rb, 2 * c + 1, nb, (int)r.kv0), hk, r.b);
               ++use;
             }
           }
@@ -774,10 +780,15 @@ cudaError_t launch(const SfaParams& p, cudaStream_t st) {
   if (a.nitems == 0) return cudaSuccess;
   static_assert(sizeof(Smem<D>) + 1024 <= 227 * 1024, "shared memory budget");
   const size_t smem = sizeof(Smem<D>) + 1024;
-  e = cudaFuncSetAttribute(sfa_fwd_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const bool paged = p.block_table != nullptr;
+  e = cudaFuncSetAttribute(paged ? sfa_fwd_tc_kernel<D, true> : sfa_fwd_tc_kernel<D, false>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int grid = a.nitems < device_sm_count() ? a.nitems : device_sm_count();
-  sfa_fwd_tc_kernel<D><<<grid, kThreads, smem, st>>>(a, tq, tk, tv);
+  if (paged)
+    sfa_fwd_tc_kernel<D, true><<<grid, kThreads, smem, st>>>(a, tq, tk, tv);
+  else
+    sfa_fwd_tc_kernel<D, false><<<grid, kThreads, smem, st>>>(a, tq, tk, tv);
   note_launch("fwd_tc", st);
   return cudaGetLastError();
 }
