@@ -137,6 +137,9 @@ __device__ __forceinline__ void decode_item(const Args& a, int item, int& row, i
   row = a.r0 + r / a.p.h_kv;
 }
 
+// TWO: the two-pass form's gradient half (its own instantiation, so the
+// one-pass kernel carries none of its checks)
+template <bool TWO>
 __global__ void __launch_bounds__(kThreads, 1)
 sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CUtensorMap tmq,
                    const __grid_constant__ CUtensorMap tmdo, const __grid_constant__ CUtensorMap tmk,
@@ -152,7 +155,7 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
   uint8_t* spp = sbase + args.off_p;
   uint8_t* sds = sbase + args.off_ds;
   uint8_t* stile = sbase + args.off_tiles;
-  const bool two = args.parts != 0;
+  constexpr bool two = TWO;
   Desc* jd = reinterpret_cast<Desc*>(sbase + args.off_desc);
   Bars& B = *reinterpret_cast<Bars*>(sbase + args.off_bar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -815,10 +818,11 @@ static cudaError_t launch(const Plan& pl, const SfaParams& p, const CUtensorMap&
   gather_rows(p, p.v_sb, p.v_st, p.v_sh, p.d_v, &vrows);
   if ((e = make_tmap_rows(&tk, p.k, (uint64_t)p.d_qk, (uint64_t)krows, a.k_rs)) != cudaSuccess) return e;
   if ((e = make_tmap_rows(&tv, p.v, (uint64_t)p.d_v, (uint64_t)vrows, a.v_rs)) != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(tokb::sfa_tok_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+  auto kern = a.parts ? tokb::sfa_tok_bwd_kernel<true> : tokb::sfa_tok_bwd_kernel<false>;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
   if (e != cudaSuccess) return e;
   const int grid = a.nitems < device_sm_count() ? a.nitems : device_sm_count();
-  tokb::sfa_tok_bwd_kernel<<<grid, tokb::kThreads, pl.smem, stream>>>(a, tq, tdo, tk, tv, tp, tds);
+  kern<<<grid, tokb::kThreads, pl.smem, stream>>>(a, tq, tdo, tk, tv, tp, tds);
   note_launch(a.parts ? "bwd_tok_grad" : "bwd_tok", stream);
   return cudaGetLastError();
 }

@@ -155,6 +155,10 @@ __device__ __forceinline__ void decode_item(const Args& a, int item, int& row, i
   row = r / a.p.h_kv;
 }
 
+// FP8: kv rows are e4m3 + row scales, widened by the gather warps; PAGED: keys
+// reach their rows through the block table.  Each mode is its own
+// instantiation: the runtime checks cost the bf16 kernel ~10 % at tok128.
+template <bool FP8, bool PAGED>
 __global__ void __launch_bounds__(kThreads, 1)
 sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CUtensorMap tmq,
                    const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv) {
@@ -276,7 +280,7 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         const int fk = lo ? f0 : f1;
         if (!((lo >> lane) & 1u)) e0 = fk;
         if (!((hi >> lane) & 1u)) e1 = fk;
-        if (p.block_table) {                   // paged cache: the keys' rows in the page pool
+        if (PAGED) {                           // paged cache: the keys' rows in the page pool
           e0 = (int)kv_row(p, r, e0);
           e1 = (int)kv_row(p, r, e1);
         }
@@ -338,7 +342,7 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       const int vp = d.vp;
       // fp8 kv: this lane's two keys' row scales (keys lane and lane + 32 of the chunk)
       float sc0 = 0.f, sc1 = 0.f;
-      if (args.fp8) {
+      if (FP8) {
         sc0 = __ldg(p.kv_scale + sbase + (int64_t)e0 * p.ks_st);
         sc1 = __ldg(p.kv_scale + sbase + (int64_t)e1 * p.ks_st);
       }
@@ -368,11 +372,11 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
               ok = wt(isk ? &B.k_empty[s_] : &B.v_empty[s_], ((use / nst) & 1) ^ 1, st, 7);
               if (ok) {
                 if (!real) mbar_arrive(full);
-                else if (!args.fp8) mbar_arrive_expect_tx(full, (uint32_t)kSlab);
+                else if (!FP8) mbar_arrive_expect_tx(full, (uint32_t)kSlab);
               }
             }
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-            if (ok && real && args.fp8) {
+            if (FP8 && ok && real) {
               // e4m3 rows -> bf16 slab: lane l converts keys l and l + 32 (64 dims each), stores
               // them 128B-swizzled as TMA would, and the warp arrives once its stores are visible
               // to the tensor cores
@@ -724,10 +728,13 @@ cudaError_t launch_fwd_tok(const SfaParams& p, cudaStream_t stream) {
     if ((e = tok::make_tmap_rows(&tv, p.v, (uint64_t)p.d_v, (uint64_t)vrows, a.v_rs)) != cudaSuccess) return e;
   }
   a.status = device_status_ptr();
-  e = cudaFuncSetAttribute(tokf::sfa_tok_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+  const bool paged = p.block_table != nullptr;
+  auto kern = a.fp8 ? (paged ? tokf::sfa_tok_fwd_kernel<true, true> : tokf::sfa_tok_fwd_kernel<true, false>)
+                    : (paged ? tokf::sfa_tok_fwd_kernel<false, true> : tokf::sfa_tok_fwd_kernel<false, false>);
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
   if (e != cudaSuccess) return e;
   const int grid = a.nitems < device_sm_count() ? a.nitems : device_sm_count();
-  tokf::sfa_tok_fwd_kernel<<<grid, tokf::kThreads, pl.smem, stream>>>(a, tq, tk, tv);
+  kern<<<grid, tokf::kThreads, pl.smem, stream>>>(a, tq, tk, tv);
   note_launch("fwd_tok", stream);
   return cudaGetLastError();
 }
