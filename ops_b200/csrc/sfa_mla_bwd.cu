@@ -10,7 +10,7 @@
 //  1. this file's kernel, per (query row, kv head, 64-head group): the
 //     stacked product
 //         [S ; dP] = [Q ; dO] . K_sel^T     (M = 128: Q rows 0-63, dO rows 64-127;
-//                                           N = 64 keys; K = D_qk, dO zero past D_v)
+//                                           N = 128 keys; K = D_qk, dO zero past D_v)
 //     valid because V is K's leading D_v dims, so one MMA chain over the
 //     gathered K slabs yields S in TMEM lanes 0-63 and dP in lanes 64-127.
 //     The S lanes form P = exp2(S*c - lse2), hand it to the dP lanes through
@@ -26,10 +26,12 @@
 // Warp roles of pass 1 (512 threads, one persistent CTA per SM):
 //   warp 0        descriptor producer: validity masks of the item's 64-slot
 //                 chunks, chunk descriptors, the stacked Q / dO loads (4-D TMA);
-//   warp 1        MMA issuer: [S ; dP] per chunk, one 64-dim slab at a time;
+//   warp 1        MMA issuer: [S ; dP] per 128-key chunk, one 64-dim slab at a time
+//                 (N = 128: a 64-key chunk's N = 64 MMAs run at half rate);
 //   warps 4-5     P (thread = head row, TMEM lanes 0-63);
 //   warps 6-7     dS' (thread = head row, TMEM lanes 64-127);
-//   warps 8-15    gather pool: warp 8+g owns K ring stage g (tile::gather4).
+//   warps 8-15    gather pool: warps 8+2g, 9+2g own K ring stage g, keys 0-63 and
+//                 64-127 of its 128-key slab (tile::gather4).
 // Every wait is bounded (~2 s); on expiry the kernel records (6 << 16) | site in
 // the status word and returns.
 #include "sfa_common.cuh"
@@ -47,21 +49,20 @@ using namespace tok;
 namespace mla {
 
 constexpr int kThreads = 512;
-constexpr int kKeys = 64;
-constexpr int kMaxTopk = 32 * kKeys;
-constexpr int kJD = 4;
-constexpr int kSlab = 64 * 128;        // 64 keys x 64 dims bf16
+constexpr int kKeys = 128;             // keys per chunk: [S ; dP] MMAs at N = 128 (full rate)
+constexpr int kMaxTopk = 16 * kKeys;
+constexpr int kJD = 3;
+constexpr int kSlab = 128 * 128;       // 128 keys x 64 dims bf16
 constexpr int kQSlab = 128 * 128;      // 128 stacked rows x 64 dims bf16
 constexpr int kHalf = 64;              // heads per item (rows 0-63 Q, 64-127 dO)
-constexpr int kMaxStages = 8;
-constexpr int kGatherWarps = 8;        // warps 8-15
-constexpr uint32_t kTmemCols = 128;    // two [S ; dP] buffers of 64 columns
-constexpr int kXBytes = kHalf * kKeys * 4;
+constexpr int kMaxStages = 4;
+constexpr uint32_t kTmemCols = 256;    // two [S ; dP] buffers of 128 columns
+constexpr int kXBytes = kHalf * 64 * 4;  // P hand-over, 64 keys at a time
 
 enum : int { kFirst = 1, kLast = 2, kSentinel = 8 };
 
 struct Desc {
-  uint32_t mlo, mhi;
+  uint32_t m[4];                       // valid keys of the chunk (bit i of m[q]: key 32 q + i)
   int flags;
   int wrow, hk, hh, b, tq, chunk;
   int64_t kbase;
@@ -115,7 +116,7 @@ sfa_mla_sdp_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
   uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const SfaParams& p = args.p;
   uint8_t* sq = sbase;                                     // stacked [Q ; dO] slabs
-  uint8_t* sk = sbase + args.off_k;                        // K ring (one slab per stage)
+  uint8_t* sk = sbase + args.off_k;                        // K ring (one 128-key slab per stage)
   float* xp = reinterpret_cast<float*>(sbase + args.off_x);
   Desc* jd = reinterpret_cast<Desc*>(sbase + args.off_desc);
   Bars& B = *reinterpret_cast<Bars*>(sbase + args.off_bar);
@@ -132,13 +133,14 @@ sfa_mla_sdp_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
     }
     mbar_init(&B.x_full, 2);
     mbar_init(&B.x_empty, 2);
-    // consumers of a descriptor: the MMA issuer, the gather pool, the four P / dS' warps
+    // consumers of a descriptor: the MMA issuer, the gather pool (two warps a stage), the four P / dS' warps
     for (int i = 0; i < kJD; ++i) {
       mbar_init(&B.jd_full[i], 1);
-      mbar_init(&B.jd_empty[i], 1 + kGatherWarps + 4);
+      mbar_init(&B.jd_empty[i], 1 + 2 * KS + 4);
     }
+    // a stage's two halves (keys 0-63, 64-127) arrive separately
     for (int i = 0; i < KS; ++i) {
-      mbar_init(&B.k_full[i], 1);
+      mbar_init(&B.k_full[i], 2);
       mbar_init(&B.k_empty[i], 1);
     }
     fence_barrier_init();
@@ -172,19 +174,21 @@ sfa_mla_sdp_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       const Row r = row_info(p, args.r0 + wrow);
       const int32_t* idx = p.block_indices + r.b * p.i_sb + r.tq * p.i_st + (int64_t)hk * p.i_sh;
       const int nch = (p.topk + kKeys - 1) / kKeys;
-      uint32_t my_lo = 0, my_hi = 0;
+      // lane c keeps the valid-key masks of chunk c
+      uint32_t my_m[4] = {0u, 0u, 0u, 0u};
       for (int c = 0; c < nch; ++c) {
-        const int s0 = c * kKeys + lane, s1 = s0 + 32;
-        const int e0 = s0 < p.topk ? __ldg(idx + s0) : -1;
-        const int e1 = s1 < p.topk ? __ldg(idx + s1) : -1;
-        const bool v0 = e0 >= 0 && e0 < r.kv_len && (!p.causal || e0 <= r.pos);
-        const bool v1 = e1 >= 0 && e1 < r.kv_len && (!p.causal || e1 <= r.pos);
-        const uint32_t lo = __ballot_sync(0xffffffffu, v0), hi = __ballot_sync(0xffffffffu, v1);
-        if (lane == c) { my_lo = lo; my_hi = hi; }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int sl = c * kKeys + 32 * q + lane;
+          const int e = sl < p.topk ? __ldg(idx + sl) : -1;
+          const bool v = e >= 0 && e < r.kv_len && (!p.causal || e <= r.pos);
+          const uint32_t m = __ballot_sync(0xffffffffu, v);
+          if (lane == c) my_m[q] = m;
+        }
       }
       // chunks without a valid key leave their workspace slots unwritten; the
-      // gradient pass skips the same chunks
-      const uint32_t chunks = __ballot_sync(0xffffffffu, (my_lo | my_hi) != 0u);
+      // gradient pass skips the same (64-key) chunks
+      const uint32_t chunks = __ballot_sync(0xffffffffu, (my_m[0] | my_m[1] | my_m[2] | my_m[3]) != 0u);
       if (chunks == 0u) continue;
       const int64_t kbase = ((int64_t)r.b * p.k_sb + r.kv0 * p.k_st + (int64_t)hk * p.k_sh) / args.k_rs;
       if (lane == 0) {
@@ -202,25 +206,35 @@ sfa_mla_sdp_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       const int cfirst = __ffs(chunks) - 1, clast = 31 - __clz(chunks);
       for (uint32_t rem = chunks; rem && ok; rem &= rem - 1u, ++job) {
         const int c = __ffs(rem) - 1;
-        const uint32_t lo = __shfl_sync(0xffffffffu, my_lo, c), hi = __shfl_sync(0xffffffffu, my_hi, c);
-        const int s0 = c * kKeys + lane, s1 = s0 + 32;
-        int e0 = s0 < p.topk ? __ldg(idx + s0) : -1;
-        int e1 = s1 < p.topk ? __ldg(idx + s1) : -1;
-        // invalid slots gather a valid key of the chunk (in bounds); their P is 0
-        const int fl = lo ? __ffs(lo) - 1 : __ffs(hi) - 1;
-        const int f0 = __shfl_sync(0xffffffffu, e0, fl), f1 = __shfl_sync(0xffffffffu, e1, fl);
-        const int fk = lo ? f0 : f1;
-        if (!((lo >> lane) & 1u)) e0 = fk;
-        if (!((hi >> lane) & 1u)) e1 = fk;
+        uint32_t m[4];
+        int e[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          m[q] = __shfl_sync(0xffffffffu, my_m[q], c);
+          const int sl = c * kKeys + 32 * q + lane;
+          e[q] = sl < p.topk ? __ldg(idx + sl) : -1;
+        }
+        // invalid slots gather the chunk's first valid key (in bounds); their P is 0
+        const int fq = m[0] ? 0 : m[1] ? 1 : m[2] ? 2 : 3;
+        const int fl = __ffs(m[fq]) - 1;
+        int fk = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int f = __shfl_sync(0xffffffffu, e[q], fl);
+          if (q == fq) fk = f;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (!((m[q] >> lane) & 1u)) e[q] = fk;
         const int js = job % kJD;
         if (lane == 0) ok = wt(&B.jd_empty[js], ((job / kJD) & 1) ^ 1, st, 2);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (!ok) break;
         Desc& d = jd[js];
-        d.keys[lane] = e0;
-        d.keys[lane + 32] = e1;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) d.keys[32 * q + lane] = e[q];
+        if (lane < 4) d.m[lane] = m[lane];
         if (lane == 0) {
-          d.mlo = lo; d.mhi = hi;
           d.flags = (c == cfirst ? kFirst : 0) | (c == clast ? kLast : 0);
           d.wrow = wrow; d.hk = hk; d.hh = hh; d.b = r.b; d.tq = (int)r.tq; d.chunk = c;
           d.kbase = kbase;
@@ -239,44 +253,48 @@ sfa_mla_sdp_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
   } else if (warp >= 8) {
     // ============================================================ gather pool
     // Slab j of the kernel's sequence (chunk-major, NQ slabs a chunk) goes to
-    // ring stage j % KS; warp 8+g owns stage g and serves every use of it in order.
-    const int g = warp - 8;
-    const int64_t kstep = p.k_st / args.k_rs;
-    int job = 0;
-    int64_t j = 0;
-    bool ok = true;
-    while (ok) {
-      const int js = job % kJD;
-      ok = wtw(&B.jd_full[js], (job / kJD) & 1, st, 4);
-      if (!ok) break;
-      const Desc& d = jd[js];
-      const int flags = d.flags;
-      if (flags & kSentinel) break;
-      const int e0 = d.keys[lane], e1 = d.keys[lane + 32];
-      const int64_t kbase = d.kbase;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&B.jd_empty[js]);
-      int kq[4];
+    // ring stage j % KS; warps 8 + 2g and 9 + 2g own stage g (keys 0-63 and
+    // 64-127 of the slab) and serve every use of it in order.
+    const int g = (warp - 8) >> 1, half = (warp - 8) & 1;
+    if (g < KS) {
+      const int64_t kstep = p.k_st / args.k_rs;
+      int job = 0;
+      int64_t j = 0;
+      bool ok = true;
+      while (ok) {
+        const int js = job % kJD;
+        ok = wtw(&B.jd_full[js], (job / kJD) & 1, st, 4);
+        if (!ok) break;
+        const Desc& d = jd[js];
+        const int flags = d.flags;
+        if (flags & kSentinel) break;
+        const int e0 = d.keys[64 * half + lane], e1 = d.keys[64 * half + 32 + lane];
+        const int64_t kbase = d.kbase;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&B.jd_empty[js]);
+        int kq[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int src = (4 * quad + i) & 31;
-        const int a = __shfl_sync(0xffffffffu, e0, src), bb = __shfl_sync(0xffffffffu, e1, src);
-        kq[i] = quad < 8 ? a : bb;
-      }
-      for (int s = 0; s < NQ && ok; ++s, ++j) {
-        const int stg = (int)(j % KS);
-        if (stg != g) continue;
-        const uint32_t use = (uint32_t)(j / KS);
-        if (lane == 0) {
-          ok = wt(&B.k_empty[stg], (use & 1) ^ 1, st, 5);
-          if (ok) mbar_arrive_expect_tx(&B.k_full[stg], (uint32_t)kSlab);
+        for (int i = 0; i < 4; ++i) {
+          const int src = (4 * quad + i) & 31;
+          const int a = __shfl_sync(0xffffffffu, e0, src), bb = __shfl_sync(0xffffffffu, e1, src);
+          kq[i] = quad < 8 ? a : bb;
         }
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (ok && lane < 16)
-          gather4(sk + stg * kSlab + quad * 512, &tmk, &B.k_full[stg], s * 64, (int)(kbase + kq[0] * kstep),
-                  (int)(kbase + kq[1] * kstep), (int)(kbase + kq[2] * kstep), (int)(kbase + kq[3] * kstep));
+        for (int s = 0; s < NQ && ok; ++s, ++j) {
+          const int stg = (int)(j % KS);
+          if (stg != g) continue;
+          const uint32_t use = (uint32_t)(j / KS);
+          if (lane == 0) {
+            ok = wt(&B.k_empty[stg], (use & 1) ^ 1, st, 5);
+            if (ok) mbar_arrive_expect_tx(&B.k_full[stg], (uint32_t)(kSlab / 2));
+          }
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          if (ok && lane < 16)
+            gather4(sk + stg * kSlab + half * (kSlab / 2) + quad * 512, &tmk, &B.k_full[stg], s * 64,
+                    (int)(kbase + kq[0] * kstep), (int)(kbase + kq[1] * kstep), (int)(kbase + kq[2] * kstep),
+                    (int)(kbase + kq[3] * kstep));
+        }
+        ++job;
       }
-      ++job;
     }
   } else if (warp == 1) {
     // ============================================================ MMA issuer: [S ; dP]
@@ -305,7 +323,7 @@ sfa_mla_sdp_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
           const uint64_t qd = smem_desc(smem_u32(sq + s * kQSlab), 16, 1024, kSw128);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            mma_bf16_ss(tmem + buf * 64, qd + (uint64_t)((k * 32) >> 4), kd + (uint64_t)((k * 32) >> 4), id_s,
+            mma_bf16_ss(tmem + buf * kKeys, qd + (uint64_t)((k * 32) >> 4), kd + (uint64_t)((k * 32) >> 4), id_s,
                         (s | k) != 0);
           mma_commit(&B.k_empty[stg]);
         }
@@ -325,7 +343,7 @@ sfa_mla_sdp_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
     const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
     const float c2 = p.scale * kLog2e;
     float ref = 0.f;                                      // lse2 (P lanes) or delta (dS' lanes)
-    int job = 0, chunk = 0;
+    int job = 0, chunk = 0, xc = 0;
     bool ok = true;
     while (ok) {
       const int js = job % kJD;
@@ -335,7 +353,9 @@ sfa_mla_sdp_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       if (flags & kSentinel) break;
       const bool hv = hm < args.HH;
       const int h = d.hk * args.G + d.hh * kHalf + hm;
-      const uint32_t mlo = d.mlo, mhi = d.mhi;
+      uint32_t mk[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) mk[q] = d.m[q];
       const int64_t wsrow = ((int64_t)d.wrow * p.h_q + h) * args.ld + (int64_t)d.chunk * kKeys;
       const int row = args.r0 + d.wrow;
       if (flags & kFirst) {
@@ -353,55 +373,61 @@ sfa_mla_sdp_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       const int buf = chunk & 1;
       if (!(ok = wtw(&B.sd_full[buf], (chunk >> 1) & 1, st, 11))) break;
       tc_fence_after();
-      float v[64];
-      {
-        float a[32];
-        tmem_ld32(tl + buf * 64, a);
-        tmem_ld_wait();
+      // the chunk's 128 keys in two halves of 64 (one P hand-over each)
+      for (int kh = 0; kh < 2 && ok; ++kh, ++xc) {
+        float v[64];
+        {
+          float a[32];
+          tmem_ld32(tl + buf * kKeys + 64 * kh, a);
+          tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = a[i];
-        tmem_ld32(tl + buf * 64 + 32, a);
-        tmem_ld_wait();
+          for (int i = 0; i < 32; ++i) v[i] = a[i];
+          tmem_ld32(tl + buf * kKeys + 64 * kh + 32, a);
+          tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[32 + i] = a[i];
-      }
-      tc_fence_before();
-      warp_arrive(&B.sd_empty[buf]);
-      // row (head hm) of the exchange buffer, 16-byte groups rotated by the row
-      float* xrow = xp + hm * kKeys;
-      if (is_p) {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const uint32_t m = i < 32 ? mlo : mhi;
-          v[i] = (hv && ((m >> (i & 31)) & 1u)) ? ex2(fmaf(v[i], c2, -ref)) : 0.f;
+          for (int i = 0; i < 32; ++i) v[32 + i] = a[i];
         }
-        // the dS' lanes have read the previous chunk's P
-        if (!(ok = wtw(&B.x_empty, (chunk & 1) ^ 1, st, 12))) break;
-#pragma unroll
-        for (int g4 = 0; g4 < 16; ++g4)
-          *reinterpret_cast<float4*>(xrow + 4 * ((g4 + hm) & 15)) =
-              make_float4(v[4 * g4], v[4 * g4 + 1], v[4 * g4 + 2], v[4 * g4 + 3]);
-        __syncwarp();
-        warp_arrive(&B.x_full);
-      } else {
-        if (!(ok = wtw(&B.x_full, chunk & 1, st, 13))) break;
-#pragma unroll
-        for (int g4 = 0; g4 < 16; ++g4) {
-          const float4 t = *reinterpret_cast<const float4*>(xrow + 4 * ((g4 + hm) & 15));
-          v[4 * g4] = p.scale * t.x * (v[4 * g4] - ref);
-          v[4 * g4 + 1] = p.scale * t.y * (v[4 * g4 + 1] - ref);
-          v[4 * g4 + 2] = p.scale * t.z * (v[4 * g4 + 2] - ref);
-          v[4 * g4 + 3] = p.scale * t.w * (v[4 * g4 + 3] - ref);
+        if (kh == 1) {
+          tc_fence_before();
+          warp_arrive(&B.sd_empty[buf]);
         }
-        __syncwarp();
-        warp_arrive(&B.x_empty);
-      }
-      if (hv) {
-        uint4* dst = reinterpret_cast<uint4*>((is_p ? args.pws : args.dsws) + wsrow);
+        const uint32_t mlo = kh ? mk[2] : mk[0], mhi = kh ? mk[3] : mk[1];
+        // row (head hm) of the exchange buffer, 16-byte groups rotated by the row
+        float* xrow = xp + hm * 64;
+        if (is_p) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          dst[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
-                              pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+          for (int i = 0; i < 64; ++i) {
+            const uint32_t m = i < 32 ? mlo : mhi;
+            v[i] = (hv && ((m >> (i & 31)) & 1u)) ? ex2(fmaf(v[i], c2, -ref)) : 0.f;
+          }
+          // the dS' lanes have read the previous hand-over
+          if (!(ok = wtw(&B.x_empty, (xc & 1) ^ 1, st, 12))) break;
+#pragma unroll
+          for (int g4 = 0; g4 < 16; ++g4)
+            *reinterpret_cast<float4*>(xrow + 4 * ((g4 + hm) & 15)) =
+                make_float4(v[4 * g4], v[4 * g4 + 1], v[4 * g4 + 2], v[4 * g4 + 3]);
+          __syncwarp();
+          warp_arrive(&B.x_full);
+        } else {
+          if (!(ok = wtw(&B.x_full, xc & 1, st, 13))) break;
+#pragma unroll
+          for (int g4 = 0; g4 < 16; ++g4) {
+            const float4 t = *reinterpret_cast<const float4*>(xrow + 4 * ((g4 + hm) & 15));
+            v[4 * g4] = p.scale * t.x * (v[4 * g4] - ref);
+            v[4 * g4 + 1] = p.scale * t.y * (v[4 * g4 + 1] - ref);
+            v[4 * g4 + 2] = p.scale * t.z * (v[4 * g4 + 2] - ref);
+            v[4 * g4 + 3] = p.scale * t.w * (v[4 * g4 + 3] - ref);
+          }
+          __syncwarp();
+          warp_arrive(&B.x_empty);
+        }
+        if (hv) {
+          uint4* dst = reinterpret_cast<uint4*>((is_p ? args.pws : args.dsws) + wsrow + 64 * kh);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
+                                pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+        }
       }
       ++chunk;
     }
@@ -479,7 +505,8 @@ bool mla_bwd_supported(const SfaParams& p, const char** why) {
   return tok_bwd_parts_supported(p, why);
 }
 
-int64_t mla_ws_ld(const SfaParams& p) { return (int64_t)((p.topk + 63) / 64) * 64; }
+// workspace row length: whole 128-key chunks of the first pass
+int64_t mla_ws_ld(const SfaParams& p) { return (int64_t)((p.topk + mla::kKeys - 1) / mla::kKeys) * mla::kKeys; }
 
 // Rows per wave: the P and dS' workspace of one wave stays within 4 GiB
 // (SFA_MLA_WAVE_ROWS overrides, for tests of the wave loop).
