@@ -307,3 +307,30 @@ def test_two_pass_backward_varlen():
     k = torch.randn(int(cu_k[-1]), Hk, Dqk, generator=g).bfloat16()
     idx = torch.randint(-1, 260, (int(cu_q[-1]), Hk, K), generator=g, dtype=torch.int32)
     _check_latent_bwd(q, k, idx, Dv, True, None, cu_q, cu_k, max(q_lens), max(k_lens))
+
+
+def test_two_pass_backward_separate_dk_dv_buffers():
+    # v is k's leading dims but the caller keeps dk and dv apart (C ABI): the
+    # two-pass form that drains dK^T and dV^T into their own accumulators
+    B, T, Hq, Dqk, Dv, K = 1, 180, 64, 320, 256, 96
+    q, k, _, idx = _inputs(B, T, Hq, 1, Dqk, Dv, K, seed=77, edge=True)
+    dev = torch.device("cuda")
+    qd, kd = q.to(dev), k.to(dev)
+    vd = kd[..., :Dv]
+    idd = idx.to(dev)
+    o, lse = ops_b200.sparse_flash_attention(qd, kd, vd, idd, 1, kernel="tcgen05")
+    do = _do(q, k[..., :Dv]).to(dev)
+    dq, dk, dv = torch.empty_like(qd), torch.empty_like(kd), torch.empty(B, T, 1, Dv, dtype=kd.dtype, device=dev)
+    cfg = S._Cfg(1, Dqk ** -0.5, True, False, T, T, 0, _lib.SFA_KERNEL_TCGEN05, False)
+    P = S.build_params(qd, kd, vd, idd, o, lse, cfg, None, None, None, do, dq, dk, dv)
+    lib = _lib.load()
+    n = lib.sfa_bwd_workspace_bytes(ctypes.byref(P))
+    ws = torch.empty(max(n, 1), dtype=torch.uint8, device=dev)
+    _lib.check(lib.sfa_bwd(ctypes.byref(P), ws.data_ptr(), n, torch.cuda.current_stream().cuda_stream), "sfa_bwd")
+    torch.cuda.synchronize()
+    ro, rl = O.sfa_forward(q.float(), k.float(), k[..., :Dv].float(), idx, 1)
+    rdq, rdk, rdv, _ = O.sfa_backward(q.float(), k.float(), k[..., :Dv].float(), idx, o.float().cpu(), rl,
+                                      do.float().cpu(), 1)
+    assert_close("dq", dq.cpu(), rdq)
+    assert_close("dk", dk.cpu(), rdk)
+    assert_close("dv", dv.cpu(), rdv)
