@@ -189,7 +189,11 @@ int sfa_select_kernel(const SfaParams* p, int is_backward);
  * Returns the kernel family or a negative error code. */
 int sfa_bwd_plan(const SfaParams* p, int32_t* dkv_mode, int32_t* dq_mode);
 
-/* Workspace (device bytes) the forward / backward need for these params. */
+/* Workspace (device bytes) the forward / backward need for these params.  The
+ * token-level backward above 256 head dims runs in two passes over bf16 P and
+ * dS' rows (topk slots per query head); its workspace holds them for a wave of
+ * query rows sized to stay within 4 GiB (the environment variable
+ * SFA_MLA_WAVE_ROWS, read at each call, sets the rows per wave instead). */
 size_t sfa_fwd_workspace_bytes(const SfaParams* p);
 size_t sfa_bwd_workspace_bytes(const SfaParams* p);
 
