@@ -332,7 +332,7 @@ def kernel_flops(name, P, cfg, fl, fused_dq):
     # dV in the gradient half
     if name == "bwd_mla_sdp":
         return two_p * (cfg.Dqk + cfg.Dv)
-    if name == "bwd_tok_grad":
+    if name in ("bwd_tok_grad", "bwd_mla_grad"):
         return two_p * (2 * cfg.Dqk + cfg.Dv)
     return 0.0
 
