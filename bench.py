@@ -378,7 +378,7 @@ def measure_config(args, cfg, world, rank, dev, split, steps, warmup, primary):
     dk = torch.empty_like(k)
     # v = kv[..., :Dv] (c4, tok128): one kv tensor, one gradient dk + dv (the
     # library sums them in fp32 when dk and dv alias)
-    dv = dk if v_view and split != "query" else torch.empty_like(v)
+    dv = dk if v_view else torch.empty_like(v)
     scfg = S._Cfg(cfg.bs, cfg.scale, cfg.causal, False, r1 - r0, ke, _lib.SFA_DKV_AUTO, _lib.SFA_KERNEL_AUTO,
                   False, S._DQ[args.dq_mode])
     P = S.build_params(q, k, v, idx, o, lse, scfg, None, None, None, do, dq, dk, dv, None)
@@ -397,8 +397,10 @@ def measure_config(args, cfg, world, rank, dev, split, steps, warmup, primary):
     sptr = stream.cuda_stream
     if split == "query":
         tc = (T + world - 1) // world
-        rs_in = torch.zeros(world * tc, cfg.B, cfg.Hk, cfg.Dqk + cfg.Dv, dtype=torch.float32, device=dev)
-        rs_out = torch.empty(tc, cfg.B, cfg.Hk, cfg.Dqk + cfg.Dv, dtype=torch.float32, device=dev)
+        # fp32 dK | dV per key (one dK + dV of the latent's dims when v is k's view)
+        width = cfg.Dqk if v_view else cfg.Dqk + cfg.Dv
+        rs_in = torch.zeros(world * tc, cfg.B, cfg.Hk, width, dtype=torch.float32, device=dev)
+        rs_out = torch.empty(tc, cfg.B, cfg.Hk, width, dtype=torch.float32, device=dev)
 
     def step():
         _lib.check(lib.sfa_fwd(Pp, None, 0, sptr), "sfa_fwd")
@@ -407,7 +409,8 @@ def measure_config(args, cfg, world, rank, dev, split, steps, warmup, primary):
         _lib.check(lib.sfa_bwd_dkdv(Pp, ws.data_ptr(), nbytes, sptr), "dkdv")
         if split == "query":
             rs_in[:ke, ..., :cfg.Dqk].copy_(dk.transpose(0, 1))
-            rs_in[:ke, ..., cfg.Dqk:].copy_(dv.transpose(0, 1))
+            if not v_view:
+                rs_in[:ke, ..., cfg.Dqk:].copy_(dv.transpose(0, 1))
             dist.reduce_scatter_tensor(rs_out, rs_in)
 
     for _ in range(warmup):

@@ -206,11 +206,17 @@ def local_step(q_rows: torch.Tensor, k_pre: torch.Tensor, v_pre: torch.Tensor, i
     rows with their ``o``, ``lse`` and ``dq``, and this rank's key share
     ``(k0, k1)`` of ``[0, kv_len)`` with the summed ``dk``, ``dv`` (fp32 sums, in
     k's dtype).  ``fwd_bwd(q, k, v, idx, do, block_size, scale, causal)`` is the
-    single-device step (the CUDA op by default)."""
+    single-device step (the CUDA op by default).  When v is a leading-dims view
+    of k (one latent kv tensor), the op returns one gradient ``dk + dv`` in k's
+    shape: it is summed here as ``dk`` and ``dv`` is None."""
     import torch.distributed as dist
     B, _, _, Dqk = q_rows.shape
     Hk, Dv = k_pre.shape[2], v_pre.shape[3]
     dev = q_rows.device
+    # decided from the inputs, so every rank (with rows or without) agrees
+    shared = (v_pre.data_ptr() == k_pre.data_ptr() and v_pre.stride() == k_pre.stride()
+              and v_pre.shape[:-1] == k_pre.shape[:-1])
+    width = Dqk if shared else Dqk + Dv
     if scale is None:
         scale = 1.0 / math.sqrt(Dqk)
     r0, r1 = rows
@@ -223,11 +229,12 @@ def local_step(q_rows: torch.Tensor, k_pre: torch.Tensor, v_pre: torch.Tensor, i
     # fp32 partials on the key axis (keys major), padded to world equal shares;
     # dk and dv travel in one buffer
     tc = (kv_len + world - 1) // world
-    buf = torch.zeros(world * tc, B, Hk, Dqk + Dv, dtype=torch.float32, device=dev)
+    buf = torch.zeros(world * tc, B, Hk, width, dtype=torch.float32, device=dev)
     if ke > 0:
         buf[:ke, ..., :Dqk] = dk.float().transpose(0, 1)
-        buf[:ke, ..., Dqk:] = dv.float().transpose(0, 1)
-    mine = torch.empty(tc, B, Hk, Dqk + Dv, dtype=torch.float32, device=dev)
+        if not shared:
+            buf[:ke, ..., Dqk:] = dv.float().transpose(0, 1)
+    mine = torch.empty(tc, B, Hk, width, dtype=torch.float32, device=dev)
     if world > 1:
         dist.reduce_scatter_tensor(mine, buf, group=group)
     else:
@@ -235,5 +242,5 @@ def local_step(q_rows: torch.Tensor, k_pre: torch.Tensor, v_pre: torch.Tensor, i
     k0, k1 = key_share(kv_len, world, rank)
     n = k1 - k0
     dk_own = mine[:n, ..., :Dqk].transpose(0, 1).to(k_pre.dtype).contiguous()
-    dv_own = mine[:n, ..., Dqk:].transpose(0, 1).to(v_pre.dtype).contiguous()
+    dv_own = None if shared else mine[:n, ..., Dqk:].transpose(0, 1).to(v_pre.dtype).contiguous()
     return dict(rows=(r0, r1), o=o, lse=lse, dq=dq, keys=(k0, k1), dk=dk_own, dv=dv_own)

@@ -141,3 +141,45 @@ def test_fit_cost_rejects_models_that_do_not_fit():
     # three ranks over-determine the fit: a residual is reported
     f = shard.fit_cost([(100, 10, 5), (100, 12, 9), (100, 20, 6)], [1.0, 1.0, 1.0], [1.0, 1.5, 1.6])
     assert f["rank"] == 2 and not f["exact"] and f["residual"] >= 0.0
+
+
+def _oracle_fwd_bwd_latent(q, k, v, idx, do, bs, scale, causal):
+    # the op's contract for v a leading-dims view of k: one gradient dk + dv in k's shape
+    o, lse, dq, dk, dv = _oracle_fwd_bwd(q, k, v, idx, do, bs, scale, causal)
+    dk = dk.clone()
+    dk[..., :v.shape[-1]] += dv
+    return o, lse, dq, dk, None
+
+
+def _latent_case():
+    cfg = W.scaled(W.CONFIGS["c4"], B=1, T=200, Hq=8, Hk=1, Dqk=48, Dv=32, bs=1, S=40)
+    d = W.make_inputs(cfg, "cpu", 6, dtype=torch.float32)
+    return cfg, d
+
+
+def _latent_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    cfg, d = _latent_case()
+    ranges = shard.query_ranges(shard.row_work(d["idx"], cfg.bs, cfg.T), world)
+    k = d["k"]
+    r = shard.shard_step(d["q"], k, k[..., :cfg.Dv], d["idx"], d["do"], rank, world, ranges, block_size=cfg.bs,
+                         fwd_bwd=_oracle_fwd_bwd_latent)
+    out[rank] = {key: (val.clone() if torch.is_tensor(val) else val) for key, val in r.items()}
+    dist.destroy_process_group()
+
+
+def test_query_range_shards_with_one_latent_kv_tensor():
+    # v = k[..., :Dv] (the MLA layout): the ranks reduce one gradient per key
+    world = 2
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_latent_worker, args=(world, _free_port(), out), nprocs=world, join=True)
+    cfg, d = _latent_case()
+    k = d["k"]
+    _, _, _, dk, _ = _oracle_fwd_bwd_latent(d["q"], k, k[..., :cfg.Dv], d["idx"], d["do"], cfg.bs, None, True)
+    for r in range(world):
+        res = out[r]
+        k0, k1 = res["keys"]
+        assert res["dv"] is None
+        assert torch.allclose(res["dk"], dk[:, k0:k1], atol=1e-4, rtol=1e-4)
