@@ -26,6 +26,9 @@ kernels    every kernel of the step, timed with CUDA events recorded between
 roofline   the kernel with the largest share of the step: its algorithmic
            FLOPs per launch / its CUDA-event duration, against the measured
            bf16 peak; traffic from an ncu capture of that kernel.
+smem_port  (block-sparse forward) the forward's shared-memory traffic modelled
+           from its N = G tiles (operand reads, gather and P writes) against
+           the port's 128 B/clk on every SM: what bounds the N = 16 forward.
 e2e        the same metric through the public API (ops_b200.sparse_flash_attention
            + autograd) with the step's inputs copied from pinned host memory and
            its outputs (o, dq, dk, dv) copied back inside the timed region; the
@@ -337,6 +340,23 @@ def kernel_flops(name, P, cfg, fl, fused_dq):
     return 0.0
 
 
+def smem_port(cfg, pairs, ms, clocks):
+    """The query-centric block-sparse forward's shared-memory traffic, modelled
+    from its tiles: per (row, kv head, selected key) the N = G MMAs read the K
+    and V rows as A operands (2·Dqk + 2·Dv bytes) and G·(Dqk + Dv)·2/128 bytes
+    of Q^T / P^T as B, the gathers write the K and V rows (2·(Dqk + Dv)) and the
+    softmax writes 2·G bytes of P.  Against the port's 128 B/clk on every SM."""
+    G = cfg.Hq // cfg.Hk
+    per_key = 4 * (cfg.Dqk + cfg.Dv) + 2 * G * (cfg.Dqk + cfg.Dv) / 128 + 2 * G
+    nbytes = pairs / G * per_key
+    mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    import torch
+    peak = 128 * torch.cuda.get_device_properties(0).multi_processor_count * mhz * 1e6 / 1e12
+    ach = nbytes / (ms * 1e-3) / 1e12
+    return {"kernel": "fwd_tc", "bytes_per_launch": nbytes, "bytes_per_row_key": per_key, "achieved_tbs": ach,
+            "peak_tbs": peak, "frac": ach / peak, "source": "modelled from the kernel's tiles (128 B/clk/SM)"}
+
+
 def measure_config(args, cfg, world, rank, dev, split, steps, warmup, primary):
     import torch
     import torch.distributed as dist
@@ -520,6 +540,7 @@ def measure_config(args, cfg, world, rank, dev, split, steps, warmup, primary):
                      "algorithmic": f"{dom_f:.4g} FLOP per launch"},
         "gather": {"kernel": fwd_name, "bytes_per_launch": gather,
                    "achieved_tbs": gather / (kern_ms[fwd_name] * 1e-3) / 1e12 if fwd_name else None},
+        **({"smem_port": smem_port(cfg, pairs, kern_ms["fwd_tc"], clocks)} if "fwd_tc" in kern_ms else {}),
         "e2e": {"value": flops_all / (e2e_max * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_max},
         "gpu_launches": int(n1 - n0),
