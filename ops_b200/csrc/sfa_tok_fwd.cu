@@ -501,16 +501,24 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       const Desc& d = jd[js];
       const int flags = d.flags;
       if (flags & kSentinel) break;
-      const int hk = d.hk, hg = d.hg, vp = d.vp, b = d.b, tq = d.tq;
       const uint32_t mlo = d.mlo, mhi = d.mhi;
-      const int h = hk * args.G + hg * 128 + m;               // query head of this thread
-      const bool hv = hg * 128 + m < args.G;
-      const int d0 = vp * args.dvp;
-      const int nd = min(p.d_v - d0, args.dvp);
-      __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.o) + (int64_t)b * p.o_sb + (int64_t)tq * p.o_st +
-                            (int64_t)h * p.o_sh + d0;
-      float* lrow = p.lse + (int64_t)b * p.l_sb + (int64_t)tq * p.l_st + (int64_t)h * p.l_sh;
+      const int vp = d.vp;
+      const int nd = min(p.d_v - vp * args.dvp, args.dvp);
+      // this thread's output row, from the descriptor where it is written (so
+      // nothing of it stays live through the chunk)
+      auto out_row = [&](const Desc& dd, int& h, bool& hv, __nv_bfloat16*& orow, float*& lrow) {
+        h = dd.hk * args.G + dd.hg * 128 + m;                 // query head of this thread
+        hv = dd.hg * 128 + m < args.G;
+        orow = reinterpret_cast<__nv_bfloat16*>(p.o) + (int64_t)dd.b * p.o_sb + (int64_t)dd.tq * p.o_st +
+               (int64_t)h * p.o_sh + dd.vp * args.dvp;
+        lrow = p.lse + (int64_t)dd.b * p.l_sb + (int64_t)dd.tq * p.l_st + (int64_t)h * p.l_sh;
+      };
       if (flags & kEmpty) {
+        int h;
+        bool hv;
+        __nv_bfloat16* orow;
+        float* lrow;
+        out_row(d, h, hv, orow, lrow);
         if (hv) {
           for (int i = 0; i < nd; i += 8)
             *reinterpret_cast<uint4*>(orow + i) = make_uint4(0, 0, 0, 0);
@@ -549,13 +557,13 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       if (!(ok = wtw(&B.p_empty, (chunk & 1) ^ 1, st, 18))) break;
       if (__any_sync(0xffffffffu, fac != 1.f)) {
         tc_fence_after();
-        for (int c0 = 0; c0 < nd; c0 += 32) {
-          float o[32];
-          tmem_ld32(tl + c0, o);
+        for (int c0 = 0; c0 < nd; c0 += 16) {
+          float o[16];
+          tmem_ld16(tl + c0, o);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= fac;
-          tmem_st32(tl + c0, o);
+          for (int i = 0; i < 16; ++i) o[i] *= fac;
+          tmem_st16(tl + c0, o);
         }
         tmem_st_wait();
         l *= fac;
@@ -594,6 +602,11 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         // epilogue: O / (l + exp(sink)), lse in natural log
         if (!(ok = wtw(&B.o_full, item_i & 1, st, 19))) break;
         tc_fence_after();
+        int h;
+        bool hv;
+        __nv_bfloat16* orow;
+        float* lrow;
+        out_row(jd[js], h, hv, orow, lrow);
         const float s2 = (p.attn_sink && hv) ? __ldg(p.attn_sink + h) * kLog2e : -INFINITY;
         const float M = fmaxf(mref, s2);
         const float w = ex2(mref - M);
