@@ -584,13 +584,17 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       if (flags & kSentinel) break;
       const int h = d.hk * args.G + d.hg * 128 + m;
       const bool hv = d.hg * 128 + m < args.G;
-      const int row = d.row, b = d.b, tq = d.tq;
       const uint32_t mlo = d.mlo, mhi = d.mhi;
       // dq dims of this item: all, or the part's (two-pass form)
       const int dqn = d.nqi * 64;
-      __nv_bfloat16* dqrow = reinterpret_cast<__nv_bfloat16*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)tq * p.dq_st +
-                             (int64_t)h * p.dq_sh + (two ? d.part * kPartSlabs * 64 : 0);
+      // the dq row, from the descriptor where it is written (nothing of it stays
+      // live through the chunk)
+      auto dq_row = [&](const Desc& dd) {
+        return reinterpret_cast<__nv_bfloat16*>(p.dq) + (int64_t)dd.b * p.dq_sb + (int64_t)dd.tq * p.dq_st +
+               (int64_t)(dd.hk * args.G + dd.hg * 128 + m) * p.dq_sh + (two ? dd.part * kPartSlabs * 64 : 0);
+      };
       if (flags & kEmpty) {
+        __nv_bfloat16* dqrow = dq_row(d);
         if (hv)
           for (int i = 0; i < dqn; i += 8) *reinterpret_cast<uint4*>(dqrow + i) = make_uint4(0, 0, 0, 0);
         warp_arrive(&B.jd_empty[js]);
@@ -605,6 +609,7 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         if (flags & kLast) {
           if (!(ok = wtw(&B.dq_full, item_i & 1, st, 26))) break;
           tc_fence_after();
+          __nv_bfloat16* dqrow = dq_row(d);
           for (int c0 = 0; c0 < dqn; c0 += 32) {
             float o[32];
             tmem_ld32(tl + args.col_dq + c0, o);
@@ -626,9 +631,9 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         continue;
       }
       if (flags & kFirst) {
-        lse2 = hv ? __ldg(p.lse + (int64_t)b * p.l_sb + (int64_t)tq * p.l_st + (int64_t)h * p.l_sh) * kLog2e
+        lse2 = hv ? __ldg(p.lse + (int64_t)d.b * p.l_sb + (int64_t)d.tq * p.l_st + (int64_t)h * p.l_sh) * kLog2e
                   : -INFINITY;
-        dl = hv ? __ldg(args.delta + (int64_t)row * p.h_q + h) : 0.f;
+        dl = hv ? __ldg(args.delta + (int64_t)d.row * p.h_q + h) : 0.f;
         if (!(lse2 > -INFINITY)) lse2 = INFINITY;          // a row with no mass: P = 0
       }
       // the P / dS' tiles are free once the previous chunk's MMAs read them
@@ -668,6 +673,7 @@ sfa_tok_bwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       if (flags & kLast) {
         if (!(ok = wtw(&B.dq_full, item_i & 1, st, 19))) break;
         tc_fence_after();
+        __nv_bfloat16* dqrow = dq_row(d);
         for (int c0 = 0; c0 < dqn; c0 += 32) {
           float o[32];
           tmem_ld32(tl + args.col_dq + c0, o);

@@ -555,23 +555,11 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       }
       // the P buffer (and O) are free once the previous chunk's PV completed
       if (!(ok = wtw(&B.p_empty, (chunk & 1) ^ 1, st, 18))) break;
-      if (__any_sync(0xffffffffu, fac != 1.f)) {
-        tc_fence_after();
-        for (int c0 = 0; c0 < nd; c0 += 16) {
-          float o[16];
-          tmem_ld16(tl + c0, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] *= fac;
-          tmem_st16(tl + c0, o);
-        }
-        tmem_st_wait();
-        l *= fac;
-      }
       mref = mnew;
       const float nm = -mref;
       const uint32_t prow = smem_u32(sp) + m * 128;
       // pass 2: P = exp2(S*c - m) for the valid keys, bf16 into the swizzled P tile
+      float lc = 0.f;
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         float sv[32];
@@ -585,7 +573,7 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             pr[i] = ((msk >> (8 * j + i)) & 1u) ? ex2(fmaf(sv[8 * j + i], c2, nm)) : 0.f;
-            l += pr[i];
+            lc += pr[i];
             if (p.compat & SFA_COMPAT_REFERENCE_P) pr[i] = ref_p(pr[i]);
           }
           const int jj = 4 * hh + j;
@@ -595,6 +583,24 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       }
       tc_fence_before();
       warp_arrive(&B.s_empty[sb]);
+      // O (and the running sum) to the raised maximum, after P: nothing of the
+      // P pass is live here, so the rare rescale costs the common path no
+      // registers; PV of this chunk is issued only after p_full below
+      if (__any_sync(0xffffffffu, fac != 1.f)) {
+        tc_fence_after();
+        for (int c0 = 0; c0 < nd; c0 += 16) {
+          float o[16];
+          tmem_ld16(tl + c0, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] *= fac;
+          tmem_st16(tl + c0, o);
+        }
+        tmem_st_wait();
+        l *= fac;
+        tc_fence_before();
+      }
+      l += lc;
       fence_proxy_async_smem();
       warp_arrive(&B.p_full);
       ++chunk;
