@@ -916,9 +916,10 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)   // 16 keys per step: +2048 B of K_e, +32 B of dS rows
               mma_bf16_ss(tmem + kColDQ, kdq + (uint64_t)(kk * 128), ddq + (uint64_t)(kk * 2), id_dq, kk != 0);
-            mma_commit(&sm.dq_full);
+            mma_commit(&sm.dq_full);   // also: dS read by the dK and dQ MMAs (the P/dS warps wait on it)
+          } else {
+            mma_commit(&sm.ds_empty);   // dS read by the dK MMAs
           }
-          mma_commit(&sm.ds_empty);   // dS read by the dK (and dQ) MMAs
         }
         if (!ok) break;
         if (kDQ && nb > 0) mma_commit(&sm.kv_empty);   // the dQ MMAs read K_e
@@ -1061,7 +1062,10 @@ sfa_bwd_dkdv_tc_kernel(const __grid_constant__ Args args, const __grid_constant_
 #pragma unroll
         for (int i = 0; i < 32; i += 2)
           dk[i / 2] = pack_bf16x2(pv[i] * (dp[i] - dl), pv[i + 1] * (dp[i + 1] - dl));
-        if (!(ok = wtw(&sm.ds_empty, (gb & 1) ^ 1, st, 29))) break;
+        // the previous batch's dS has been read: with the fused dQ its dQ MMAs
+        // were the last readers and their commit (dq_full) says so, which
+        // saves the issuing thread a second commit per batch
+        if (!(ok = wtw(kDQ ? &sm.dq_full : &sm.ds_empty, (gb & 1) ^ 1, st, 29))) break;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const uint32_t off = (uint32_t)(((wg * 4 + c) ^ (lrow & 7)) * 16);
