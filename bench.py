@@ -550,54 +550,89 @@ def measure_config(args, cfg, world, rank, dev, split, steps, warmup, primary):
     return line
 
 
+def e2e_chunks(cfg, split, units):
+    """The e2e pipeline's chunks: (batch, kv head, row0, row1, first, last)
+    per chunk, or [None] for the query split (one chunk: the rank's rows).
+    A configuration with fewer than 8 units (c3: 4, c4: 1) also cuts each
+    unit's query rows into ranges, so the copies of one range overlap the
+    kernels of another; ``first`` / ``last`` mark a unit's first and last
+    range (its k / v go in with the first, its dk / dv come back after the
+    last)."""
+    if split == "query":
+        return [None]
+    b0, b1, h0, h1 = units
+    n_units = (b1 - b0) * (h1 - h0)
+    n_r = -(-8 // n_units) if n_units < 8 and cfg.T >= 8192 else 1
+    return [(b, h, cfg.T * i // n_r, cfg.T * (i + 1) // n_r, i == 0, i == n_r - 1)
+            for b in range(b0, b1) for h in range(h0, h1) for i in range(n_r)]
+
+
 def e2e_pipeline(args, cfg, d, split, units, rows, world, rank, dev, stream, flush, v_view, steps):
     """Public-API step with host-resident inputs/outputs; returns (ms, h2d, d2h).
 
-    The rank's share is cut into chunks of one (batch, kv head) unit each;
-    chunk i's H2D copies run on one stream, its forward + backward on a
-    second, its D2H copies on a third, so the PCIe traffic of neighbouring
-    chunks overlaps the kernels (and H2D overlaps D2H)."""
+    The rank's share is cut into chunks (``e2e_chunks``: one (batch, kv
+    head) unit each, or row ranges of a unit when units are few); chunk i's
+    H2D copies run on one stream, its forward + backward on a second, its D2H
+    copies on a third, so the PCIe traffic of neighbouring chunks overlaps the
+    kernels (and H2D overlaps D2H).  Within a chunk the forward starts once
+    q/k/v/idx are in (dO is still crossing) and o goes back while the backward
+    runs, which shortens the last chunk's tail.  A row range takes keys
+    [0, row1) (causal: every row keeps its position) and its dk / dv partial is
+    added into the unit's fp32 sum, rounded to bf16 after the unit's last
+    range."""
     import torch
 
     import ops_b200
     from ops_b200 import shard
-    b0, b1, h0, h1 = units
     r0, r1, ke = rows
     G = cfg.Hq // cfg.Hk
     q, k, v, idx, do = d["q"], d["k"], d["v"], d["idx"], d["do"]
-    if split == "query":
-        chunks = [None]
-    else:   # one chunk per (batch, kv head) unit: the last chunk's copies are the only ones not hidden
-        chunks = [(b, b + 1, h, h + 1) for b in range(b0, b1) for h in range(h0, h1)]
+    chunks = e2e_chunks(cfg, split, units)
 
     def pin(t):
         return t.contiguous().cpu().pin_memory()
 
-    host, dbuf, outs = [], [], []
+    host, dbuf, outs, unit_of = [], [], [], []
+    unit_dev, unit_acc = {}, {}
     for c in chunks:
         if c is None:   # query split: this rank's rows and visible keys
             hs = dict(q=pin(q[:, r0:r1]), k=pin(k[:, :ke]), idx=pin(idx[:, r0:r1]), do=pin(do[:, r0:r1]))
             if not v_view:
                 hs["v"] = pin(v[:, :ke])
-        else:
-            cb0, cb1, ch0, ch1 = c
-            hs = dict(q=pin(q[cb0:cb1, :, ch0 * G:ch1 * G]), k=pin(k[cb0:cb1, :, ch0:ch1]),
-                      idx=pin(idx[cb0:cb1, :, ch0:ch1]), do=pin(do[cb0:cb1, :, ch0 * G:ch1 * G]))
-            if not v_view:
-                hs["v"] = pin(v[cb0:cb1, :, ch0:ch1])
-        host.append(hs)
-        dbuf.append({n: torch.empty(t.shape, dtype=t.dtype, device=dev) for n, t in hs.items()})
-        o_sh = tuple(hs["q"].shape[:-1]) + (cfg.Dv,)
-        if c is None:
+            db = {n: torch.empty(t.shape, dtype=t.dtype, device=dev) for n, t in hs.items()}
             k0, k1 = shard.key_share(cfg.T, world, rank)
             kv_sh = (cfg.B, k1 - k0, cfg.Hk)
+            o_sh = tuple(hs["q"].shape[:-1]) + (cfg.Dv,)
+            od = dict(o=torch.empty(o_sh, dtype=q.dtype, pin_memory=True),
+                      dq=torch.empty(tuple(hs["q"].shape), dtype=q.dtype, pin_memory=True),
+                      dk=torch.empty(kv_sh + (cfg.Dqk,), dtype=k.dtype, pin_memory=True))
+            if not v_view:
+                od["dv"] = torch.empty(kv_sh + (cfg.Dv,), dtype=v.dtype, pin_memory=True)
+            unit_of.append(None)
         else:
-            kv_sh = tuple(hs["k"].shape[:-1])
-        od = dict(o=torch.empty(o_sh, dtype=q.dtype, pin_memory=True),
-                  dq=torch.empty(tuple(hs["q"].shape), dtype=q.dtype, pin_memory=True),
-                  dk=torch.empty(kv_sh + (cfg.Dqk,), dtype=k.dtype, pin_memory=True))
-        if not v_view:
-            od["dv"] = torch.empty(kv_sh + (cfg.Dv,), dtype=v.dtype, pin_memory=True)
+            b, h, c0, c1, first, last = c
+            hs = dict(q=pin(q[b:b + 1, c0:c1, h * G:(h + 1) * G]), idx=pin(idx[b:b + 1, c0:c1, h:h + 1]),
+                      do=pin(do[b:b + 1, c0:c1, h * G:(h + 1) * G]))
+            if first:   # the unit's keys go in once, with its first range
+                hs["k"] = pin(k[b:b + 1, :, h:h + 1])
+                if not v_view:
+                    hs["v"] = pin(v[b:b + 1, :, h:h + 1])
+            db = {n: torch.empty(t.shape, dtype=t.dtype, device=dev) for n, t in hs.items()}
+            if first:
+                unit_dev[(b, h)] = db
+                if not last:   # ranges: fp32 sums of the dk / dv partials
+                    unit_acc[(b, h)] = {n: torch.empty(db[n].shape, dtype=torch.float32, device=dev)
+                                        for n in (("k",) if v_view else ("k", "v"))}
+            od = dict(o=torch.empty(tuple(hs["q"].shape[:-1]) + (cfg.Dv,), dtype=q.dtype, pin_memory=True),
+                      dq=torch.empty(tuple(hs["q"].shape), dtype=q.dtype, pin_memory=True))
+            if last:
+                kdev = unit_dev[(b, h)]
+                od["dk"] = torch.empty(tuple(kdev["k"].shape), dtype=k.dtype, pin_memory=True)
+                if not v_view:
+                    od["dv"] = torch.empty(tuple(kdev["v"].shape), dtype=v.dtype, pin_memory=True)
+            unit_of.append((b, h))
+        host.append(hs)
+        dbuf.append(db)
         outs.append(od)
     h2d = sum(t.numel() * t.element_size() for hs in host for t in hs.values())
     d2h = sum(t.numel() * t.element_size() for od in outs for t in od.values())
@@ -609,38 +644,67 @@ def e2e_pipeline(args, cfg, d, split, units, rows, world, rank, dev, stream, flu
         start.record(stream)
         for s in (s_in, s_c, s_out):
             s.wait_event(start)
-        in_ev = []
+        fwd_ev, bwd_ev = [], []   # per chunk: forward inputs in / dO in
         for hs, db in zip(host, dbuf):
             with torch.cuda.stream(s_in):
                 for n in hs:
-                    db[n].copy_(hs[n], non_blocking=True)
+                    if n != "do":
+                        db[n].copy_(hs[n], non_blocking=True)
                 e = torch.cuda.Event()
                 e.record(s_in)
-                in_ev.append(e)
+                fwd_ev.append(e)
+                db["do"].copy_(hs["do"], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(s_in)
+                bwd_ev.append(e)
         for i, (c, db, od) in enumerate(zip(chunks, dbuf, outs)):
+            res = []
             with torch.cuda.stream(s_c):
-                s_c.wait_event(in_ev[i])
+                s_c.wait_event(fwd_ev[i])
                 if c is None:
+                    s_c.wait_event(bwd_ev[i])
                     r = shard.local_step(db["q"], db["k"], db["k"][..., :cfg.Dv] if v_view else db["v"], db["idx"],
                                          db["do"], (r0, r1), cfg.T, rank, world, cfg.bs, cfg.scale)
                     res = [("o", r["o"]), ("dq", r["dq"]), ("dk", r["dk"])] + \
                         ([] if v_view else [("dv", r["dv"])])
                 else:
+                    _, _, c0, c1, first, last = c
+                    kd = unit_dev[unit_of[i]]
+                    acc = unit_acc.get(unit_of[i])
+                    ke_c = c1 if cfg.causal else cfg.T   # causal: rows < c1 see no key past c1
                     qg = db["q"].detach().requires_grad_()
-                    kg = db["k"].detach().requires_grad_()
-                    vg = kg[..., :cfg.Dv] if v_view else db["v"].detach().requires_grad_()
+                    kg = kd["k"][:, :ke_c].detach().requires_grad_()
+                    vg = kg[..., :cfg.Dv] if v_view else kd["v"][:, :ke_c].detach().requires_grad_()
                     oo, _ = ops_b200.sparse_flash_attention(qg, kg, vg, db["idx"], cfg.bs, cfg.scale,
                                                             causal=cfg.causal, dq_mode=args.dq_mode)
+                    e_fwd = torch.cuda.Event()
+                    e_fwd.record(s_c)
+                    with torch.cuda.stream(s_out):   # o leaves while the backward runs
+                        s_out.wait_event(e_fwd)
+                        od["o"].copy_(oo.detach(), non_blocking=True)
+                    s_c.wait_event(bwd_ev[i])
                     oo.backward(db["do"])
-                    res = [("o", oo.detach()), ("dq", qg.grad), ("dk", kg.grad)] + \
-                        ([] if v_view else [("dv", vg.grad)])
+                    res = [("o", oo.detach()), ("dq", qg.grad)]
+                    grads = [("k", kg.grad)] + ([] if v_view else [("v", vg.grad)])
+                    if acc is not None:   # a row range: add this partial to the unit's fp32 sum
+                        for n, g in grads:
+                            if first:
+                                acc[n].zero_()
+                            acc[n][:, :ke_c] += g
+                        if last:
+                            grads = [(n, acc[n].to(k.dtype)) for n, _ in grads]
+                    if last:
+                        res += [("d" + n, g) for n, g in grads]
+                    else:
+                        res += [("_" + n, g) for n, g in grads]   # kept alive until the step ends
                 e = torch.cuda.Event()
                 e.record(s_c)
             keep.append(res)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(e)
                 for n, t in res:
-                    od[n].copy_(t, non_blocking=True)
+                    if n in od and (c is None or n != "o"):
+                        od[n].copy_(t, non_blocking=True)
         end = torch.cuda.Event()
         end.record(s_out)
         stream.wait_event(end)
