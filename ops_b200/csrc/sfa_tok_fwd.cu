@@ -10,9 +10,12 @@
 // Q stays in shared memory for the whole item; the selected rows stream in
 // 64-key chunks gathered with TMA `tile::gather4` (four kv rows per copy,
 // 128B-swizzled 64-dim slabs) — K slabs for S, then the V slabs of this
-// item's part.  O for one part (at most 256 dims = 256 TMEM columns) and two
-// S buffers (2 x 64 columns) fit the 512 TMEM columns; D_v beyond 256 (MLA:
-// 512) is split into parts computed by separate work items, each recomputing S.
+// item's part.  O for one part (at most 256 dims = 256 TMEM columns), two
+// S buffers (2 x 64 columns) and P (bf16, 32 columns) fit the 512 TMEM
+// columns; D_v beyond 256 (MLA: 512) is split into parts computed by separate
+// work items, each recomputing S.  P stays in TMEM as the PV MMA's A operand,
+// so shared memory holds only Q and the K / V rings (MLA: three K stages
+// where a shared-memory P left room for two).
 //
 // Softmax: one thread per head row (the row is thread-local in TMEM, so the
 // max and the sum need no cross-thread reduction).  P = exp2(S*c - m) uses a
@@ -64,6 +67,7 @@ constexpr int kQSlab = 128 * 128;    // bytes of one 128-row x 64-dim Q slab
 constexpr float kRescaleLog2 = 8.f;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 256;      // two S buffers of 64 columns after O's 256
+constexpr uint32_t kColP = 384;      // P of one chunk: 64 keys as bf16 pairs, 32 columns
 
 enum : int { kFirst = 1, kLast = 2, kEmpty = 4, kSentinel = 8 };
 
@@ -81,7 +85,7 @@ struct Args {
   int nitems, nrows, n_hg, n_vp, HG, G, nq;
   int dvp;                           // dims of a full V part (<= 256)
   int kst, vst;                      // ring stages (2 slabs each)
-  uint32_t off_k, off_v, off_p, off_desc, off_bar;   // smem offsets (Q at 0)
+  uint32_t off_k, off_v, off_desc, off_bar;   // smem offsets (Q at 0)
   int64_t k_rs, v_rs;                // element strides of one gather row (k / v)
   int fp8;                           // kv stored as e4m3 + row scales: slabs converted to bf16 here
   int32_t* status;
@@ -168,7 +172,6 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
   uint8_t* sq = sbase;
   uint8_t* sk = sbase + args.off_k;
   uint8_t* sv = sbase + args.off_v;
-  uint8_t* sp = sbase + args.off_p;
   Desc* jd = reinterpret_cast<Desc*>(sbase + args.off_desc);
   Bars& B = *reinterpret_cast<Bars*>(sbase + args.off_bar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -446,7 +449,6 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
   } else if (warp == 2) {
     // ============================================================ PV issuer
     if (lane == 0) {
-      const uint64_t pdesc = smem_desc(smem_u32(sp), 16, 1024, kSw128);
       int job = 0, vuse = 0, item_i = 0, chunk = 0;
       bool ok = true;
       while (ok) {
@@ -469,8 +471,8 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
             const uint64_t vd = smem_desc(smem_u32(sv + vs * 2 * kSlab), kSlab, 1024, kSw128);
             const uint32_t id_o = idesc_bf16(128, 64 * nsl, false, true);
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              mma_bf16_ss(tmem + s * 64, pdesc + (uint64_t)((k * 32) >> 4), vd + (uint64_t)((k * 2048) >> 4), id_o,
+            for (int k = 0; k < 4; ++k)   // A = P from TMEM: 16 keys = 8 columns per K step
+              mma_bf16_ts(tmem + s * 64, tmem + kColP + k * 8, vd + (uint64_t)((k * 2048) >> 4), id_o,
                           !((flags & kFirst) && k == 0));
             mma_commit(&B.v_empty[vs]);
           }
@@ -557,8 +559,8 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       if (!(ok = wtw(&B.p_empty, (chunk & 1) ^ 1, st, 18))) break;
       mref = mnew;
       const float nm = -mref;
-      const uint32_t prow = smem_u32(sp) + m * 128;
-      // pass 2: P = exp2(S*c - m) for the valid keys, bf16 into the swizzled P tile
+      // pass 2: P = exp2(S*c - m) for the valid keys, bf16 pairs into this
+      // thread's TMEM lane (keys 2i, 2i+1 in column kColP + i)
       float lc = 0.f;
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
@@ -567,20 +569,22 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         tmem_ld32(ts + hh * 32, sv);
         tmem_ld_wait();
         const uint32_t msk = hh ? mhi : mlo;
+        float pk[16];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float pr[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            pr[i] = ((msk >> (8 * j + i)) & 1u) ? ex2(fmaf(sv[8 * j + i], c2, nm)) : 0.f;
-            lc += pr[i];
-            if (p.compat & SFA_COMPAT_REFERENCE_P) pr[i] = ref_p(pr[i]);
+        for (int i = 0; i < 32; i += 2) {
+          float p0 = ((msk >> i) & 1u) ? ex2(fmaf(sv[i], c2, nm)) : 0.f;
+          float p1 = ((msk >> (i + 1)) & 1u) ? ex2(fmaf(sv[i + 1], c2, nm)) : 0.f;
+          lc += p0;
+          lc += p1;
+          if (p.compat & SFA_COMPAT_REFERENCE_P) {
+            p0 = ref_p(p0);
+            p1 = ref_p(p1);
           }
-          const int jj = 4 * hh + j;
-          st_shared_v4(prow + ((jj ^ (m & 7)) << 4), pack_bf16x2(pr[0], pr[1]), pack_bf16x2(pr[2], pr[3]),
-                       pack_bf16x2(pr[4], pr[5]), pack_bf16x2(pr[6], pr[7]));
+          pk[i / 2] = __uint_as_float(pack_bf16x2(p0, p1));
         }
+        tmem_st16(tl + kColP + hh * 16, pk);
       }
+      tmem_st_wait();
       tc_fence_before();
       warp_arrive(&B.s_empty[sb]);
       // O (and the running sum) to the raised maximum, after P: nothing of the
@@ -601,7 +605,6 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         tc_fence_before();
       }
       l += lc;
-      fence_proxy_async_smem();
       warp_arrive(&B.p_full);
       ++chunk;
       if (flags & kLast) {
@@ -671,12 +674,14 @@ static bool plan(const SfaParams& p, Plan* out, const char** why) {
   if (!a.k_rs || !a.v_rs) { *why = "k/v batch, token and head strides must fold into evenly spaced rows"; return false; }
   a.fp8 = p.kv_dtype == SFA_KV_FP8_E4M3 ? 1 : 0;
   if (krows > INT32_MAX || vrows > INT32_MAX) { *why = "too many kv rows for 32-bit gather coordinates"; return false; }
-  // shared memory: Q (nq slabs of 16 KB), P (16 KB), K / V rings of 2-slab (16 KB) stages
+  // shared memory: Q (nq slabs of 16 KB), K / V rings of 2-slab (16 KB) stages (P is in TMEM)
   const size_t budget = 227 * 1024 - 1024;
   const size_t desc = ((sizeof(Desc) * kJD + 127) / 128) * 128;
   const size_t bars = ((sizeof(Bars) + 127) / 128) * 128;
-  const size_t fixed = (size_t)a.nq * kQSlab + 16384 + desc + bars;
+  const size_t fixed = (size_t)a.nq * kQSlab + desc + bars;
   if (fixed + 4 * 2 * kSlab > budget) { *why = "head dims too large for shared memory"; return false; }
+  // grow the K ring first (MLA: 3 K + 2 V stages measured 68.5 ms at c4
+  // against 74.6 for 2 K + 3 V)
   int ks = 2, vs = 2;
   while (fixed + (size_t)(ks + vs + 1) * 2 * kSlab <= budget && ks + vs < 8) {
     if (ks <= vs) ++ks; else ++vs;
@@ -685,8 +690,7 @@ static bool plan(const SfaParams& p, Plan* out, const char** why) {
   a.vst = vs;
   a.off_k = (uint32_t)a.nq * kQSlab;
   a.off_v = a.off_k + ks * 2 * kSlab;
-  a.off_p = a.off_v + vs * 2 * kSlab;
-  a.off_desc = a.off_p + 16384;
+  a.off_desc = a.off_v + vs * 2 * kSlab;
   a.off_bar = a.off_desc + (uint32_t)desc;
   out->smem = a.off_bar + bars + 1024;
   a.nrows = num_rows_host(p);
