@@ -138,8 +138,9 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # Fixed sample per configuration: fwd+bwd of the last `last` queries of the
 # (batch 0, kv head 0) unit (decode: the forward of the first `seqs`
-# sequences).  A few seconds of fp32 work on 16 host threads each.
-CPU_SAMPLE = {"c1": {"last": 1024}, "c2": {"last": 8192}, "c3": {"last": 1024}, "c4": {"last": 64},
+# sequences).  Up to a few seconds of fp32 work on 16 host threads each;
+# cpu_baseline repeats it with further seeds until its time budget is spent.
+CPU_SAMPLE = {"c1": {"last": 1024}, "c2": {"last": 8192}, "c3": {"last": 1024}, "c4": {"last": 128},
               "c5": {"seqs": 16}, "tok128": {"last": 256}}
 
 
@@ -189,15 +190,17 @@ def cpu_unit(cfg):
     return ("GB/s", 1e9) if cfg.fwd_only else ("TFLOP/s", 1e12)
 
 
-def cpu_baseline(cfg, reps=2):
-    """The fixed sample, `reps` times (seeds 0..reps-1): total work / total time."""
+def cpu_baseline(cfg, min_s=10.0, max_reps=8):
+    """The fixed sample with seeds 0, 1, ... until `min_s` seconds of CPU work
+    (or `max_reps` samples) have run: total work / total time."""
     import torch
     torch.set_num_threads(os.cpu_count() or 1)
-    tt, ww = 0.0, 0.0
-    for r in range(reps):
-        dt, w = cpu_sample_run(cfg, seed=r)
+    tt, ww, reps = 0.0, 0.0, 0
+    while reps < max_reps and (reps == 0 or tt < min_s):
+        dt, w = cpu_sample_run(cfg, seed=reps)
         tt += dt
         ww += w
+        reps += 1
     unit, div = cpu_unit(cfg)
     return {"value": ww / tt / div, "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"{cpu_sample_desc(cfg)}; {reps} seeds, {tt:.1f} s"}
@@ -1002,7 +1005,7 @@ def run_ours(args, cfg):
             sub = measure_decode(args, sub_cfg, 1, 0, dev, 5, 3, False)
         else:
             sub = measure_config(args, sub_cfg, 1, 0, dev, "none", 3, 3, False)
-        extra[name] = (sub, None if args.no_cpu else cpu_baseline(sub_cfg, reps=1))
+        extra[name] = (sub, None if args.no_cpu else cpu_baseline(sub_cfg, min_s=2.0))
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
