@@ -534,7 +534,12 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
       if (!(ok = wtw(&B.s_full[sb], (chunk >> 1) & 1, st, 17))) break;
       tc_fence_after();
       const uint32_t ts = tl + kColS + sb * kKeys;
-      // pass 1: the chunk's max over its valid keys (S read in 32-column halves)
+      // pass 1: the chunk's max over its valid keys (S read in 32-column halves).
+      // A chunk whose 64 keys are all valid (every chunk of a row that selects
+      // a full top-k) skips the per-key mask tests, which otherwise keep the
+      // integer pipe busier than the exponentials keep the MUFU.
+      const bool full = (mlo & mhi) == 0xffffffffu;
+      const bool compat = (p.compat & SFA_COMPAT_REFERENCE_P) != 0;
       float mc = -INFINITY;
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
@@ -542,9 +547,14 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         tmem_ld32(ts + hh * 32, sv);
         tmem_ld_wait();
         const uint32_t msk = hh ? mhi : mlo;
+        if (full) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if ((msk >> i) & 1u) mc = fmaxf(mc, sv[i]);
+          for (int i = 0; i < 32; ++i) mc = fmaxf(mc, sv[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if ((msk >> i) & 1u) mc = fmaxf(mc, sv[i]);
+        }
       }
       const float zc = mc * c2;                // finite: the chunk has a valid key
       float mnew = mref, fac = 1.f;
@@ -570,17 +580,27 @@ sfa_tok_fwd_kernel(const __grid_constant__ Args args, const __grid_constant__ CU
         tmem_ld_wait();
         const uint32_t msk = hh ? mhi : mlo;
         float pk[16];
+        if (full && !compat) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float p0 = ((msk >> i) & 1u) ? ex2(fmaf(sv[i], c2, nm)) : 0.f;
-          float p1 = ((msk >> (i + 1)) & 1u) ? ex2(fmaf(sv[i + 1], c2, nm)) : 0.f;
-          lc += p0;
-          lc += p1;
-          if (p.compat & SFA_COMPAT_REFERENCE_P) {
-            p0 = ref_p(p0);
-            p1 = ref_p(p1);
+          for (int i = 0; i < 32; i += 2) {
+            const float p0 = ex2(fmaf(sv[i], c2, nm)), p1 = ex2(fmaf(sv[i + 1], c2, nm));
+            lc += p0;
+            lc += p1;
+            pk[i / 2] = __uint_as_float(pack_bf16x2(p0, p1));
           }
-          pk[i / 2] = __uint_as_float(pack_bf16x2(p0, p1));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            float p0 = ((msk >> i) & 1u) ? ex2(fmaf(sv[i], c2, nm)) : 0.f;
+            float p1 = ((msk >> (i + 1)) & 1u) ? ex2(fmaf(sv[i + 1], c2, nm)) : 0.f;
+            lc += p0;
+            lc += p1;
+            if (compat) {
+              p0 = ref_p(p0);
+              p1 = ref_p(p1);
+            }
+            pk[i / 2] = __uint_as_float(pack_bf16x2(p0, p1));
+          }
         }
         tmem_st16(tl + kColP + hh * 16, pk);
       }
