@@ -7,6 +7,8 @@
 //   * fp32 dk/dv accumulators -> bf16 outputs (atomic dk/dv path).
 //   * the block->query inverted index used by the key-centric dk/dv pass:
 //     count -> exclusive scan -> fill, deterministic (no atomics on positions).
+#include <type_traits>
+
 #include "sfa_common.cuh"
 #include "sfa_internal.h"
 
@@ -80,7 +82,7 @@ template <int kDv>
 __global__ void __launch_bounds__(kPreThreads)
 preprocess_vec_kernel(SfaParams p, float* __restrict__ delta, float* __restrict__ dsink_part) {
   extern __shared__ float sdelta[];  // [kPreRows][h_q]
-  constexpr int kU = 4;
+  constexpr int kU = 4;   // (row, head) pairs in flight per half-warp (8 measured slower)
   const int rows = num_rows(p);
   const int row0 = blockIdx.x * kPreRows;
   const int hw = threadIdx.x >> 4, l16 = threadIdx.x & 15;   // half-warp = one (row, head)
@@ -313,18 +315,23 @@ cudaError_t launch_reduce_dkdv_ranges(const SfaParams& p, const BwdLayout& L, co
 // dq = bf16(scale * acc) for the fused dQ: acc is fp32 [rows][h_q][d_qk].
 // kVec: eight consecutive dims per thread (d_qk % 8 == 0), one 16-byte store
 // (16-byte aligned dq rows); otherwise four dims and element stores.
-template <bool kVec>
+// kIdx32: the element-group count fits 32 bits, so the index arithmetic (three
+// divisions per group) stays in 32-bit integers; 64-bit divisions otherwise
+// cost more issue slots than the group's 48 bytes of traffic leave room for.
+template <bool kVec, bool kIdx32>
 __global__ void convert_dq_kernel(SfaParams p, const float* __restrict__ acc) {
   constexpr int kE = kVec ? 8 : 4;
+  using Idx = typename std::conditional<kIdx32, uint32_t, int64_t>::type;
   const int D = p.d_qk;
   const int64_t rows = p.cu_seqlens_q == nullptr ? (int64_t)p.batch * p.q_len : (int64_t)p.total_q;
-  const int64_t n = rows * p.h_q * (D / kE);
+  const Idx n = (Idx)(rows * p.h_q * (D / kE));
+  const Idx groups = (Idx)(D / kE), hq = (Idx)p.h_q;
   __nv_bfloat16* dq = reinterpret_cast<__nv_bfloat16*>(p.dq);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int d = (int)(i % (D / kE)) * kE;
-    const int64_t rh = i / (D / kE);
-    const int h = (int)(rh % p.h_q);
-    const int row = (int)(rh / p.h_q);
+  for (Idx i = (Idx)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (Idx)gridDim.x * blockDim.x) {
+    const int d = (int)(i % groups) * kE;
+    const Idx rh = i / groups;
+    const int h = (int)(rh % hq);
+    const int row = (int)(rh / hq);
     int64_t b = 0, t = row;
     if (p.cu_seqlens_q == nullptr) { b = row / p.q_len; t = row - b * p.q_len; }
     const float4* src = reinterpret_cast<const float4*>(acc + rh * D + d);
@@ -351,10 +358,16 @@ cudaError_t launch_convert_dq(const SfaParams& p, const float* dq_acc, cudaStrea
   const int grid = device_sm_count() * 8;
   const bool vec = p.d_qk % 8 == 0 && (reinterpret_cast<uintptr_t>(p.dq) % 16 == 0) && p.dq_sb % 8 == 0 &&
                    p.dq_st % 8 == 0 && p.dq_sh % 8 == 0;
-  if (vec)
-    convert_dq_kernel<true><<<grid, 256, 0, st>>>(p, dq_acc);
+  const int64_t rows = p.cu_seqlens_q == nullptr ? (int64_t)p.batch * p.q_len : (int64_t)p.total_q;
+  const bool i32 = rows * p.h_q * p.d_qk < ((int64_t)1 << 31);
+  if (vec && i32)
+    convert_dq_kernel<true, true><<<grid, 256, 0, st>>>(p, dq_acc);
+  else if (vec)
+    convert_dq_kernel<true, false><<<grid, 256, 0, st>>>(p, dq_acc);
+  else if (i32)
+    convert_dq_kernel<false, true><<<grid, 256, 0, st>>>(p, dq_acc);
   else
-    convert_dq_kernel<false><<<grid, 256, 0, st>>>(p, dq_acc);
+    convert_dq_kernel<false, false><<<grid, 256, 0, st>>>(p, dq_acc);
   note_launch("convert_dq", st);
   return cudaGetLastError();
 }
