@@ -219,3 +219,52 @@ def test_fp8_kv_quantisation_is_exact_in_bf16():
     assert torch.equal(deq.bfloat16().float(), deq)                             # exact in bf16
     rel = ((deq - kv.float()).abs() / kv.float().abs().amax(-1, keepdim=True).clamp_min(1e-6)).max()
     assert float(rel) <= 2 ** -4                                                # e4m3: 3 mantissa bits
+
+
+def test_e2e_chunks_cover_every_unit_row_once():
+    """bench's end-to-end pipeline cuts each (batch, kv head) unit into row
+    ranges when a rank has fewer than 8 units: every row of every unit falls
+    in exactly one range, in order, with the unit's first and last marked."""
+    import bench
+    for name in ("c1", "c2", "c3", "c4", "tok128"):
+        cfg = W.CONFIGS[name]
+        for world in (1, 2, 4, 8):
+            units = bench.unit_range(cfg, world, world - 1)
+            if units is None:
+                continue
+            b0, b1, h0, h1 = units
+            per_unit = {}
+            for b, h, r0, r1, first, last in bench.e2e_chunks(cfg, "units", units):
+                per_unit.setdefault((b, h), []).append((r0, r1, first, last))
+            assert sorted(per_unit) == [(b, h) for b in range(b0, b1) for h in range(h0, h1)], (name, world)
+            for rs in per_unit.values():
+                assert rs[0][0] == 0 and rs[-1][1] == cfg.T
+                assert all(a[1] == c[0] and a[0] < a[1] for a, c in zip(rs, rs[1:]))
+                assert [x[2] for x in rs] == [True] + [False] * (len(rs) - 1)
+                assert [x[3] for x in rs] == [False] * (len(rs) - 1) + [True]
+    assert bench.e2e_chunks(W.CONFIGS["c2"], "query", (0, 4, 0, 4)) == [None]
+
+
+def test_row_ranges_over_leading_keys_reproduce_the_whole_op():
+    """What the e2e row ranges rely on: rows [r0, r1) against keys [0, r1)
+    keep every row's causal position (bottom-right alignment), so o, lse and
+    dq of a range equal the whole op's rows, and the ranges' dk / dv partials
+    sum to the whole op's dk / dv."""
+    cfg = W.scaled(W.CONFIGS["c2"], B=1, T=320, Hq=4, Hk=1, S=4)
+    d = W.make_inputs(cfg, "cpu", 0)
+    q, k, v, do = (d[n].float() for n in ("q", "k", "v", "do"))
+    idx = d["idx"]
+    o, lse = O.sfa_forward(q, k, v, idx, cfg.bs, cfg.scale)
+    dq, dk, dv, _ = O.sfa_backward(q, k, v, idx, o, lse, do, cfg.bs, cfg.scale)
+    dk_sum, dv_sum = torch.zeros_like(dk), torch.zeros_like(dv)
+    for r0, r1 in ((0, 96), (96, 200), (200, 320)):
+        oc, lc = O.sfa_forward(q[:, r0:r1], k[:, :r1], v[:, :r1], idx[:, r0:r1], cfg.bs, cfg.scale)
+        dqc, dkc, dvc, _ = O.sfa_backward(q[:, r0:r1], k[:, :r1], v[:, :r1], idx[:, r0:r1], oc, lc, do[:, r0:r1],
+                                          cfg.bs, cfg.scale)
+        torch.testing.assert_close(oc, o[:, r0:r1], rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(lc, lse[:, r0:r1], rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(dqc, dq[:, r0:r1], rtol=1e-5, atol=1e-5)
+        dk_sum[:, :r1] += dkc
+        dv_sum[:, :r1] += dvc
+    torch.testing.assert_close(dk_sum, dk, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(dv_sum, dv, rtol=1e-4, atol=1e-4)
